@@ -1,0 +1,330 @@
+"""Decode benchmark: Llama-3-8B-architecture Q4_K_M-style GGUF, batch 1, greedy,
+after a 2048-token prompt.
+
+A step is one decode token through the device token loop (every layer's
+fused dequant-matvecs, attention over the HBM KV cache, LM head and argmax).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+- ``value``: whole-job decode tok/s with the token loop resident on the device
+  (K greedy steps as back-to-back CUDA-graph launches, CUDA events, max over
+  ranks).  Weights (4.9 GB) are far larger than L2 (126 MB), so every step
+  streams them from HBM.
+- ``e2e``: the same metric through the public C ABI call ``fl_forward`` with
+  the token id copied host→device and the argmax copied back every step.
+- ``roofline``: the dequant-matvec kernel class (algorithmic GGUF bytes ÷
+  per-launch CUDA-event durations of an eagerly launched step) against the
+  measured HBM copy bandwidth in MEASURED_PEAKS.json.
+- ``cpu_baseline``: the C restatement of the reference CPU path (oracle/),
+  all host threads, on a bounded sample: 2 of the 32 decoder layers at the same
+  position plus the LM head, extrapolated to the full model.
+- ``--impl reference``: that CPU path alone, timed per step the same way.
+
+With N > 1 GPUs each rank decodes its own replica of the model (the tensor-
+parallel path is not built yet), so scaling is weak.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+CONFIG = "llama3-8b"
+PROMPT = 2048
+METRIC = "decode tok/s, Llama-3-8B-arch Q4_K_M-style GGUF, bs=1 greedy after a 2048-token prompt"
+NOMINAL_HBM_GBS = 8000.0
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.out = tempfile.NamedTemporaryFile(prefix="clocks_", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.gpu)], stdout=self.out,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.out.close()
+        rows = []
+        for line in Path(self.out.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.out.name)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+def dist_setup():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def allreduce_max(v: float, ws: int) -> float:
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws: int):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def model_image(ws: int, rank: int) -> np.ndarray:
+    from dotnetfoundryllm_b200 import ggufgen
+    if ws == 1:
+        return ggufgen.build_model(CONFIG)
+    path = Path(tempfile.gettempdir()) / f"foundry_bench_{CONFIG}_{os.environ.get('MASTER_PORT', '0')}.gguf"
+    if rank == 0:
+        ggufgen.build_model(CONFIG, str(path))
+    barrier(ws)
+    img = np.fromfile(path, dtype=np.uint8)
+    barrier(ws)
+    if rank == 0:
+        path.unlink(missing_ok=True)
+    return img
+
+
+def cpu_sample(img: np.ndarray, position: int, repeats: int = 3, threads: int | None = None) -> dict:
+    """Oracle timing on 2 decoder layers + the LM head; per-token estimate."""
+    from oracle import oracle as O
+    threads = threads or os.cpu_count() or 1
+    O.set_threads(threads)
+    m = O.Model(img, max_layers=2)
+    s = O.Session(m)
+    s.fake_length(position)
+    t_layers, t_head = [], []
+    for _ in range(repeats):
+        s.fake_length(position)
+        t0 = time.perf_counter()
+        rc = s.forward_layers(1, position, 2)
+        t1 = time.perf_counter()
+        rc2 = s.forward_head()
+        t2 = time.perf_counter()
+        assert rc == 0 and rc2 == 0, (rc, rc2)
+        t_layers.append(t1 - t0)
+        t_head.append(t2 - t1)
+    n_layers = m.n_layers
+    s.close()
+    m.close()
+    per_tok = (min(t_layers) / 2) * n_layers + min(t_head)
+    return {"tok_s": 1.0 / per_tok, "per_token_s": per_tok, "threads": threads, "layer_s": min(t_layers) / 2,
+            "head_s": min(t_head), "n_layers": n_layers}
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    from dotnetfoundryllm_b200 import ggufgen
+    img = ggufgen.build_model(CONFIG)
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    m = O.Model(img, max_layers=2)
+    s = O.Session(m)
+    pos = PROMPT - 1
+    times = []
+    for i in range(args.warmup + args.steps):
+        s.fake_length(pos + i)
+        t0 = time.perf_counter()
+        s.forward_layers(1, pos + i, 2)
+        t1 = time.perf_counter()
+        s.forward_head()
+        t2 = time.perf_counter()
+        if i >= args.warmup:
+            times.append((t1 - t0) / 2 * m.n_layers + (t2 - t1))
+    s.close()
+    m.close()
+    per = sum(times) / len(times)
+    value = 1.0 / per
+    sample = (f"per step: 2 of 32 decoder layers (F32 weights dequantized at load, as the reference does) at "
+              f"positions {pos}..{pos + args.warmup + args.steps - 1} plus the LM head, layer time x16")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF)",
+        "config": {"workload": f"{CONFIG} Q4_K/Q6_K bs=1 decode after a {PROMPT}-token prompt",
+                   "model": CONFIG, "global_batch": 1, "seq_len": PROMPT},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args, ws, rank, local):
+    from dotnetfoundryllm_b200 import loader, runtime
+    img = model_image(ws, rank)
+    max_ctx = PROMPT + args.warmup + 2 * args.steps + 64
+    model = loader.load(img, device=local, max_ctx=max_ctx)
+    fwd = runtime.CudaForwardPass(model, max_ctx=max_ctx)
+    from dotnetfoundryllm_b200 import ggufgen
+    prompt = ggufgen.prompt_ids(PROMPT, model.desc.vocab, 0)
+    kv = object()
+    # prefill the way LlamaLanguageModel does: one Forward per prompt token but the last
+    t0 = time.perf_counter()
+    for i in range(PROMPT - 1):
+        fwd.forward(int(prompt[i]), i, kv, want_logits=False)
+    prefill_s = time.perf_counter() - t0
+    pos = PROMPT - 1
+    tok = int(prompt[-1])
+    # warm-up (device-resident greedy loop)
+    if args.warmup:
+        out = fwd.decode_greedy(tok, pos, args.warmup)
+        tok = int(out[-1])
+        pos += args.warmup
+    launches = fwd.launches_per_step()
+    clocks = ClockSampler(local) if rank == 0 else None
+    barrier(ws)
+    if clocks:
+        clocks.start()
+    ms = fwd.time_decode(tok, pos, args.steps)
+    clk = clocks.stop() if clocks else None
+    ms_max = allreduce_max(ms, ws)
+    pos_timed = pos
+    pos += args.steps
+    # e2e through the C ABI with host buffers
+    barrier(ws)
+    t0 = time.perf_counter()
+    cur = tok
+    for i in range(args.steps):
+        cur = fwd.forward(cur, pos + i, kv, want_logits=False)
+    e2e_s = time.perf_counter() - t0
+    e2e_max = allreduce_max(e2e_s, ws)
+    # roofline of the dequant-matvec kernel class (eager launches, events per kernel)
+    profs = [fwd.profile_step(int(prompt[i % PROMPT]), pos + args.steps + i) for i in range(3)]
+    mv_ms = min(p["ms"]["matvec"] for p in profs)
+    mv_bytes = profs[0]["bytes"]["matvec"]
+    peaks = load_peaks()
+    achieved = mv_bytes / (mv_ms / 1e3) / 1e9
+    d = model.desc
+    kvd = d.n_kv_heads * d.head_dim
+    avg_ctx = pos_timed + args.steps / 2 + 1
+    kv_bytes = d.n_layers * kvd * 4 * (2 * avg_ctx + 2)
+    step_bytes = model.weight_bytes() + kv_bytes
+    ms_per_step = ms_max / args.steps
+    step_gbs = step_bytes / (ms_per_step / 1e3) / 1e9
+    value = ws * args.steps / (ms_max / 1e3)
+    result = None
+    if rank == 0:
+        cpu = cpu_sample(img, pos_timed)
+        traffic = None
+        tf = ROOT / "profiles" / "traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get(CONFIG)
+        result = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF, N(0,0.02) weights)",
+            "config": {"workload": f"{CONFIG} Q4_K/Q6_K bs=1 greedy decode, positions {pos_timed}.."
+                                   f"{pos_timed + args.steps - 1} after a {PROMPT}-token prompt",
+                       "model": CONFIG, "global_batch": ws, "seq_len": PROMPT,
+                       "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (4.9 GB of weights per step)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                         "kernel": "fl_mv_kernel (all dequant-matvec launches of one step)",
+                         "peak_source": peaks["source"], "frac_of_nominal_8tbs": achieved / NOMINAL_HBM_GBS,
+                         "step_bytes": step_bytes, "step_gbs": step_gbs,
+                         "step_frac": step_gbs / peaks["hbm_gbs"]},
+            "cpu_baseline": {"value": cpu["tok_s"], "unit": "tok/s", "cores": cpu["threads"], "kind": "port",
+                             "sample": "oracle (C restatement of the reference CPU path, F32 weights) on 2 of 32 "
+                                       f"decoder layers at position {pos_timed} + the LM head, layer time x16"},
+            "e2e": {"value": ws * args.steps / e2e_max, "unit": "tok/s", "h2d_bytes_per_step": 16,
+                    "d2h_bytes_per_step": 4},
+            "gpu_launches": launches * args.steps,
+            "clocks": clk,
+            "prefill_reference_style_s": prefill_s,
+        }
+    fwd.close()
+    model.close()
+    return result
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        return
+    ws, rank, local = dist_setup()
+    res = run_ours(args, ws, rank, local)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,131 @@
+/*
+ * fl_kernels.h — launch parameters and host launchers of the device kernels.
+ * (Internal to libfoundry_cuda.so; the public ABI is include/foundry_cuda.h.)
+ */
+#ifndef FL_KERNELS_H
+#define FL_KERNELS_H
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define FL_MV_MAX_SEG 3
+#define FL_MV_WARPS 8
+#define FL_MV_THREADS (FL_MV_WARPS * 32)
+
+/* Input transforms of the matvec prologue (the op that produced the vector in
+ * the reference, fused in front of LinearProjection). */
+enum {
+    FL_IN_PLAIN = 0,        /* x as is; |x| <= *absmax */
+    FL_IN_RMSNORM = 1,      /* TensorOperations.RmsNorm(x, w, eps) */
+    FL_IN_GEMMA_NORM = 2,   /* TensorOperations.GemmaRmsNorm(x, w) */
+    FL_IN_GEMMA_RESID = 3,  /* x' = x + GemmaRmsNorm(pend, pend_w) (stored), then GemmaRmsNorm(x', w) */
+};
+
+/* Epilogues (the op that consumed LinearProjection's output). */
+enum {
+    FL_EPI_STORE = 0,   /* y[row] = v (+ bias) */
+    FL_EPI_RESID = 1,   /* y[row] += v  (TensorPrimitives.Add(_x, _xNorm, _x)) */
+    FL_EPI_QKV = 2,     /* bias, RoPE, q store, K/V cache append */
+    FL_EPI_GLU = 3,     /* act = silu|gelu(gate) * up over interleaved gate/up rows */
+    FL_EPI_LOGITS = 4,  /* logits (+ final softcap) and greedy argmax */
+};
+
+struct FlMvSeg {
+    const uint8_t* w;    /* repacked units of this segment */
+    const float* bias;   /* per-row bias (Qwen2) or NULL */
+    int32_t fmt, expanded, unit_bytes, n_tiles;
+    int32_t tile0;       /* first global tile of the segment */
+    int32_t rows;        /* logical rows */
+};
+
+struct FlMvArgs {
+    FlMvSeg seg[FL_MV_MAX_SEG];
+    int32_t n_seg, n_tiles, n_kb, K;
+    int32_t slot_bytes, n_slots;   /* per-warp ring */
+    /* prologue */
+    int32_t in_mode;
+    const float* x;
+    const float* norm_w;
+    float eps;
+    const float* pend;
+    const float* pend_w;
+    float* resid_out;
+    const float* absmax;           /* FL_IN_PLAIN bound on |x| */
+    /* epilogue */
+    int32_t epi;
+    float* y;
+    int32_t rows_total;
+    /* QKV */
+    int32_t q_rows, kv_rows, head_dim;
+    const float* rope_cs;          /* [max_ctx][head_dim/2][2] cos, sin */
+    const int32_t* pos;            /* device position */
+    float* q_out;
+    float* k_cache;
+    float* v_cache;
+    /* GLU */
+    int32_t act_gelu;
+    float* act_out;
+    float* act_absmax;
+    /* logits */
+    float softcap;
+    float* cta_best;               /* [grid][2]: value, index bits */
+    int32_t* counter;
+    int32_t* argmax_out;
+    int* err;
+};
+
+/* Dynamic shared memory of a matvec launch. */
+size_t fl_mv_smem_bytes(const FlMvArgs& a);
+/* Opts the matvec kernels into large dynamic shared memory on the current
+ * device (call before stream capture). */
+cudaError_t fl_mv_configure();
+cudaError_t fl_launch_matvec(const FlMvArgs& a, int grid, cudaStream_t st, bool pdl);
+
+/* Embedding row (bit-exact dequant of token_embd row `token`). */
+struct FlEmbedArgs {
+    const uint8_t* raw;     /* raw GGUF bytes of token_embd.weight */
+    int32_t ggml_type, hidden, vocab;
+    const int32_t* token;   /* device token id */
+    float* x;
+    float* zero_buf;        /* absmax slots cleared each step */
+    int32_t zero_n;
+    int* err;
+};
+cudaError_t fl_launch_embed(const FlEmbedArgs& a, cudaStream_t st, bool pdl);
+
+/* Split-K decode attention over the F32 KV cache. */
+struct FlAttnArgs {
+    const float* q;              /* [n_heads*head_dim] after RoPE */
+    const float* k_cache;        /* [max_ctx][kv_dim] */
+    const float* v_cache;
+    float* out;                  /* [n_heads*head_dim] */
+    float* out_absmax;
+    float* part;                 /* [n_kv][n_split][grp][head_dim + 2] */
+    int32_t* counter;            /* [n_kv] */
+    const int32_t* pos;
+    int32_t n_heads, n_kv, head_dim, n_split, window;
+    float scale, softcap;
+    int* err;
+};
+cudaError_t fl_launch_attention(const FlAttnArgs& a, cudaStream_t st, bool pdl);
+
+/* Position bookkeeping of the device-resident decode loop: token <- argmax,
+ * pos <- pos + 1, and the generated id appended to a device array. */
+struct FlAdvanceArgs {
+    int32_t* token;
+    int32_t* pos;
+    const int32_t* argmax;
+    int32_t* out_tokens;
+    int32_t* step;
+};
+cudaError_t fl_launch_advance(const FlAdvanceArgs& a, cudaStream_t st, bool pdl);
+
+/* Bit-exact block dequantization (fl_dequant). */
+cudaError_t fl_launch_dequant(int32_t ggml_type, const uint8_t* src, int64_t n_blocks, float* dst, cudaStream_t st);
+
+/* Top-k of a logits vector: k largest (value desc, index asc). */
+cudaError_t fl_launch_topk(const float* logits, int32_t n, int32_t k, int32_t* ids, float* vals, uint8_t* scratch,
+                           size_t scratch_bytes, cudaStream_t st);
+size_t fl_topk_scratch_bytes(int32_t n, int32_t k);
+
+#endif

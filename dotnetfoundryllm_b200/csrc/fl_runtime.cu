@@ -1,0 +1,968 @@
+/*
+ * fl_runtime.cu — the C ABI (include/foundry_cuda.h): device model, upload +
+ * repack, per-request session with an HBM KV cache, and the token step as one
+ * CUDA graph of programmatic-dependent launches.
+ *
+ * Reference seam: LlamaLanguageModel takes a Func<IForwardPass> factory and an
+ * IDisposable model resource (src/DotNetFoundryLLM.Inference/
+ * LlamaLanguageModel.cs:48-80); fl_model is that resource and fl_session +
+ * fl_forward the IForwardPass (IForwardPass.cs:8-15).
+ */
+#include <cmath>
+#include <climits>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/foundry_cuda.h"
+#include "fl_kernels.h"
+#include "fl_repack.h"
+
+/* ── errors ─────────────────────────────────────────────────────────────── */
+static thread_local std::string g_err;
+
+static int fail(int code, const char* fmt, ...)
+{
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) {                                                                   \
+            if (e_ == cudaErrorMemoryAllocation)                                                   \
+                return fail(FL_ERR_OOM, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+            return fail(FL_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+        }                                                                                          \
+    } while (0)
+
+extern "C" const char* fl_last_error(void) { return g_err.c_str(); }
+extern "C" int32_t fl_abi_version(void) { return FL_ABI_VERSION; }
+
+/* ── device objects ─────────────────────────────────────────────────────── */
+struct DevMatrix {
+    fl_matrix_layout L;
+    uint8_t* d = nullptr;
+    bool present = false;
+};
+
+struct Layer {
+    DevMatrix wq, wk, wv, wo, gate_up, down;
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *post_attn_norm = nullptr, *post_ffn_norm = nullptr;
+    float *bq = nullptr, *bk = nullptr, *bv = nullptr;
+    std::vector<uint8_t> stash;      /* raw bytes of gate or up until its partner arrives */
+    int stash_type = -1, stash_is_gate = 0;
+};
+
+struct fl_model {
+    fl_model_desc d;
+    int sm_count = 148;
+    std::vector<Layer> layers;
+    uint8_t* emb_raw = nullptr;
+    int emb_type = -1;
+    int64_t emb_bytes = 0;
+    DevMatrix output;
+    float* out_norm = nullptr;
+    float* rope_cs = nullptr;
+    bool finalized = false;
+    std::vector<void*> allocs;
+    double weight_bytes = 0;
+};
+
+struct fl_session {
+    fl_model* m = nullptr;
+    int max_ctx = 0, cur_len = 0;
+    cudaStream_t st = nullptr;
+    float *xa = nullptr, *xb = nullptr, *q = nullptr, *att = nullptr, *act = nullptr, *o = nullptr, *logits = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+    float* absmax = nullptr; /* [2*L] attn_out, act */
+    int n_absmax = 0;
+    int32_t* state = nullptr; /* token, pos, argmax, step, err, head_counter */
+    int32_t* attn_counter = nullptr;
+    float* attn_part = nullptr;
+    float* cta_best = nullptr;
+    int32_t* out_tokens = nullptr;
+    int32_t* topk_ids = nullptr;
+    float* topk_vals = nullptr;
+    uint8_t* topk_scratch = nullptr;
+    size_t topk_scratch_bytes = 0;
+    int32_t* h_state = nullptr; /* pinned */
+    cudaGraphExec_t graph = nullptr;
+    int launches = 0;
+    int attn_split = 1;
+    std::vector<void*> allocs;
+};
+
+enum { ST_TOKEN = 0, ST_POS = 1, ST_ARGMAX = 2, ST_STEP = 3, ST_ERR = 4, ST_HEADCNT = 5, ST_N = 8 };
+
+template <typename T>
+static int dalloc(std::vector<void*>& list, T** p, size_t bytes)
+{
+    void* v = nullptr;
+    cudaError_t e = cudaMalloc(&v, bytes ? bytes : 16);
+    if (e != cudaSuccess) return fail(FL_ERR_OOM, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    list.push_back(v);
+    *p = reinterpret_cast<T*>(v);
+    return FL_OK;
+}
+
+static int block_elems(int t)
+{
+    switch (t) {
+    case FL_T_F32: case FL_T_F16: case FL_T_BF16: return 1;
+    case FL_T_Q4_0: case FL_T_Q8_0: return 32;
+    case FL_T_Q4_K: case FL_T_Q5_K: case FL_T_Q6_K: case FL_T_Q8_K: return 256;
+    default: return 0;
+    }
+}
+static int block_bytes(int t)
+{
+    switch (t) {
+    case FL_T_F32: return 4;
+    case FL_T_F16: case FL_T_BF16: return 2;
+    case FL_T_Q4_0: return 18;
+    case FL_T_Q8_0: return 34;
+    case FL_T_Q4_K: return 144;
+    case FL_T_Q5_K: return 176;
+    case FL_T_Q6_K: return 210;
+    case FL_T_Q8_K: return 292;
+    default: return 0;
+    }
+}
+
+/* ── model ──────────────────────────────────────────────────────────────── */
+extern "C" int fl_model_create(const fl_model_desc* desc, fl_model** out)
+{
+    if (!desc || !out) return fail(FL_ERR_ARG, "null argument");
+    if (desc->struct_size != (int32_t)sizeof(fl_model_desc)) return fail(FL_ERR_ARG, "fl_model_desc size mismatch");
+    const fl_model_desc& d = *desc;
+    if (d.arch < FL_ARCH_LLAMA || d.arch > FL_ARCH_QWEN2) return fail(FL_ERR_UNSUPPORTED, "unknown arch %d", d.arch);
+    /* LlamaForwardPass.cs:48-52 */
+    if (d.n_kv_heads <= 0 || d.n_heads <= 0 || d.n_kv_heads > d.n_heads || d.n_heads % d.n_kv_heads != 0)
+        return fail(FL_ERR_ARG, "Invalid attention head configuration: NumHeads=%d, NumKvHeads=%d.", d.n_heads,
+                    d.n_kv_heads);
+    if (d.n_layers <= 0 || d.hidden <= 0 || d.ffn <= 0 || d.vocab <= 0 || d.max_ctx <= 0)
+        return fail(FL_ERR_ARG, "non-positive dimension");
+    if (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256)
+        return fail(FL_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128, 256)", d.head_dim);
+    int grp = d.n_heads / d.n_kv_heads;
+    if (grp != 1 && grp != 2 && grp != 4 && grp != 8) return fail(FL_ERR_UNSUPPORTED, "GQA group %d", grp);
+    if (d.hidden % 32 || d.ffn % 32 || (d.n_heads * d.head_dim) % 32)
+        return fail(FL_ERR_UNSUPPORTED, "dimensions must be multiples of 32");
+    if (d.tp_size > 1) return fail(FL_ERR_UNSUPPORTED, "tensor parallelism is not built into this library yet");
+    if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice(%d) failed", d.device);
+    fl_model* m = new fl_model();
+    m->d = d;
+    m->layers.resize((size_t)d.n_layers);
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d.device) == cudaSuccess && sms > 0)
+        m->sm_count = sms;
+    /* RoPE table: theta = pos' * invFreq[i], invFreq[i] = 1/powf(base, 2i/hd)
+     * (LlamaForwardPass.cs:64-70, 135-148; TensorOperations.cs:250-260),
+     * cos/sin from the C runtime as MathF does on Linux. */
+    const int half = d.head_dim / 2;
+    std::vector<float> inv((size_t)half), cs((size_t)d.max_ctx * half * 2);
+    for (int i = 0; i < half; i++) {
+        float ex = (2.0f * (float)i) / (float)d.head_dim;
+        inv[(size_t)i] = 1.0f / powf(d.rope_base, ex);
+    }
+    for (int p = 0; p < d.max_ctx; p++) {
+        float pos = d.rope_scaled ? (float)p / d.rope_factor : (float)p;
+        for (int i = 0; i < half; i++) {
+            float th = pos * inv[(size_t)i];
+            cs[((size_t)p * half + i) * 2] = cosf(th);
+            cs[((size_t)p * half + i) * 2 + 1] = sinf(th);
+        }
+    }
+    int rc = dalloc(m->allocs, &m->rope_cs, cs.size() * 4);
+    if (rc) { delete m; return rc; }
+    if (cudaMemcpy(m->rope_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        fl_model_destroy(m);
+        return fail(FL_ERR_CUDA, "rope table upload failed");
+    }
+    *out = m;
+    return FL_OK;
+}
+
+extern "C" void fl_model_destroy(fl_model* m)
+{
+    if (!m) return;
+    cudaSetDevice(m->d.device);
+    for (void* p : m->allocs) cudaFree(p);
+    delete m;
+}
+
+/* Dequantizes a small tensor (norm weights, biases) on the device, bit-exact. */
+static int upload_vector(fl_model* m, int type, const void* bytes, uint64_t nbytes, int64_t expect, float** out)
+{
+    int be = block_elems(type), bb = block_bytes(type);
+    if (!be) return fail(FL_ERR_UNSUPPORTED, "Tensor type %d is not supported for dequantization.", type);
+    if (nbytes % (uint64_t)bb) return fail(FL_ERR_ARG, "tensor byte length is not a multiple of the block size");
+    int64_t n = (int64_t)(nbytes / bb) * be;
+    if (n != expect) return fail(FL_ERR_ARG, "vector has %lld elements, expected %lld", (long long)n, (long long)expect);
+    uint8_t* raw = nullptr;
+    float* dst = nullptr;
+    int rc = dalloc(m->allocs, &dst, (size_t)expect * 4);
+    if (rc) return rc;
+    CK(cudaMalloc(&raw, nbytes));
+    CK(cudaMemcpy(raw, bytes, nbytes, cudaMemcpyHostToDevice));
+    CK(fl_launch_dequant(type, raw, n, dst, 0));
+    CK(cudaDeviceSynchronize());
+    CK(cudaFree(raw));
+    *out = dst;
+    m->weight_bytes += (double)nbytes;
+    return FL_OK;
+}
+
+static int upload_matrix(fl_model* m, int type, int rows, int cols, const uint8_t* raw, const uint8_t* raw2,
+                         const int32_t* row_map, DevMatrix* dm, double gguf_bytes)
+{
+    fl_matrix_layout L;
+    int r = fl_layout_for(type, rows, cols, &L);
+    if (r == -1) return fail(FL_ERR_UNSUPPORTED, "matrix type %d has no quantized matvec path", type);
+    if (r == -2) return fail(FL_ERR_UNSUPPORTED, "matrix row length %d is not a multiple of 32", cols);
+    std::vector<uint8_t> host((size_t)L.total_bytes);
+    fl_repack(&L, raw, raw2, row_map, host.data(), 0);
+    int rc = dalloc(m->allocs, &dm->d, (size_t)L.total_bytes);
+    if (rc) return rc;
+    CK(cudaMemcpy(dm->d, host.data(), (size_t)L.total_bytes, cudaMemcpyHostToDevice));
+    dm->L = L;
+    dm->present = true;
+    m->weight_bytes += gguf_bytes;
+    return FL_OK;
+}
+
+static bool parse_layer(const char* name, int* layer, std::string* suffix)
+{
+    if (strncmp(name, "blk.", 4) != 0) return false;
+    char* end = nullptr;
+    long l = strtol(name + 4, &end, 10);
+    if (!end || *end != '.') return false;
+    *layer = (int)l;
+    *suffix = end + 1;
+    return true;
+}
+
+extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, const uint64_t* dims, int32_t ndims,
+                               const void* bytes, uint64_t nbytes)
+{
+    if (!m || !name || !dims || ndims <= 0 || ndims > 4 || (!bytes && nbytes)) return fail(FL_ERR_ARG, "null argument");
+    if (m->finalized) return fail(FL_ERR_STATE, "model already finalized");
+    if (!block_elems(type)) return fail(FL_ERR_UNSUPPORTED, "Tensor type %d is not supported for dequantization.", type);
+    if (cudaSetDevice(m->d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    int64_t elems = 1;
+    for (int i = 0; i < ndims; i++) elems *= (int64_t)dims[i];
+    if (elems % block_elems(type) || (uint64_t)(elems / block_elems(type) * block_bytes(type)) != nbytes)
+        return fail(FL_ERR_ARG, "%s: %llu bytes do not match %lld elements of type %d", name,
+                    (unsigned long long)nbytes, (long long)elems, type);
+    const fl_model_desc& d = m->d;
+    const int h = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim, f = d.ffn;
+    const uint8_t* raw = static_cast<const uint8_t*>(bytes);
+    auto mat_shape_ok = [&](int rows, int cols) {
+        return ndims >= 2 && (int64_t)dims[0] == cols && elems == (int64_t)rows * cols;
+    };
+    std::string n(name);
+    if (n == "token_embd.weight") {
+        if (elems != (int64_t)d.vocab * h) return fail(FL_ERR_ARG, "token_embd.weight has %lld elements", (long long)elems);
+        int rc = dalloc(m->allocs, &m->emb_raw, nbytes);
+        if (rc) return rc;
+        CK(cudaMemcpy(m->emb_raw, raw, nbytes, cudaMemcpyHostToDevice));
+        m->emb_type = type;
+        m->emb_bytes = (int64_t)nbytes;
+        return FL_OK;
+    }
+    if (n == "output_norm.weight") return upload_vector(m, type, raw, nbytes, h, &m->out_norm);
+    if (n == "output.weight") {
+        if (!mat_shape_ok(d.vocab, h)) return fail(FL_ERR_ARG, "output.weight shape mismatch");
+        return upload_matrix(m, type, d.vocab, h, raw, nullptr, nullptr, &m->output, (double)nbytes);
+    }
+    int l;
+    std::string sfx;
+    if (!parse_layer(name, &l, &sfx)) return FL_OK; /* tensors the forward pass does not read are ignored */
+    if (l < 0 || l >= d.n_layers) return FL_OK;
+    Layer& L = m->layers[(size_t)l];
+    if (sfx == "attn_norm.weight") return upload_vector(m, type, raw, nbytes, h, &L.attn_norm);
+    if (sfx == "ffn_norm.weight") return upload_vector(m, type, raw, nbytes, h, &L.ffn_norm);
+    if (sfx == "post_attn_norm.weight") return upload_vector(m, type, raw, nbytes, h, &L.post_attn_norm);
+    if (sfx == "post_ffn_norm.weight") return upload_vector(m, type, raw, nbytes, h, &L.post_ffn_norm);
+    if (sfx == "attn_q.bias") return upload_vector(m, type, raw, nbytes, qd, &L.bq);
+    if (sfx == "attn_k.bias") return upload_vector(m, type, raw, nbytes, kvd, &L.bk);
+    if (sfx == "attn_v.bias") return upload_vector(m, type, raw, nbytes, kvd, &L.bv);
+    struct { const char* s; DevMatrix* dm; int rows, cols; } mats[] = {
+        {"attn_q.weight", &L.wq, qd, h}, {"attn_k.weight", &L.wk, kvd, h}, {"attn_v.weight", &L.wv, kvd, h},
+        {"attn_output.weight", &L.wo, h, qd}, {"ffn_down.weight", &L.down, h, f},
+    };
+    for (auto& e : mats) {
+        if (sfx == e.s) {
+            if (!mat_shape_ok(e.rows, e.cols)) return fail(FL_ERR_ARG, "%s shape mismatch", name);
+            return upload_matrix(m, type, e.rows, e.cols, raw, nullptr, nullptr, e.dm, (double)nbytes);
+        }
+    }
+    if (sfx == "ffn_gate.weight" || sfx == "ffn_up.weight") {
+        if (!mat_shape_ok(f, h)) return fail(FL_ERR_ARG, "%s shape mismatch", name);
+        if (f % 8) return fail(FL_ERR_UNSUPPORTED, "feed_forward_length %d is not a multiple of 8", f);
+        const bool is_gate = sfx == "ffn_gate.weight";
+        if (L.stash_type < 0) {
+            L.stash.assign(raw, raw + nbytes);
+            L.stash_type = type;
+            L.stash_is_gate = is_gate;
+            return FL_OK;
+        }
+        if (L.stash_is_gate == (int)is_gate) return fail(FL_ERR_ARG, "%s uploaded twice", name);
+        if (L.stash_type != type)
+            return fail(FL_ERR_UNSUPPORTED, "ffn_gate and ffn_up of layer %d have different types", l);
+        const uint8_t* gate = is_gate ? raw : L.stash.data();
+        const uint8_t* up = is_gate ? L.stash.data() : raw;
+        /* interleave: tile T rows 0..7 = gate rows 8T.., rows 8..15 = up rows 8T.. */
+        std::vector<int32_t> map((size_t)2 * f);
+        for (int R = 0; R < 2 * f; R++) {
+            int T = R / 16, r = R % 16;
+            map[(size_t)R] = r < 8 ? (8 * T + r) : (-1 - (8 * T + r - 8));
+        }
+        int rc = upload_matrix(m, type, 2 * f, h, gate, up, map.data(), &L.gate_up, 2.0 * (double)nbytes);
+        std::vector<uint8_t>().swap(L.stash);
+        return rc;
+    }
+    return FL_OK;
+}
+
+extern "C" int fl_model_finalize(fl_model* m)
+{
+    if (!m) return fail(FL_ERR_ARG, "null model");
+    if (m->finalized) return FL_OK;
+    if (cudaSetDevice(m->d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    const fl_model_desc& d = m->d;
+    if (!m->emb_raw) return fail(FL_ERR_STATE, "Required tensor 'token_embd.weight' not found in GGUF file.");
+    if (!m->out_norm) return fail(FL_ERR_STATE, "Required tensor 'output_norm.weight' not found in GGUF file.");
+    for (int l = 0; l < d.n_layers; l++) {
+        Layer& L = m->layers[(size_t)l];
+        const char* miss = nullptr;
+        if (!L.attn_norm) miss = "attn_norm.weight";
+        else if (!L.wq.present) miss = "attn_q.weight";
+        else if (!L.wk.present) miss = "attn_k.weight";
+        else if (!L.wv.present) miss = "attn_v.weight";
+        else if (!L.wo.present) miss = "attn_output.weight";
+        else if (!L.ffn_norm) miss = "ffn_norm.weight";
+        else if (!L.gate_up.present) miss = L.stash_type >= 0 ? (L.stash_is_gate ? "ffn_up.weight" : "ffn_gate.weight")
+                                                                : "ffn_gate.weight";
+        else if (!L.down.present) miss = "ffn_down.weight";
+        else if (d.arch == FL_ARCH_GEMMA2 && !L.post_attn_norm) miss = "post_attn_norm.weight";
+        else if (d.arch == FL_ARCH_GEMMA2 && !L.post_ffn_norm) miss = "post_ffn_norm.weight";
+        else if (d.arch == FL_ARCH_QWEN2 && (!L.bq || !L.bk || !L.bv)) miss = "attn_q/k/v.bias";
+        if (miss) return fail(FL_ERR_STATE, "Required tensor 'blk.%d.%s' not found in GGUF file.", l, miss);
+    }
+    if (!m->output.present) {
+        /* LoadTensorOptional("output.weight") ?? tokenEmbed (GgufModelLoader.cs:368-369) */
+        std::vector<uint8_t> host((size_t)m->emb_bytes);
+        CK(cudaMemcpy(host.data(), m->emb_raw, (size_t)m->emb_bytes, cudaMemcpyDeviceToHost));
+        int rc = upload_matrix(m, m->emb_type, d.vocab, d.hidden, host.data(), nullptr, nullptr, &m->output,
+                               (double)m->emb_bytes);
+        if (rc) return rc;
+    }
+    /* one embedding row per step */
+    m->weight_bytes += (double)m->emb_bytes / d.vocab;
+    m->finalized = true;
+    return FL_OK;
+}
+
+extern "C" int fl_model_weight_bytes(fl_model* m, double* bytes)
+{
+    if (!m || !bytes) return fail(FL_ERR_ARG, "null argument");
+    *bytes = m->weight_bytes;
+    return FL_OK;
+}
+
+/* ── session ────────────────────────────────────────────────────────────── */
+static void ring_config(FlMvArgs& a)
+{
+    int maxu = 0;
+    for (int i = 0; i < a.n_seg; i++) maxu = a.seg[i].unit_bytes > maxu ? a.seg[i].unit_bytes : maxu;
+    a.slot_bytes = (maxu + 127) & ~127;
+    int n = (12 * 1024) / a.slot_bytes;
+    a.n_slots = n < 2 ? 2 : (n > 4 ? 4 : n);
+}
+
+static void set_seg(FlMvArgs& a, int i, const DevMatrix& dm, const float* bias, int tile0)
+{
+    a.seg[i].w = dm.d;
+    a.seg[i].bias = bias;
+    a.seg[i].fmt = dm.L.fmt;
+    a.seg[i].expanded = dm.L.expanded;
+    a.seg[i].unit_bytes = dm.L.unit_bytes;
+    a.seg[i].n_tiles = dm.L.n_tiles;
+    a.seg[i].tile0 = tile0;
+    a.seg[i].rows = dm.L.rows;
+}
+
+static FlMvArgs base_args(fl_session* s, const DevMatrix& dm, int K)
+{
+    FlMvArgs a;
+    memset(&a, 0, sizeof a);
+    set_seg(a, 0, dm, nullptr, 0);
+    a.n_seg = 1;
+    a.n_tiles = dm.L.n_tiles;
+    a.n_kb = dm.L.n_kb;
+    a.K = K;
+    a.rows_total = dm.L.rows;
+    a.err = s ? s->state + ST_ERR : nullptr;
+    ring_config(a);
+    return a;
+}
+
+static int grid_for(const fl_model* m, const FlMvArgs& a) { return a.n_tiles < m->sm_count ? a.n_tiles : m->sm_count; }
+
+enum { CLS_MV = 0, CLS_ATTN = 1, CLS_OTHER = 2 };
+
+struct Recorder {
+    std::vector<cudaEvent_t>* ev = nullptr;
+    std::vector<int>* cls = nullptr;
+    std::vector<double>* bytes = nullptr;
+    int launches = 0;
+    void mark(cudaStream_t st, int c, double b)
+    {
+        launches++;
+        if (!ev) return;
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        cudaEventRecord(e, st);
+        ev->push_back(e);
+        cls->push_back(c);
+        bytes->push_back(b);
+    }
+};
+
+static double mat_bytes(const DevMatrix& dm) { return (double)dm.L.gguf_bytes; }
+
+/* Enqueues one token step (LlamaForwardPass.Forward and the per-arch copies). */
+static int record_step(fl_session* s, bool pdl, Recorder& rec)
+{
+    fl_model* m = s->m;
+    const fl_model_desc& d = m->d;
+    const int h = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim;
+    const bool gemma = d.arch == FL_ARCH_GEMMA2;
+    cudaStream_t st = s->st;
+    int32_t* token = s->state + ST_TOKEN;
+    int32_t* pos = s->state + ST_POS;
+
+    FlEmbedArgs ea;
+    ea.raw = m->emb_raw;
+    ea.ggml_type = m->emb_type;
+    ea.hidden = h;
+    ea.vocab = d.vocab;
+    ea.token = token;
+    ea.x = s->xa;
+    ea.zero_buf = s->absmax;
+    ea.zero_n = s->n_absmax;
+    ea.err = s->state + ST_ERR;
+    CK(fl_launch_embed(ea, st, pdl));
+    rec.mark(st, CLS_OTHER, (double)m->emb_bytes / d.vocab);
+
+    float* x = s->xa;
+    float* x_other = s->xb;
+    for (int l = 0; l < d.n_layers; l++) {
+        Layer& L = m->layers[(size_t)l];
+        float* amax_att = s->absmax + 2 * l;
+        float* amax_act = s->absmax + 2 * l + 1;
+        float* kc = s->kc + (size_t)l * s->max_ctx * kvd;
+        float* vc = s->vc + (size_t)l * s->max_ctx * kvd;
+        /* attention sub-layer: norm → q,k,v (+bias) → RoPE → KV append */
+        FlMvArgs a = base_args(s, L.wq, h);
+        set_seg(a, 0, L.wq, L.bq, 0);
+        set_seg(a, 1, L.wk, L.bk, L.wq.L.n_tiles);
+        set_seg(a, 2, L.wv, L.bv, L.wq.L.n_tiles + L.wk.L.n_tiles);
+        a.n_seg = 3;
+        a.n_tiles = L.wq.L.n_tiles + L.wk.L.n_tiles + L.wv.L.n_tiles;
+        ring_config(a);
+        if (!gemma) {
+            a.in_mode = FL_IN_RMSNORM;
+            a.x = x;
+            a.norm_w = L.attn_norm;
+            a.eps = d.rms_eps;
+        } else if (l == 0) {
+            a.in_mode = FL_IN_GEMMA_NORM;
+            a.x = x;
+            a.norm_w = L.attn_norm;
+            a.eps = 1e-6f;
+        } else {
+            a.in_mode = FL_IN_GEMMA_RESID;
+            a.x = x;
+            a.pend = s->o;
+            a.pend_w = m->layers[(size_t)l - 1].post_ffn_norm;
+            a.resid_out = x_other;
+            a.norm_w = L.attn_norm;
+            a.eps = 1e-6f;
+            std::swap(x, x_other);
+        }
+        a.epi = FL_EPI_QKV;
+        a.q_rows = qd;
+        a.kv_rows = kvd;
+        a.head_dim = d.head_dim;
+        a.rope_cs = m->rope_cs;
+        a.pos = pos;
+        a.q_out = s->q;
+        a.k_cache = kc;
+        a.v_cache = vc;
+        CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
+        rec.mark(st, CLS_MV, mat_bytes(L.wq) + mat_bytes(L.wk) + mat_bytes(L.wv) + 4.0 * h);
+
+        FlAttnArgs at;
+        at.q = s->q;
+        at.k_cache = kc;
+        at.v_cache = vc;
+        at.out = s->att;
+        at.out_absmax = amax_att;
+        at.part = s->attn_part;
+        at.counter = s->attn_counter;
+        at.pos = pos;
+        at.n_heads = d.n_heads;
+        at.n_kv = d.n_kv_heads;
+        at.head_dim = d.head_dim;
+        at.n_split = s->attn_split;
+        int window = INT_MAX;
+        if (d.arch == FL_ARCH_MISTRAL) window = d.sliding_window;
+        if (gemma && (l % 2) == 0) window = d.sliding_window;
+        at.window = window > 0 ? window : INT_MAX;
+        at.scale = d.attn_scale;
+        at.softcap = gemma ? d.attn_softcap : 0.0f;
+        at.err = s->state + ST_ERR;
+        CK(fl_launch_attention(at, st, pdl));
+        rec.mark(st, CLS_ATTN, 0.0);
+
+        /* output projection + residual (Gemma: post-attention norm first) */
+        a = base_args(s, L.wo, qd);
+        a.in_mode = FL_IN_PLAIN;
+        a.x = s->att;
+        a.absmax = amax_att;
+        a.epi = gemma ? FL_EPI_STORE : FL_EPI_RESID;
+        a.y = gemma ? s->o : x;
+        CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
+        rec.mark(st, CLS_MV, mat_bytes(L.wo));
+
+        /* FFN: norm → gate/up → SiLU|GELU(gate)*up */
+        a = base_args(s, L.gate_up, h);
+        if (!gemma) {
+            a.in_mode = FL_IN_RMSNORM;
+            a.x = x;
+            a.norm_w = L.ffn_norm;
+            a.eps = d.rms_eps;
+        } else {
+            a.in_mode = FL_IN_GEMMA_RESID;
+            a.x = x;
+            a.pend = s->o;
+            a.pend_w = L.post_attn_norm;
+            a.resid_out = x_other;
+            a.norm_w = L.ffn_norm;
+            a.eps = 1e-6f;
+            std::swap(x, x_other);
+        }
+        a.epi = FL_EPI_GLU;
+        a.rows_total = d.ffn;
+        a.act_gelu = gemma ? 1 : 0;
+        a.act_out = s->act;
+        a.act_absmax = amax_act;
+        CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
+        rec.mark(st, CLS_MV, mat_bytes(L.gate_up) + 4.0 * h);
+
+        a = base_args(s, L.down, d.ffn);
+        a.in_mode = FL_IN_PLAIN;
+        a.x = s->act;
+        a.absmax = amax_act;
+        a.epi = gemma ? FL_EPI_STORE : FL_EPI_RESID;
+        a.y = gemma ? s->o : x;
+        CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
+        rec.mark(st, CLS_MV, mat_bytes(L.down));
+    }
+    /* final norm + LM head + greedy argmax */
+    FlMvArgs a = base_args(s, m->output, h);
+    if (!gemma) {
+        a.in_mode = FL_IN_RMSNORM;
+        a.x = x;
+        a.norm_w = m->out_norm;
+        a.eps = d.rms_eps;
+    } else {
+        a.in_mode = FL_IN_GEMMA_RESID;
+        a.x = x;
+        a.pend = s->o;
+        a.pend_w = m->layers.back().post_ffn_norm;
+        a.resid_out = x_other;
+        a.norm_w = m->out_norm;
+        a.eps = 1e-6f;
+    }
+    a.epi = FL_EPI_LOGITS;
+    a.y = s->logits;
+    a.softcap = gemma ? d.final_softcap : 0.0f;
+    a.cta_best = s->cta_best;
+    a.counter = s->state + ST_HEADCNT;
+    a.argmax_out = s->state + ST_ARGMAX;
+    CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
+    rec.mark(st, CLS_MV, mat_bytes(m->output) + 4.0 * h);
+
+    FlAdvanceArgs ad;
+    ad.token = token;
+    ad.pos = pos;
+    ad.argmax = s->state + ST_ARGMAX;
+    ad.out_tokens = s->out_tokens;
+    ad.step = s->state + ST_STEP;
+    CK(fl_launch_advance(ad, st, pdl));
+    rec.mark(st, CLS_OTHER, 0.0);
+    return FL_OK;
+}
+
+extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch, int32_t kv_dtype, fl_session** out)
+{
+    if (!m || !out) return fail(FL_ERR_ARG, "null argument");
+    if (!m->finalized) {
+        int rc = fl_model_finalize(m);
+        if (rc) return rc;
+    }
+    if (kv_dtype != FL_KV_F32) return fail(FL_ERR_UNSUPPORTED, "kv dtype %d", kv_dtype);
+    if (max_batch > 1) return fail(FL_ERR_UNSUPPORTED, "batched sessions are not built into this library yet");
+    const fl_model_desc& d = m->d;
+    if (max_ctx <= 0 || max_ctx > d.max_ctx) max_ctx = d.max_ctx;
+    if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    fl_session* s = new fl_session();
+    s->m = m;
+    s->max_ctx = max_ctx;
+    const int h = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim, grp = d.n_heads / d.n_kv_heads;
+    /* splits: ~2 CTAs per SM over all kv heads */
+    int split = (2 * m->sm_count + d.n_kv_heads - 1) / d.n_kv_heads;
+    if (split > max_ctx) split = max_ctx;
+    if (split < 1) split = 1;
+    s->attn_split = split;
+    s->n_absmax = 2 * d.n_layers;
+    int rc = FL_OK;
+    size_t kv_bytes = (size_t)d.n_layers * max_ctx * kvd * 4;
+    int headgrid = m->output.L.n_tiles < m->sm_count ? m->output.L.n_tiles : m->sm_count;
+#define AL(p, b) if (!rc) rc = dalloc(s->allocs, &(p), (b))
+    AL(s->xa, (size_t)h * 4);
+    AL(s->xb, (size_t)h * 4);
+    AL(s->o, (size_t)h * 4);
+    AL(s->q, (size_t)qd * 4);
+    AL(s->att, (size_t)qd * 4);
+    AL(s->act, (size_t)d.ffn * 4);
+    AL(s->logits, (size_t)d.vocab * 4);
+    AL(s->kc, kv_bytes);
+    AL(s->vc, kv_bytes);
+    AL(s->absmax, (size_t)s->n_absmax * 4);
+    AL(s->state, (size_t)ST_N * 4);
+    AL(s->attn_counter, (size_t)d.n_kv_heads * 4);
+    AL(s->attn_part, (size_t)d.n_kv_heads * split * grp * (d.head_dim + 2) * 4);
+    AL(s->cta_best, (size_t)headgrid * 8 + 8);
+    AL(s->out_tokens, (size_t)max_ctx * 4 + 4);
+    s->topk_scratch_bytes = fl_topk_scratch_bytes(d.vocab, 0);
+    AL(s->topk_scratch, s->topk_scratch_bytes);
+    AL(s->topk_ids, (size_t)d.vocab * 4);
+    AL(s->topk_vals, (size_t)d.vocab * 4);
+#undef AL
+    if (rc) {
+        fl_session_destroy(s);
+        return rc;
+    }
+    if (cudaMallocHost(&s->h_state, ST_N * 4) != cudaSuccess || cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
+        fl_session_destroy(s);
+        return fail(FL_ERR_CUDA, "stream/pinned allocation failed");
+    }
+    cudaMemsetAsync(s->state, 0, ST_N * 4, s->st);
+    cudaMemsetAsync(s->attn_counter, 0, (size_t)d.n_kv_heads * 4, s->st);
+    cudaMemsetAsync(s->kc, 0, kv_bytes, s->st);
+    cudaMemsetAsync(s->vc, 0, kv_bytes, s->st);
+    if (cudaStreamSynchronize(s->st) != cudaSuccess) {
+        fl_session_destroy(s);
+        return fail(FL_ERR_CUDA, "session init failed");
+    }
+    if (fl_mv_configure() != cudaSuccess) {
+        fl_session_destroy(s);
+        return fail(FL_ERR_CUDA, "matvec kernel configuration failed");
+    }
+    /* capture the token step once */
+    Recorder rec;
+    cudaGraph_t g = nullptr;
+    if (cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        fl_session_destroy(s);
+        return fail(FL_ERR_CUDA, "graph capture failed to start");
+    }
+    rc = record_step(s, true, rec);
+    cudaError_t ce = cudaStreamEndCapture(s->st, &g);
+    if (rc || ce != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        fl_session_destroy(s);
+        return rc ? rc : fail(FL_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+    }
+    ce = cudaGraphInstantiate(&s->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) {
+        fl_session_destroy(s);
+        return fail(FL_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
+    }
+    s->launches = rec.launches;
+    *out = s;
+    return FL_OK;
+}
+
+extern "C" void fl_session_destroy(fl_session* s)
+{
+    if (!s) return;
+    cudaSetDevice(s->m->d.device);
+    if (s->st) cudaStreamSynchronize(s->st);
+    if (s->graph) cudaGraphExecDestroy(s->graph);
+    for (void* p : s->allocs) cudaFree(p);
+    if (s->h_state) cudaFreeHost(s->h_state);
+    if (s->st) cudaStreamDestroy(s->st);
+    delete s;
+}
+
+extern "C" int fl_session_reset(fl_session* s, int32_t seq_slot)
+{
+    if (!s) return fail(FL_ERR_ARG, "null session");
+    if (seq_slot != 0) return fail(FL_ERR_ARG, "sequence slot %d (single-sequence session)", seq_slot);
+    s->cur_len = 0;
+    return FL_OK;
+}
+
+extern "C" int fl_session_launches_per_step(fl_session* s, int32_t* n)
+{
+    if (!s || !n) return fail(FL_ERR_ARG, "null argument");
+    *n = s->launches;
+    return FL_OK;
+}
+
+static int check_device_err(fl_session* s)
+{
+    int32_t err = 0;
+    CK(cudaMemcpy(&err, s->state + ST_ERR, 4, cudaMemcpyDeviceToHost));
+    if (err == 0) return FL_OK;
+    int32_t zero = 0;
+    cudaMemcpy(s->state + ST_ERR, &zero, 4, cudaMemcpyHostToDevice);
+    if (err == 1) return fail(FL_ERR_TIMEOUT, "a bounded device wait expired (bulk copy did not complete)");
+    return fail(FL_ERR_ARG, "device reported error %d", err);
+}
+
+static int set_state(fl_session* s, int token, int pos)
+{
+    s->h_state[ST_TOKEN] = token;
+    s->h_state[ST_POS] = pos;
+    s->h_state[ST_ARGMAX] = 0;
+    s->h_state[ST_STEP] = 0;
+    CK(cudaMemcpyAsync(s->state, s->h_state, 4 * 4, cudaMemcpyHostToDevice, s->st));
+    return FL_OK;
+}
+
+extern "C" int fl_forward(fl_session* s, int32_t token, int32_t position, float* logits, int32_t* argmax)
+{
+    if (!s) return fail(FL_ERR_ARG, "null session");
+    const fl_model_desc& d = s->m->d;
+    if ((uint32_t)token >= (uint32_t)d.vocab)
+        return fail(FL_ERR_ARG, "Token id %d is outside the valid vocabulary range [0, %d].", token, d.vocab - 1);
+    if (position < 0 || position >= s->max_ctx)
+        return fail(FL_ERR_ARG, "position %d is outside the KV cache [0, %d)", position, s->max_ctx);
+    if (position > s->cur_len)
+        return fail(FL_ERR_ARG, "position %d skips cached positions (cache holds %d)", position, s->cur_len);
+    if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    int rc = set_state(s, token, position);
+    if (rc) return rc;
+    CK(cudaGraphLaunch(s->graph, s->st));
+    if (logits) CK(cudaMemcpyAsync(logits, s->logits, (size_t)d.vocab * 4, cudaMemcpyDeviceToHost, s->st));
+    if (argmax) CK(cudaMemcpyAsync(&s->h_state[ST_ARGMAX], s->state + ST_ARGMAX, 4, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaStreamSynchronize(s->st));
+    rc = check_device_err(s);
+    if (rc) return rc;
+    if (argmax) *argmax = s->h_state[ST_ARGMAX];
+    s->cur_len = position + 1;
+    return FL_OK;
+}
+
+static int run_steps(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, float* ms)
+{
+    const fl_model_desc& d = s->m->d;
+    if ((uint32_t)token >= (uint32_t)d.vocab) return fail(FL_ERR_ARG, "Token id %d is outside the vocabulary", token);
+    if (start_pos < 0 || start_pos > s->cur_len || n_steps < 0 || start_pos + n_steps > s->max_ctx)
+        return fail(FL_ERR_ARG, "steps [%d, %d) do not fit the KV cache (holds %d of %d)", start_pos,
+                    start_pos + n_steps, s->cur_len, s->max_ctx);
+    if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    int rc = set_state(s, token, start_pos);
+    if (rc) return rc;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ms) {
+        CK(cudaEventCreate(&e0));
+        CK(cudaEventCreate(&e1));
+        CK(cudaEventRecord(e0, s->st));
+    }
+    for (int i = 0; i < n_steps; i++) CK(cudaGraphLaunch(s->graph, s->st));
+    if (ms) CK(cudaEventRecord(e1, s->st));
+    CK(cudaStreamSynchronize(s->st));
+    if (ms) {
+        cudaEventElapsedTime(ms, e0, e1);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    rc = check_device_err(s);
+    if (rc) return rc;
+    s->cur_len = start_pos + n_steps;
+    return FL_OK;
+}
+
+extern "C" int fl_decode_greedy(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, int32_t* out_tokens)
+{
+    if (!s) return fail(FL_ERR_ARG, "null session");
+    int rc = run_steps(s, token, start_pos, n_steps, nullptr);
+    if (rc) return rc;
+    if (out_tokens && n_steps > 0) CK(cudaMemcpy(out_tokens, s->out_tokens, (size_t)n_steps * 4, cudaMemcpyDeviceToHost));
+    return FL_OK;
+}
+
+extern "C" int fl_time_decode(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, float* ms)
+{
+    if (!s || !ms) return fail(FL_ERR_ARG, "null argument");
+    return run_steps(s, token, start_pos, n_steps, ms);
+}
+
+extern "C" int fl_profile_step(fl_session* s, int32_t token, int32_t position, double* ms, double* bytes,
+                               int32_t* launches)
+{
+    if (!s || !ms || !bytes) return fail(FL_ERR_ARG, "null argument");
+    const fl_model_desc& d = s->m->d;
+    if ((uint32_t)token >= (uint32_t)d.vocab || position < 0 || position >= s->max_ctx || position > s->cur_len)
+        return fail(FL_ERR_ARG, "bad token/position");
+    if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    int rc = set_state(s, token, position);
+    if (rc) return rc;
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> cls;
+    std::vector<double> by;
+    Recorder rec;
+    rec.ev = &ev;
+    rec.cls = &cls;
+    rec.bytes = &by;
+    cudaEvent_t e0;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventRecord(e0, s->st));
+    rc = record_step(s, false, rec);
+    if (rc) return rc;
+    CK(cudaStreamSynchronize(s->st));
+    for (int i = 0; i < FL_PROF_N; i++) { ms[i] = 0; bytes[i] = 0; }
+    cudaEvent_t prev = e0;
+    for (size_t i = 0; i < ev.size(); i++) {
+        float t = 0;
+        cudaEventElapsedTime(&t, prev, ev[i]);
+        ms[cls[i]] += t;
+        bytes[cls[i]] += by[i];
+        ms[FL_PROF_STEP] += t;
+        bytes[FL_PROF_STEP] += by[i];
+        prev = ev[i];
+    }
+    for (auto e : ev) cudaEventDestroy(e);
+    cudaEventDestroy(e0);
+    if (launches) *launches = (int32_t)ev.size();
+    rc = check_device_err(s);
+    if (rc) return rc;
+    s->cur_len = position + 1;
+    return FL_OK;
+}
+
+extern "C" int fl_topk(fl_session* s, int32_t k, int32_t* ids, float* vals, float* threshold)
+{
+    if (!s || !ids || !vals) return fail(FL_ERR_ARG, "null argument");
+    const fl_model_desc& d = s->m->d;
+    if (k < 1 || k > d.vocab) return fail(FL_ERR_ARG, "k must be in [1, %d]", d.vocab);
+    if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    CK(fl_launch_topk(s->logits, d.vocab, k, s->topk_ids, s->topk_vals, s->topk_scratch, s->topk_scratch_bytes, s->st));
+    CK(cudaMemcpyAsync(ids, s->topk_ids, (size_t)k * 4, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaMemcpyAsync(vals, s->topk_vals, (size_t)k * 4, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaStreamSynchronize(s->st));
+    if (threshold) *threshold = vals[k - 1];
+    return FL_OK;
+}
+
+/* ── stateless helpers ──────────────────────────────────────────────────── */
+extern "C" int fl_dequant(int32_t type, const void* src, uint64_t nbytes, float* dst, uint64_t dst_len)
+{
+    /* Dequantizer.Dequantize (Dequantizer.cs:488-504) validation order */
+    int be = block_elems(type), bb = block_bytes(type);
+    if (!be) return fail(FL_ERR_UNSUPPORTED, "Tensor type %d is not supported for dequantization.", type);
+    if (nbytes % (uint64_t)bb) return fail(FL_ERR_ARG, "Source length must be a multiple of %d.", bb);
+    uint64_t n = nbytes / bb * be;
+    if (dst_len < n) return fail(FL_ERR_ARG, "Destination must hold at least %llu floats.", (unsigned long long)n);
+    if (n == 0) return FL_OK;
+    if (!src || !dst) return fail(FL_ERR_ARG, "null argument");
+    uint8_t* dsrc = nullptr;
+    float* ddst = nullptr;
+    CK(cudaMalloc(&dsrc, nbytes));
+    cudaError_t e = cudaMalloc(&ddst, n * 4);
+    if (e != cudaSuccess) {
+        cudaFree(dsrc);
+        return fail(FL_ERR_OOM, "cudaMalloc: %s", cudaGetErrorString(e));
+    }
+    e = cudaMemcpy(dsrc, src, nbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = fl_launch_dequant(type, dsrc, (int64_t)n, ddst, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(dst, ddst, n * 4, cudaMemcpyDeviceToHost);
+    cudaFree(dsrc);
+    cudaFree(ddst);
+    if (e != cudaSuccess) return fail(FL_ERR_CUDA, "fl_dequant: %s", cudaGetErrorString(e));
+    return FL_OK;
+}
+
+extern "C" int fl_matvec(int32_t type, const void* w, uint64_t nbytes, int32_t rows, int32_t cols, const float* x,
+                         float* y)
+{
+    if (!w || !x || !y) return fail(FL_ERR_ARG, "null argument");
+    fl_matrix_layout L;
+    int r = fl_layout_for(type, rows, cols, &L);
+    if (r == -1) return fail(FL_ERR_UNSUPPORTED, "type %d has no quantized matvec path", type);
+    if (r == -2) return fail(FL_ERR_UNSUPPORTED, "row length %d is not a multiple of 32", cols);
+    if ((int64_t)nbytes != L.gguf_bytes) return fail(FL_ERR_ARG, "byte length does not match rows x cols");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    std::vector<uint8_t> host((size_t)L.total_bytes);
+    fl_repack(&L, static_cast<const uint8_t*>(w), nullptr, nullptr, host.data(), 0);
+    float amax = 0.0f;
+    for (int i = 0; i < cols; i++) amax = fmaxf(amax, fabsf(x[i]));
+    std::vector<void*> al;
+    DevMatrix dm;
+    dm.L = L;
+    float *dx = nullptr, *dy = nullptr, *dam = nullptr;
+    int* derr = nullptr;
+    int rc = dalloc(al, &dm.d, (size_t)L.total_bytes);
+    if (!rc) rc = dalloc(al, &dx, (size_t)L.n_kb * 256 * 4);
+    if (!rc) rc = dalloc(al, &dy, (size_t)rows * 4);
+    if (!rc) rc = dalloc(al, &dam, 16);
+    if (!rc) rc = dalloc(al, &derr, 16);
+    cudaError_t e = cudaSuccess;
+    if (!rc) {
+        e = cudaMemcpy(dm.d, host.data(), (size_t)L.total_bytes, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(dx, x, (size_t)cols * 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(dam, &amax, 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemset(derr, 0, 16);
+        if (e == cudaSuccess) {
+            FlMvArgs a = base_args(nullptr, dm, cols);
+            a.err = derr;
+            a.in_mode = FL_IN_PLAIN;
+            a.x = dx;
+            a.absmax = dam;
+            a.epi = FL_EPI_STORE;
+            a.y = dy;
+            int grid = a.n_tiles < sms ? a.n_tiles : sms;
+            e = fl_launch_matvec(a, grid, 0, false);
+        }
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemcpy(y, dy, (size_t)rows * 4, cudaMemcpyDeviceToHost);
+        int err = 0;
+        if (e == cudaSuccess) e = cudaMemcpy(&err, derr, 4, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && err) rc = fail(FL_ERR_TIMEOUT, "bounded device wait expired");
+    }
+    for (void* p : al) cudaFree(p);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(FL_ERR_CUDA, "fl_matvec: %s", cudaGetErrorString(e));
+    return FL_OK;
+}

@@ -1,0 +1,259 @@
+"""Host-side mirror of the reference's forward-pass seam over the C ABI.
+
+``CudaModel`` is the device counterpart of ``LlamaWeights``/``Gemma2Weights``
+(the ``IDisposable modelResources`` of ``LlamaLanguageModel``,
+src/DotNetFoundryLLM.Inference/LlamaLanguageModel.cs:48-80) and
+``CudaForwardPass`` implements ``IForwardPass``
+(src/DotNetFoundryLLM.Architectures/IForwardPass.cs:8-15): ``forward(token_id,
+position, kv_cache)`` and ``logits``.  The KV cache lives in HBM; the
+``kv_cache`` argument is only the session key, as in the C# backend.
+
+Error behaviour follows the reference: a token id outside [0, vocab) raises
+``ArgumentOutOfRangeError`` (LlamaForwardPass.cs:89-93), an unknown tensor type
+``NotSupportedError`` (Dequantizer.cs:501-502), a missing tensor
+``InvalidOperationError`` (GgufModelLoader.cs:411-412), use after dispose
+``ObjectDisposedError`` (LlamaWeights.cs:138-139).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _native as N
+
+
+class FoundryError(RuntimeError):
+    code = -1
+
+
+class ArgumentError(FoundryError, ValueError):
+    """System.ArgumentException."""
+
+
+class ArgumentOutOfRangeError(ArgumentError, IndexError):
+    """System.ArgumentOutOfRangeException."""
+
+
+class NotSupportedError(FoundryError, NotImplementedError):
+    """System.NotSupportedException."""
+
+
+class InvalidOperationError(FoundryError):
+    """System.InvalidOperationException."""
+
+
+class ObjectDisposedError(InvalidOperationError):
+    """System.ObjectDisposedException."""
+
+
+class DeviceTimeoutError(FoundryError, TimeoutError):
+    """A bounded device-side wait expired (FL_ERR_TIMEOUT)."""
+
+
+class DeviceError(FoundryError):
+    """CUDA / NCCL / allocation failure."""
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc == N.FL_OK:
+        return
+    msg = N.last_error()
+    text = f"{what}: {msg}" if what else msg
+    if rc == N.FL_ERR_ARG:
+        cls = ArgumentOutOfRangeError if ("outside" in msg or "range" in msg) else ArgumentError
+    elif rc == N.FL_ERR_UNSUPPORTED:
+        cls = NotSupportedError
+    elif rc == N.FL_ERR_STATE:
+        cls = InvalidOperationError
+    elif rc == N.FL_ERR_TIMEOUT:
+        cls = DeviceTimeoutError
+    else:
+        cls = DeviceError
+    err = cls(text)
+    err.code = rc
+    raise err
+
+
+def _ptr(a: np.ndarray) -> C.c_void_p:
+    return a.ctypes.data_as(C.c_void_p)
+
+
+class CudaModel:
+    """Device weights of one model (repacked GGUF blocks, no F32 copy)."""
+
+    def __init__(self, desc: N.FlModelDesc):
+        self.lib = N.cuda()
+        self.desc = desc
+        h = C.c_void_p()
+        check(self.lib.fl_model_create(C.byref(desc), C.byref(h)), "fl_model_create")
+        self._h = h
+
+    @property
+    def handle(self) -> C.c_void_p:
+        if self._h is None:
+            raise ObjectDisposedError("CudaModel")
+        return self._h
+
+    def upload(self, name: str, ggml_type: int, dims: list[int], payload: np.ndarray) -> None:
+        payload = np.ascontiguousarray(payload, dtype=np.uint8)
+        d = (C.c_uint64 * len(dims))(*dims)
+        check(self.lib.fl_model_upload(self.handle, name.encode(), ggml_type, d, len(dims), _ptr(payload),
+                                       payload.size), f"upload {name}")
+
+    def finalize(self) -> None:
+        check(self.lib.fl_model_finalize(self.handle), "fl_model_finalize")
+
+    def weight_bytes(self) -> float:
+        b = C.c_double()
+        check(self.lib.fl_model_weight_bytes(self.handle, C.byref(b)))
+        return b.value
+
+    def close(self) -> None:
+        if self._h is not None:
+            self.lib.fl_model_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class CudaForwardPass:
+    """IForwardPass over a device session (one KV cache in HBM)."""
+
+    def __init__(self, model: CudaModel, max_ctx: int = 0):
+        self.model = model
+        self.lib = model.lib
+        h = C.c_void_p()
+        check(self.lib.fl_session_create(model.handle, max_ctx, 1, 0, C.byref(h)), "fl_session_create")
+        self._h = h
+        self.vocab = model.desc.vocab
+        self._logits = np.zeros(self.vocab, dtype=np.float32)
+        self._argmax = C.c_int32()
+        self._kv_key = None
+
+    @property
+    def handle(self) -> C.c_void_p:
+        if self._h is None:
+            raise ObjectDisposedError("CudaForwardPass")
+        return self._h
+
+    @property
+    def logits(self) -> np.ndarray:
+        """IForwardPass.Logits: logits of the most recent forward call."""
+        return self._logits
+
+    def forward(self, token_id: int, position: int, kv_cache=None, want_logits: bool = True) -> int:
+        """IForwardPass.Forward; returns the greedy argmax as a convenience."""
+        if kv_cache is not self._kv_key or position == 0:
+            check(self.lib.fl_session_reset(self.handle, 0))
+            self._kv_key = kv_cache
+        check(self.lib.fl_forward(self.handle, int(token_id), int(position),
+                                  _ptr(self._logits) if want_logits else None, C.byref(self._argmax)),
+              "fl_forward")
+        return int(self._argmax.value)
+
+    def decode_greedy(self, token_id: int, start_pos: int, n_steps: int) -> np.ndarray:
+        out = np.zeros(max(n_steps, 1), dtype=np.int32)
+        check(self.lib.fl_decode_greedy(self.handle, int(token_id), int(start_pos), int(n_steps), _ptr(out)),
+              "fl_decode_greedy")
+        return out[:n_steps]
+
+    def topk(self, k: int) -> tuple[np.ndarray, np.ndarray, float]:
+        ids = np.zeros(k, dtype=np.int32)
+        vals = np.zeros(k, dtype=np.float32)
+        thr = C.c_float()
+        check(self.lib.fl_topk(self.handle, k, _ptr(ids), _ptr(vals), C.byref(thr)), "fl_topk")
+        return ids, vals, thr.value
+
+    def time_decode(self, token_id: int, start_pos: int, n_steps: int) -> float:
+        ms = C.c_float()
+        check(self.lib.fl_time_decode(self.handle, int(token_id), int(start_pos), int(n_steps), C.byref(ms)),
+              "fl_time_decode")
+        return ms.value
+
+    def profile_step(self, token_id: int, position: int) -> dict:
+        ms = (C.c_double * N.FL_PROF_N)()
+        by = (C.c_double * N.FL_PROF_N)()
+        nl = C.c_int32()
+        check(self.lib.fl_profile_step(self.handle, int(token_id), int(position), ms, by, C.byref(nl)),
+              "fl_profile_step")
+        names = ["matvec", "attention", "other", "step"]
+        return {"ms": dict(zip(names, list(ms))), "bytes": dict(zip(names, list(by))), "launches": nl.value}
+
+    def launches_per_step(self) -> int:
+        n = C.c_int32()
+        check(self.lib.fl_session_launches_per_step(self.handle, C.byref(n)))
+        return n.value
+
+    def close(self) -> None:
+        if self._h is not None:
+            self.lib.fl_session_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def generate_greedy(fwd: CudaForwardPass, prompt: np.ndarray, max_tokens: int, eos: int | None = None,
+                    collect_logits: bool = False):
+    """LlamaLanguageModel.GenerateAsync with Temperature = 0
+    (LlamaLanguageModel.cs:126-293): Forward every prompt token but the last,
+    then forward the last prompt token as decode step 0 and feed back the
+    ArgMax; stop at EOS or after max_tokens.  Returns (tokens, logits|None)."""
+    kv = object()
+    pos = 0
+    for i in range(len(prompt) - 1):
+        fwd.forward(int(prompt[i]), pos, kv, want_logits=False)
+        pos += 1
+    nxt = int(prompt[-1]) if len(prompt) else fwd.model.desc.bos
+    toks, logs = [], []
+    for _ in range(max_tokens):
+        nxt = fwd.forward(nxt, pos, kv, want_logits=collect_logits)
+        pos += 1
+        if collect_logits:
+            logs.append(fwd.logits.copy())
+        toks.append(nxt)
+        if eos is not None and nxt == eos:
+            break
+    return np.array(toks, dtype=np.int32), (np.stack(logs) if collect_logits else None)
+
+
+def dequantize(ggml_type: int, raw: np.ndarray, dst_len: int | None = None) -> np.ndarray:
+    """Dequantizer.Dequantize on the device (bit-exact)."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    lib = N.cuda()
+    if dst_len is None:
+        from .gguf import BLOCK
+        be, bb = BLOCK.get(ggml_type, (1, 1))
+        dst_len = raw.size // bb * be
+    out = np.zeros(max(dst_len, 1), dtype=np.float32)
+    check(lib.fl_dequant(ggml_type, _ptr(raw), raw.size, _ptr(out), dst_len), "fl_dequant")
+    return out[:dst_len]
+
+
+def matvec(ggml_type: int, raw: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    """One dequant-matvec launch through the forward pass's kernel."""
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(rows, dtype=np.float32)
+    check(N.cuda().fl_matvec(ggml_type, _ptr(raw), raw.size, rows, cols, _ptr(x), _ptr(y)), "fl_matvec")
+    return y

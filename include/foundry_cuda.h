@@ -1,0 +1,172 @@
+/*
+ * foundry_cuda.h — C ABI of the B200 token-loop backend for DotNetFoundryLLM.
+ *
+ * Plain C: opaque handles, pointers and sizes; no CUDA or torch types.  The
+ * C# side binds these with [LibraryImport].
+ *
+ * Each entry point names the reference interface it replaces (paths inside
+ * justinamiller/DotNetFoundryLLM v1.0.0).
+ *
+ * Error convention: every int-returning call returns FL_OK (0) or one of the
+ * FL_ERR_* codes below, and fl_last_error() returns the message of the last
+ * failure on the calling thread.  The C# wrapper maps the codes onto the
+ * exception types the reference throws (ArgumentOutOfRangeException for a bad
+ * token id, NotSupportedException for an unknown tensor type, ...).
+ */
+#ifndef FOUNDRY_CUDA_H
+#define FOUNDRY_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FL_ABI_VERSION 1
+
+#define FL_OK 0
+#define FL_ERR_ARG 1          /* ArgumentException / ArgumentOutOfRangeException */
+#define FL_ERR_OOM 2          /* device allocation failed */
+#define FL_ERR_CUDA 3         /* CUDA runtime error (message has the name) */
+#define FL_ERR_NCCL 4         /* NCCL error */
+#define FL_ERR_TIMEOUT 5      /* a bounded device-side wait gave up */
+#define FL_ERR_UNSUPPORTED 6  /* NotSupportedException (tensor type, shape) */
+#define FL_ERR_STATE 7        /* InvalidOperationException / ObjectDisposedException */
+
+#define FL_ARCH_LLAMA 0       /* LlamaForwardPass.cs */
+#define FL_ARCH_MISTRAL 1     /* MistralForwardPass.cs */
+#define FL_ARCH_GEMMA2 2      /* Gemma2ForwardPass.cs */
+#define FL_ARCH_QWEN2 3       /* Qwen2ForwardPass.cs */
+
+#define FL_KV_F32 0           /* KvCache.cs layout: F32 [max_ctx, kv_dim] per layer */
+
+typedef struct fl_model fl_model;
+typedef struct fl_session fl_session;
+
+/* Model hyper-parameters: the union of LlamaConfig.cs, MistralConfig.cs and
+ * Gemma2Config.cs as GgufModelLoader.BuildConfig/BuildGemma2/BuildMistral fill
+ * them (src/DotNetFoundryLLM.ModelFormats.Gguf/GgufModelLoader.cs:104-334). */
+typedef struct fl_model_desc {
+    int32_t struct_size;      /* sizeof(fl_model_desc) */
+    int32_t arch;             /* FL_ARCH_* (GgufModelLoader.Build :89-102) */
+    int32_t n_layers;         /* LayerCount */
+    int32_t hidden;           /* HiddenSize */
+    int32_t ffn;              /* IntermediateSize */
+    int32_t n_heads;          /* NumHeads */
+    int32_t n_kv_heads;       /* NumKvHeads */
+    int32_t head_dim;         /* HeadDim (Gemma2: HeadDimOverride when set) */
+    int32_t vocab;            /* VocabSize */
+    int32_t max_ctx;          /* MaxContextLength */
+    int32_t bos, eos;         /* BosTokenId, EosTokenId */
+    int32_t sliding_window;   /* Mistral/Gemma2 SlidingWindowSize; INT32_MAX = none */
+    int32_t rope_scaled;      /* 1 when RopeScalingType is linear|yarn and factor > 0 */
+    float rms_eps;            /* TensorOperations.RmsNorm eps (1e-5); Gemma2 uses 1e-6 always */
+    float rope_base;          /* RopeBaseFreq */
+    float rope_factor;        /* RopeScalingFactor */
+    float attn_softcap;       /* Gemma2 AttnLogitSoftcap (0 = off) */
+    float final_softcap;      /* Gemma2 FinalLogitSoftcap (0 = off) */
+    float attn_scale;         /* 1/sqrt(head_dim), or Gemma2 QueryPreAttnScalar */
+    int32_t device;           /* CUDA device ordinal for this rank */
+    int32_t tp_rank, tp_size; /* tensor parallelism inside one box (1 = off) */
+    const void* nccl_id;      /* 128-byte ncclUniqueId shared by all ranks when tp_size > 1 */
+} fl_model_desc;
+
+/* Last error message of the calling thread ("" when none). */
+const char* fl_last_error(void);
+int32_t fl_abi_version(void);
+
+/* Replaces GgufModelLoader's F32 weight assembly (LoadWeights :336-372):
+ * creates an empty device model for the given config. */
+int fl_model_create(const fl_model_desc* desc, fl_model** out);
+
+/* Replaces GgufModelLoader.LoadTensor (GgufModelLoader.cs:409-418) +
+ * Dequantizer.Dequantize (Dequantizer.cs:488-504): takes the RAW GGUF block
+ * bytes of one tensor (GgufFile.GetTensorBytes, GgufFile.cs:76-97), copies
+ * them before returning (the caller's span may be a reused mmap scratch
+ * buffer, GgufFile.cs:94-96) and repacks them into the device layout.  No F32
+ * expansion happens.  `name` is the GGUF tensor name (token_embd.weight,
+ * blk.N.attn_q.weight, ...); dims are in GGUF order (ne0 = row length). */
+int fl_model_upload(fl_model* m, const char* name, int32_t ggml_type, const uint64_t* dims, int32_t ndims,
+                    const void* bytes, uint64_t nbytes);
+
+/* Checks that every tensor the forward pass needs is present (the
+ * "Required tensor ... not found" check of LoadTensor, GgufModelLoader.cs:
+ * 411-412; output.weight falls back to token_embd.weight, :368-369). */
+int fl_model_finalize(fl_model* m);
+
+/* Replaces LlamaWeights.Dispose (LlamaWeights.cs:93-105). */
+void fl_model_destroy(fl_model* m);
+
+/* Per-request forward-pass state: replaces `new KvCache(layers, maxContext,
+ * kvDim)` (LlamaLanguageModel.cs:129) and the scratch arrays each forward
+ * pass allocates (LlamaForwardPass.cs:54-62).  The KV cache lives in HBM.
+ * max_ctx <= 0 uses the model's MaxContextLength. */
+int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch, int32_t kv_dtype, fl_session** out);
+
+/* KvCache.Clear (KvCache.cs:138-144). */
+int fl_session_reset(fl_session* s, int32_t seq_slot);
+
+/* IForwardPass.Forward(tokenId, position, kvCache) (IForwardPass.cs:8-15,
+ * LlamaForwardPass.cs:82-130 and the Mistral/Gemma2/Qwen2 copies), plus the
+ * greedy sampler (GreedySampler.cs:17 / SamplerPipeline.cs:79-82).
+ * K/V for `position` are written into the device cache; attention covers
+ * [max(0, position+1-window), position+1).  position must be <= the number of
+ * cached positions (a smaller value rewinds).  logits (vocab floats, the
+ * IForwardPass.Logits span) and argmax (TensorPrimitives.IndexOfMax, first
+ * maximum) are copied to host memory when the pointers are non-NULL. */
+int fl_forward(fl_session* s, int32_t token, int32_t position, float* logits, int32_t* argmax);
+
+/* Greedy decode of n_steps tokens entirely on the device: step i feeds the
+ * argmax of step i-1 (step 0 feeds `token`) at position start_pos + i.  The
+ * generated ids are copied to out_tokens (n_steps ints) at the end.  This is
+ * the decode loop of LlamaLanguageModel.GenerateAsync (LlamaLanguageModel.cs:
+ * 162-216) with Temperature = 0 and no host round trip per token. */
+int fl_decode_greedy(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, int32_t* out_tokens);
+
+/* TopKSampler.ApplyTopK (TopKSampler.cs:42-71) on the logits of the last
+ * forward: the k largest logits (value descending, index ascending) and the
+ * threshold (the k-th largest).  Ties at the threshold are what ApplyTopK
+ * keeps; ids/vals receive exactly k entries. */
+int fl_topk(fl_session* s, int32_t k, int32_t* ids, float* vals, float* threshold);
+
+void fl_session_destroy(fl_session* s);
+
+/* Dequantizer.Dequantize (Dequantizer.cs:488-504) on the device, bit-exact:
+ * src is host memory with whole blocks, dst receives the F32 values.
+ * Returns FL_ERR_ARG for a length that is not a multiple of the block size or a
+ * dst that is too small (the ArgumentException cases), FL_ERR_UNSUPPORTED for
+ * a type id outside {0,1,2,8,12,13,14,15,30}. */
+int fl_dequant(int32_t ggml_type, const void* src, uint64_t nbytes, float* dst, uint64_t dst_len);
+
+/* One dequant-matvec launch, y = W x, through the same repack and kernel the
+ * forward pass uses (LinearProjection, LlamaForwardPass.cs:237-260, over the
+ * quantized weights).  W is raw GGUF bytes for rows x cols elements. */
+int fl_matvec(int32_t ggml_type, const void* w, uint64_t nbytes, int32_t rows, int32_t cols, const float* x,
+              float* y);
+
+/* Timing helpers for the benchmark: run the token step eagerly with CUDA
+ * events around each kernel class on the session stream; fills
+ * ms[class] and bytes[class] (algorithmic bytes) for FL_PROF_* classes. */
+#define FL_PROF_MATVEC 0
+#define FL_PROF_ATTN 1
+#define FL_PROF_OTHER 2
+#define FL_PROF_STEP 3
+#define FL_PROF_N 4
+int fl_profile_step(fl_session* s, int32_t token, int32_t position, double* ms, double* bytes, int32_t* launches);
+
+/* Device step time of the captured token graph: runs n_steps greedy steps as
+ * in fl_decode_greedy and returns the elapsed device milliseconds (CUDA events
+ * on the session stream). */
+int fl_time_decode(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, float* ms);
+
+/* Bytes of weights one decode step reads (the GGUF payload of every matrix,
+ * norm and one embedding row): the roofline numerator without the KV term. */
+int fl_model_weight_bytes(fl_model* m, double* bytes);
+
+/* Number of kernels the token graph launches per step. */
+int fl_session_launches_per_step(fl_session* s, int32_t* n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

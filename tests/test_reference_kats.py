@@ -1,0 +1,157 @@
+"""The CPU restatement (oracle) and the host GGUF reader against every
+known-answer vector of the reference's own tests (tests/golden/
+reference_kats.json, each entry citing its DequantizerTests.cs /
+GreedySamplerTests.cs / TopKSamplerTests.cs / GgufReaderTests.cs line)."""
+from __future__ import annotations
+
+import json
+import struct
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+KATS = json.loads((Path(__file__).parent / "golden" / "reference_kats.json").read_text())
+
+
+def test_fixture_matches_generator():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("mk", Path(__file__).parent / "golden" / "make_reference_kats.py")
+    mk = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mk)
+    gen = {k: [{kk: vv for kk, vv in e.items() if kk != "needle"} for e in v] for k, v in mk.KATS.items()}
+    assert json.loads(json.dumps(gen)) == KATS
+    assert mk.check_against_reference() == []
+
+
+@pytest.mark.parametrize("e", KATS["half_to_float"], ids=lambda e: hex(e["bits"]))
+def test_half_to_float(e):
+    assert O.lib().or_half_to_float(e["bits"]) == e["value"]
+
+
+@pytest.mark.parametrize("e", KATS["bf16_to_float"], ids=lambda e: hex(e["bits"]))
+def test_bf16_to_float(e):
+    assert O.lib().or_bf16_to_float(e["bits"]) == e["value"]
+
+
+@pytest.mark.parametrize("e", KATS["dequantize"], ids=lambda e: e["name"])
+def test_dequantize_known_blocks(e):
+    raw = np.frombuffer(bytes.fromhex(e["hex"]), dtype=np.uint8)
+    rc, out = O.dequantize(e["type"], raw)
+    assert rc == O.OK
+    if "expect_all" in e:
+        np.testing.assert_array_equal(out, np.array(e["expect_all"], dtype=np.float32))
+    for k, v in e.get("expect", {}).items():
+        assert out[int(k)] == np.float32(v)
+
+
+@pytest.mark.parametrize("e", KATS["dequantize_throws"], ids=lambda e: f"type{e['type']}-{e['src_len']}")
+def test_dequantize_throws(e):
+    raw = np.zeros(e["src_len"], dtype=np.uint8)
+    rc, _ = O.dequantize(e["type"], raw, e["dst_len"])
+    expect = O.ARGUMENT_EXCEPTION if e["exception"] == "ArgumentException" else O.NOT_SUPPORTED
+    assert rc == expect
+
+
+@pytest.mark.parametrize("e", KATS["element_count"], ids=lambda e: f"type{e['type']}")
+def test_element_count(e):
+    assert O.lib().or_element_count(e["type"], e["bytes"]) == e["count"]
+
+
+@pytest.mark.parametrize("e", KATS["argmax"], ids=lambda e: str(e["x"]))
+def test_greedy_argmax(e):
+    x = np.array(e["x"], dtype=np.float32)
+    assert O.lib().or_argmax(x.ctypes.data_as(O.C.c_void_p), x.size) == e["index"]
+
+
+@pytest.mark.parametrize("e", KATS["apply_topk"], ids=lambda e: f"k{e['k']}")
+def test_apply_topk(e):
+    x = np.array(e["x"], dtype=np.float32)
+    orig = x.copy()
+    O.lib().or_apply_topk(x.ctypes.data_as(O.C.c_void_p), x.size, e["k"])
+    for i in e["neg_inf"]:
+        assert x[i] == -np.inf
+    for i in e["kept"]:
+        assert x[i] == orig[i]
+
+
+def test_dot():
+    e = KATS["dot"][0]
+    a = np.array(e["a"], dtype=np.float32)
+    b = np.array(e["b"], dtype=np.float32)
+    assert O.lib().or_dot(a.ctypes.data_as(O.C.c_void_p), b.ctypes.data_as(O.C.c_void_p), 3) == e["value"]
+
+
+# ── GGUF reader cases (GgufReaderTests.cs) through both the Python mirror and
+#    the oracle's C restatement ──────────────────────────────────────────────
+
+def _gguf(version=3, n_t=0, kvs=b"", n_kv=0, tensors=b""):
+    return b"GGUF" + struct.pack("<IQQ", version, n_t, n_kv) + kvs + tensors
+
+
+def _s(x: str) -> bytes:
+    b = x.encode()
+    return struct.pack("<Q", len(b)) + b
+
+
+def _oracle_parse(data: bytes):
+    buf = np.frombuffer(data, dtype=np.uint8).copy()
+    err = O.C.create_string_buffer(256)
+    h = O.lib().or_gguf_parse(buf.ctypes.data_as(O.C.c_void_p), buf.size, err, 256)
+    return h, err.value.decode(), buf
+
+
+def test_gguf_invalid_magic():
+    from dotnetfoundryllm_b200 import gguf
+    data = bytes([0, 1, 2, 3, 3, 0, 0, 0] + [0] * 16)
+    with pytest.raises(gguf.ModelLoadError, match="(?i)magic"):
+        gguf.parse(data)
+    h, err, _ = _oracle_parse(data)
+    assert not h and "magic" in err.lower()
+
+
+@pytest.mark.parametrize("v", [0, 1, 4])
+def test_gguf_invalid_version(v):
+    from dotnetfoundryllm_b200 import gguf
+    with pytest.raises(gguf.ModelLoadError, match="(?i)version"):
+        gguf.parse(_gguf(v))
+    h, err, _ = _oracle_parse(_gguf(v))
+    assert not h and "version" in err.lower()
+
+
+@pytest.mark.parametrize("v", [2, 3])
+def test_gguf_empty(v):
+    from dotnetfoundryllm_b200 import gguf
+    g = gguf.parse(_gguf(v))
+    assert g.version == v and g.tensors == [] and g.metadata == {}
+    h, _, keep = _oracle_parse(_gguf(v))
+    assert h and O.lib().or_gguf_version(h) == v and O.lib().or_gguf_tensor_count(h) == 0
+    O.lib().or_gguf_free(h)
+
+
+def test_gguf_metadata_and_tensor_info():
+    from dotnetfoundryllm_b200 import gguf
+    kv = _s("general.architecture") + struct.pack("<I", gguf.STR) + _s("llama")
+    kv += _s("llama.block_count") + struct.pack("<II", gguf.U32, 32)
+    kv += _s("tokenizer.ggml.tokens") + struct.pack("<IIQ", gguf.ARR, gguf.STR, 2) + _s("hello") + _s("world")
+    ti = _s("output_norm.weight") + struct.pack("<IQIQ", 1, 4096, gguf.T_F32, 0)
+    ti += _s("token_embd.weight") + struct.pack("<IQQIQ", 2, 32000, 4096, gguf.T_F32, 16384)
+    data = _gguf(3, 2, kv, 3, ti)
+    g = gguf.parse(data)
+    assert g.metadata["general.architecture"].value == "llama"
+    assert g.metadata["llama.block_count"].value == 32
+    assert g.metadata["tokenizer.ggml.tokens"].value == ["hello", "world"]
+    t = g.find_tensor("output_norm.weight")
+    assert t.type == gguf.T_F32 and t.element_count == 4096 and t.offset == 0
+    t2 = g.find_tensor("token_embd.weight")
+    assert t2.dims == [32000, 4096]
+    assert g.find_tensor("nonexistent") is None
+    assert g.data_start == (len(data) + 31) // 32 * 32
+    h, _, keep = _oracle_parse(data)
+    assert h
+    assert O.lib().or_gguf_find_tensor(h, b"token_embd.weight") == 1
+    assert O.lib().or_gguf_find_tensor(h, b"nonexistent") == -1
+    assert O.lib().or_gguf_data_start(h) == g.data_start
+    O.lib().or_gguf_free(h)
