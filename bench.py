@@ -134,13 +134,25 @@ def barrier(ws: int):
         dist.barrier()
 
 
-def model_image(ws: int, rank: int) -> np.ndarray:
+def spec(args):
+    """The benchmark model; --layers keeps every matrix shape but fewer blocks
+    (used only to size profiler captures)."""
+    import dataclasses
+
+    from dotnetfoundryllm_b200 import ggufgen
+    s = ggufgen.SPECS[CONFIG]
+    if args.layers:
+        s = dataclasses.replace(s, n_layers=args.layers)
+    return s
+
+
+def model_image(args, ws: int, rank: int) -> np.ndarray:
     from dotnetfoundryllm_b200 import ggufgen
     if ws == 1:
-        return ggufgen.build_model(CONFIG)
+        return ggufgen.build_model(spec(args))
     path = Path(tempfile.gettempdir()) / f"foundry_bench_{CONFIG}_{os.environ.get('MASTER_PORT', '0')}.gguf"
     if rank == 0:
-        ggufgen.build_model(CONFIG, str(path))
+        ggufgen.build_model(spec(args), str(path))
     barrier(ws)
     img = np.fromfile(path, dtype=np.uint8)
     barrier(ws)
@@ -180,13 +192,13 @@ def run_reference(args, ws, rank):
     if rank != 0:
         return
     from dotnetfoundryllm_b200 import ggufgen
-    img = ggufgen.build_model(CONFIG)
+    img = ggufgen.build_model(spec(args))
     from oracle import oracle as O
     threads = os.cpu_count() or 1
     O.set_threads(threads)
     m = O.Model(img, max_layers=2)
     s = O.Session(m)
-    pos = PROMPT - 1
+    pos = args.prompt - 1
     times = []
     for i in range(args.warmup + args.steps):
         s.fake_length(pos + i)
@@ -207,8 +219,8 @@ def run_reference(args, ws, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF)",
-        "config": {"workload": f"{CONFIG} Q4_K/Q6_K bs=1 decode after a {PROMPT}-token prompt",
-                   "model": CONFIG, "global_batch": 1, "seq_len": PROMPT},
+        "config": {"workload": f"{CONFIG} Q4_K/Q6_K bs=1 decode after a {args.prompt}-token prompt",
+                   "model": CONFIG, "global_batch": 1, "seq_len": args.prompt},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -216,19 +228,19 @@ def run_reference(args, ws, rank):
 
 def run_ours(args, ws, rank, local):
     from dotnetfoundryllm_b200 import loader, runtime
-    img = model_image(ws, rank)
-    max_ctx = PROMPT + args.warmup + 2 * args.steps + 64
+    img = model_image(args, ws, rank)
+    max_ctx = args.prompt + args.warmup + 2 * args.steps + 64
     model = loader.load(img, device=local, max_ctx=max_ctx)
     fwd = runtime.CudaForwardPass(model, max_ctx=max_ctx)
     from dotnetfoundryllm_b200 import ggufgen
-    prompt = ggufgen.prompt_ids(PROMPT, model.desc.vocab, 0)
+    prompt = ggufgen.prompt_ids(args.prompt, model.desc.vocab, 0)
     kv = object()
     # prefill the way LlamaLanguageModel does: one Forward per prompt token but the last
     t0 = time.perf_counter()
-    for i in range(PROMPT - 1):
+    for i in range(args.prompt - 1):
         fwd.forward(int(prompt[i]), i, kv, want_logits=False)
     prefill_s = time.perf_counter() - t0
-    pos = PROMPT - 1
+    pos = args.prompt - 1
     tok = int(prompt[-1])
     # warm-up (device-resident greedy loop)
     if args.warmup:
@@ -254,7 +266,7 @@ def run_ours(args, ws, rank, local):
     e2e_s = time.perf_counter() - t0
     e2e_max = allreduce_max(e2e_s, ws)
     # roofline of the dequant-matvec kernel class (eager launches, events per kernel)
-    profs = [fwd.profile_step(int(prompt[i % PROMPT]), pos + args.steps + i) for i in range(3)]
+    profs = [fwd.profile_step(int(prompt[i % args.prompt]), pos + args.steps + i) for i in range(3)]
     mv_ms = min(p["ms"]["matvec"] for p in profs)
     mv_bytes = profs[0]["bytes"]["matvec"]
     peaks = load_peaks()
@@ -269,7 +281,7 @@ def run_ours(args, ws, rank, local):
     value = ws * args.steps / (ms_max / 1e3)
     result = None
     if rank == 0:
-        cpu = cpu_sample(img, pos_timed)
+        cpu = {"tok_s": None, "threads": 0} if args.no_cpu_baseline else cpu_sample(img, pos_timed)
         traffic = None
         tf = ROOT / "profiles" / "traffic.json"
         if tf.exists():
@@ -279,8 +291,8 @@ def run_ours(args, ws, rank, local):
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF, N(0,0.02) weights)",
             "config": {"workload": f"{CONFIG} Q4_K/Q6_K bs=1 greedy decode, positions {pos_timed}.."
-                                   f"{pos_timed + args.steps - 1} after a {PROMPT}-token prompt",
-                       "model": CONFIG, "global_batch": ws, "seq_len": PROMPT,
+                                   f"{pos_timed + args.steps - 1} after a {args.prompt}-token prompt",
+                       "model": CONFIG, "global_batch": ws, "seq_len": args.prompt,
                        "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
                        "l2": "inputs larger than L2 (4.9 GB of weights per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -309,6 +321,9 @@ def main():
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (default: the BASELINE 2048)")
+    ap.add_argument("--layers", type=int, default=0, help="profiling only: fewer blocks, same matrix shapes")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="profiling only: skip the CPU sample")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -98,6 +98,7 @@ INTERNAL_API = [
     ("fl_layout_for", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.POINTER(FlMatrixLayout)]),
     ("fl_repack", C.c_int, [C.POINTER(FlMatrixLayout), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]),
     ("fl_emulate_matvec", C.c_int, [C.POINTER(FlMatrixLayout), C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("fl_session_phase_ms", C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
 ]
 
 GEN_API = [

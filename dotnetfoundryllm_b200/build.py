@@ -24,9 +24,9 @@ CSRC = PKG / "csrc"
 LIB = PKG / "_lib"
 OBJ = PKG / "_build"
 
-CUDA_SOURCES = ["fl_matvec.cu", "fl_misc.cu", "fl_runtime.cu"]
+CUDA_SOURCES = ["fl_matvec.cu", "fl_misc.cu", "fl_token.cu", "fl_runtime.cu"]
 HOST_SOURCES = ["fl_repack.cpp"]
-HEADERS = ["fl_layout.h", "fl_decode.h", "fl_device.cuh", "fl_kernels.h", "fl_repack.h"]
+HEADERS = ["fl_layout.h", "fl_decode.h", "fl_device.cuh", "fl_kernels.h", "fl_repack.h", "fl_mv_core.cuh", "fl_dequant.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -76,10 +76,15 @@ struct FlMvArgs {
 
 /* Dynamic shared memory of a matvec launch. */
 size_t fl_mv_smem_bytes(const FlMvArgs& a);
+/* Shared memory of a launch without its weight ring (x encoding, barriers,
+ * reduction slots) for k-blocks n_kb. */
+size_t fl_mv_fixed_smem_bytes(int n_kb);
 /* Opts the matvec kernels into large dynamic shared memory on the current
  * device (call before stream capture). */
 cudaError_t fl_mv_configure();
 cudaError_t fl_launch_matvec(const FlMvArgs& a, int grid, cudaStream_t st, bool pdl);
+/* Sizes the per-warp weight ring of a standalone launch (slot = largest unit). */
+void fl_mv_ring_config(FlMvArgs& a);
 
 /* Embedding row (bit-exact dequant of token_embd row `token`). */
 struct FlEmbedArgs {
@@ -91,7 +96,6 @@ struct FlEmbedArgs {
     int32_t zero_n;
     int* err;
 };
-cudaError_t fl_launch_embed(const FlEmbedArgs& a, cudaStream_t st, bool pdl);
 
 /* Split-K decode attention over the F32 KV cache. */
 struct FlAttnArgs {
@@ -107,18 +111,40 @@ struct FlAttnArgs {
     float scale, softcap;
     int* err;
 };
-cudaError_t fl_launch_attention(const FlAttnArgs& a, cudaStream_t st, bool pdl);
 
-/* Position bookkeeping of the device-resident decode loop: token <- argmax,
- * pos <- pos + 1, and the generated id appended to a device array. */
-struct FlAdvanceArgs {
+/* ── the persistent token kernel (fl_token.cu) ─────────────────────────── */
+#define FL_TK_WARPS 15
+
+enum { FL_PH_EMBED = 0, FL_PH_MATVEC = 1, FL_PH_ATTN = 2 };
+
+struct FlPhase {
+    int32_t kind;
+    int32_t pad;
+    FlMvArgs mv;
+    FlAttnArgs at;
+    FlEmbedArgs em;
+};
+
+struct FlTokenArgs {
+    const FlPhase* phases;       /* device array */
+    int32_t n_phases;
+    int32_t n_slots, slot_bytes; /* weight ring */
+    size_t scratch_bytes;        /* x encoding / attention scratch */
+    int32_t* bar;                /* grid barrier counter, zeroed before each launch */
+    int* err;
+    uint64_t* timestamps;        /* [n_phases + 1] globaltimer at each phase start, CTA 0 */
+    /* device-resident decode loop */
+    int32_t advance;
     int32_t* token;
     int32_t* pos;
-    const int32_t* argmax;
     int32_t* out_tokens;
     int32_t* step;
 };
-cudaError_t fl_launch_advance(const FlAdvanceArgs& a, cudaStream_t st, bool pdl);
+
+size_t fl_token_smem_bytes(int n_slots, int slot_bytes, size_t scratch_bytes);
+cudaError_t fl_token_configure(int* max_dyn_smem);
+cudaError_t fl_launch_token(const FlTokenArgs& ta, int grid, size_t smem, cudaStream_t st);
+const void* fl_token_kernel_ptr();
 
 /* Bit-exact block dequantization (fl_dequant). */
 cudaError_t fl_launch_dequant(int32_t ggml_type, const uint8_t* src, int64_t n_blocks, float* dst, cudaStream_t st);

@@ -1,13 +1,14 @@
 /*
  * fl_runtime.cu — the C ABI (include/foundry_cuda.h): device model, upload +
  * repack, per-request session with an HBM KV cache, and the token step as one
- * CUDA graph of programmatic-dependent launches.
+ * persistent cooperative kernel (fl_token.cu) replayed from a CUDA graph.
  *
  * Reference seam: LlamaLanguageModel takes a Func<IForwardPass> factory and an
  * IDisposable model resource (src/DotNetFoundryLLM.Inference/
  * LlamaLanguageModel.cs:48-80); fl_model is that resource and fl_session +
  * fl_forward the IForwardPass (IForwardPass.cs:8-15).
  */
+#include <algorithm>
 #include <cmath>
 #include <climits>
 #include <cstdarg>
@@ -100,6 +101,16 @@ struct fl_session {
     cudaGraphExec_t graph = nullptr;
     int launches = 0;
     int attn_split = 1;
+    /* the token step: phase list + persistent kernel configuration */
+    FlPhase* d_phases = nullptr;
+    int n_phases = 0;
+    std::vector<int> phase_cls;
+    std::vector<double> phase_bytes;
+    int32_t* bar = nullptr;
+    uint64_t* timestamps = nullptr;
+    FlTokenArgs ta;
+    size_t tk_smem = 0;
+    int tk_grid = 0;
     std::vector<void*> allocs;
 };
 
@@ -382,16 +393,7 @@ extern "C" int fl_model_weight_bytes(fl_model* m, double* bytes)
     return FL_OK;
 }
 
-/* ── session ────────────────────────────────────────────────────────────── */
-static void ring_config(FlMvArgs& a)
-{
-    int maxu = 0;
-    for (int i = 0; i < a.n_seg; i++) maxu = a.seg[i].unit_bytes > maxu ? a.seg[i].unit_bytes : maxu;
-    a.slot_bytes = (maxu + 127) & ~127;
-    int n = (12 * 1024) / a.slot_bytes;
-    a.n_slots = n < 2 ? 2 : (n > 4 ? 4 : n);
-}
-
+/* ── session: the token step as a phase list for the persistent kernel ─── */
 static void set_seg(FlMvArgs& a, int i, const DevMatrix& dm, const float* bias, int tile0)
 {
     a.seg[i].w = dm.d;
@@ -415,57 +417,55 @@ static FlMvArgs base_args(fl_session* s, const DevMatrix& dm, int K)
     a.K = K;
     a.rows_total = dm.L.rows;
     a.err = s ? s->state + ST_ERR : nullptr;
-    ring_config(a);
     return a;
 }
 
-static int grid_for(const fl_model* m, const FlMvArgs& a) { return a.n_tiles < m->sm_count ? a.n_tiles : m->sm_count; }
-
 enum { CLS_MV = 0, CLS_ATTN = 1, CLS_OTHER = 2 };
-
-struct Recorder {
-    std::vector<cudaEvent_t>* ev = nullptr;
-    std::vector<int>* cls = nullptr;
-    std::vector<double>* bytes = nullptr;
-    int launches = 0;
-    void mark(cudaStream_t st, int c, double b)
-    {
-        launches++;
-        if (!ev) return;
-        cudaEvent_t e;
-        cudaEventCreate(&e);
-        cudaEventRecord(e, st);
-        ev->push_back(e);
-        cls->push_back(c);
-        bytes->push_back(b);
-    }
-};
 
 static double mat_bytes(const DevMatrix& dm) { return (double)dm.L.gguf_bytes; }
 
-/* Enqueues one token step (LlamaForwardPass.Forward and the per-arch copies). */
-static int record_step(fl_session* s, bool pdl, Recorder& rec)
+struct PhaseList {
+    std::vector<FlPhase> ph;
+    std::vector<int> cls;
+    std::vector<double> bytes;
+    void add_mv(const FlMvArgs& a, double b)
+    {
+        FlPhase p;
+        memset(&p, 0, sizeof p);
+        p.kind = FL_PH_MATVEC;
+        p.mv = a;
+        ph.push_back(p);
+        cls.push_back(CLS_MV);
+        bytes.push_back(b);
+    }
+};
+
+/* The ops of LlamaForwardPass.Forward (LlamaForwardPass.cs:82-130; Gemma2
+ * post-norms Gemma2ForwardPass.cs:78-104; Qwen2 biases Qwen2ForwardPass.cs:
+ * 83-85; Mistral window MistralForwardPass.cs:196) as phases. */
+static void build_phases(fl_session* s, PhaseList& P)
 {
     fl_model* m = s->m;
     const fl_model_desc& d = m->d;
     const int h = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim;
     const bool gemma = d.arch == FL_ARCH_GEMMA2;
-    cudaStream_t st = s->st;
-    int32_t* token = s->state + ST_TOKEN;
     int32_t* pos = s->state + ST_POS;
 
-    FlEmbedArgs ea;
-    ea.raw = m->emb_raw;
-    ea.ggml_type = m->emb_type;
-    ea.hidden = h;
-    ea.vocab = d.vocab;
-    ea.token = token;
-    ea.x = s->xa;
-    ea.zero_buf = s->absmax;
-    ea.zero_n = s->n_absmax;
-    ea.err = s->state + ST_ERR;
-    CK(fl_launch_embed(ea, st, pdl));
-    rec.mark(st, CLS_OTHER, (double)m->emb_bytes / d.vocab);
+    FlPhase e;
+    memset(&e, 0, sizeof e);
+    e.kind = FL_PH_EMBED;
+    e.em.raw = m->emb_raw;
+    e.em.ggml_type = m->emb_type;
+    e.em.hidden = h;
+    e.em.vocab = d.vocab;
+    e.em.token = s->state + ST_TOKEN;
+    e.em.x = s->xa;
+    e.em.zero_buf = s->absmax;
+    e.em.zero_n = s->n_absmax;
+    e.em.err = s->state + ST_ERR;
+    P.ph.push_back(e);
+    P.cls.push_back(CLS_OTHER);
+    P.bytes.push_back((double)m->emb_bytes / d.vocab);
 
     float* x = s->xa;
     float* x_other = s->xb;
@@ -482,7 +482,6 @@ static int record_step(fl_session* s, bool pdl, Recorder& rec)
         set_seg(a, 2, L.wv, L.bv, L.wq.L.n_tiles + L.wk.L.n_tiles);
         a.n_seg = 3;
         a.n_tiles = L.wq.L.n_tiles + L.wk.L.n_tiles + L.wv.L.n_tiles;
-        ring_config(a);
         if (!gemma) {
             a.in_mode = FL_IN_RMSNORM;
             a.x = x;
@@ -512,31 +511,33 @@ static int record_step(fl_session* s, bool pdl, Recorder& rec)
         a.q_out = s->q;
         a.k_cache = kc;
         a.v_cache = vc;
-        CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
-        rec.mark(st, CLS_MV, mat_bytes(L.wq) + mat_bytes(L.wk) + mat_bytes(L.wv) + 4.0 * h);
+        P.add_mv(a, mat_bytes(L.wq) + mat_bytes(L.wk) + mat_bytes(L.wv) + 4.0 * h);
 
-        FlAttnArgs at;
-        at.q = s->q;
-        at.k_cache = kc;
-        at.v_cache = vc;
-        at.out = s->att;
-        at.out_absmax = amax_att;
-        at.part = s->attn_part;
-        at.counter = s->attn_counter;
-        at.pos = pos;
-        at.n_heads = d.n_heads;
-        at.n_kv = d.n_kv_heads;
-        at.head_dim = d.head_dim;
-        at.n_split = s->attn_split;
+        FlPhase at;
+        memset(&at, 0, sizeof at);
+        at.kind = FL_PH_ATTN;
+        at.at.q = s->q;
+        at.at.k_cache = kc;
+        at.at.v_cache = vc;
+        at.at.out = s->att;
+        at.at.out_absmax = amax_att;
+        at.at.part = s->attn_part;
+        at.at.counter = s->attn_counter;
+        at.at.pos = pos;
+        at.at.n_heads = d.n_heads;
+        at.at.n_kv = d.n_kv_heads;
+        at.at.head_dim = d.head_dim;
+        at.at.n_split = s->attn_split;
         int window = INT_MAX;
         if (d.arch == FL_ARCH_MISTRAL) window = d.sliding_window;
-        if (gemma && (l % 2) == 0) window = d.sliding_window;
-        at.window = window > 0 ? window : INT_MAX;
-        at.scale = d.attn_scale;
-        at.softcap = gemma ? d.attn_softcap : 0.0f;
-        at.err = s->state + ST_ERR;
-        CK(fl_launch_attention(at, st, pdl));
-        rec.mark(st, CLS_ATTN, 0.0);
+        if (gemma && (l % 2) == 0) window = d.sliding_window; /* Gemma2ForwardPass.cs:87 */
+        at.at.window = window > 0 ? window : INT_MAX;
+        at.at.scale = d.attn_scale;
+        at.at.softcap = gemma ? d.attn_softcap : 0.0f;
+        at.at.err = s->state + ST_ERR;
+        P.ph.push_back(at);
+        P.cls.push_back(CLS_ATTN);
+        P.bytes.push_back(0.0);
 
         /* output projection + residual (Gemma: post-attention norm first) */
         a = base_args(s, L.wo, qd);
@@ -545,8 +546,7 @@ static int record_step(fl_session* s, bool pdl, Recorder& rec)
         a.absmax = amax_att;
         a.epi = gemma ? FL_EPI_STORE : FL_EPI_RESID;
         a.y = gemma ? s->o : x;
-        CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
-        rec.mark(st, CLS_MV, mat_bytes(L.wo));
+        P.add_mv(a, mat_bytes(L.wo));
 
         /* FFN: norm → gate/up → SiLU|GELU(gate)*up */
         a = base_args(s, L.gate_up, h);
@@ -570,8 +570,7 @@ static int record_step(fl_session* s, bool pdl, Recorder& rec)
         a.act_gelu = gemma ? 1 : 0;
         a.act_out = s->act;
         a.act_absmax = amax_act;
-        CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
-        rec.mark(st, CLS_MV, mat_bytes(L.gate_up) + 4.0 * h);
+        P.add_mv(a, mat_bytes(L.gate_up) + 4.0 * h);
 
         a = base_args(s, L.down, d.ffn);
         a.in_mode = FL_IN_PLAIN;
@@ -579,8 +578,7 @@ static int record_step(fl_session* s, bool pdl, Recorder& rec)
         a.absmax = amax_act;
         a.epi = gemma ? FL_EPI_STORE : FL_EPI_RESID;
         a.y = gemma ? s->o : x;
-        CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
-        rec.mark(st, CLS_MV, mat_bytes(L.down));
+        P.add_mv(a, mat_bytes(L.down));
     }
     /* final norm + LM head + greedy argmax */
     FlMvArgs a = base_args(s, m->output, h);
@@ -604,17 +602,14 @@ static int record_step(fl_session* s, bool pdl, Recorder& rec)
     a.cta_best = s->cta_best;
     a.counter = s->state + ST_HEADCNT;
     a.argmax_out = s->state + ST_ARGMAX;
-    CK(fl_launch_matvec(a, grid_for(m, a), st, pdl));
-    rec.mark(st, CLS_MV, mat_bytes(m->output) + 4.0 * h);
+    P.add_mv(a, mat_bytes(m->output) + 4.0 * h);
+}
 
-    FlAdvanceArgs ad;
-    ad.token = token;
-    ad.pos = pos;
-    ad.argmax = s->state + ST_ARGMAX;
-    ad.out_tokens = s->out_tokens;
-    ad.step = s->state + ST_STEP;
-    CK(fl_launch_advance(ad, st, pdl));
-    rec.mark(st, CLS_OTHER, 0.0);
+/* One token step: zero the grid-barrier counter, then the persistent kernel. */
+static int enqueue_step(fl_session* s)
+{
+    CK(cudaMemsetAsync(s->bar, 0, 4, s->st));
+    CK(fl_launch_token(s->ta, s->tk_grid, s->tk_smem, s->st));
     return FL_OK;
 }
 
@@ -630,19 +625,21 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     const fl_model_desc& d = m->d;
     if (max_ctx <= 0 || max_ctx > d.max_ctx) max_ctx = d.max_ctx;
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    int max_dyn = 0;
+    if (fl_token_configure(&max_dyn) != cudaSuccess) return fail(FL_ERR_CUDA, "token kernel configuration failed");
     fl_session* s = new fl_session();
     s->m = m;
     s->max_ctx = max_ctx;
     const int h = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim, grp = d.n_heads / d.n_kv_heads;
-    /* splits: ~2 CTAs per SM over all kv heads */
-    int split = (2 * m->sm_count + d.n_kv_heads - 1) / d.n_kv_heads;
+    const int G = m->sm_count;
+    /* attention items (kv head, split): about one per SM */
+    int split = (G + d.n_kv_heads - 1) / d.n_kv_heads;
     if (split > max_ctx) split = max_ctx;
     if (split < 1) split = 1;
     s->attn_split = split;
     s->n_absmax = 2 * d.n_layers;
     int rc = FL_OK;
     size_t kv_bytes = (size_t)d.n_layers * max_ctx * kvd * 4;
-    int headgrid = m->output.L.n_tiles < m->sm_count ? m->output.L.n_tiles : m->sm_count;
 #define AL(p, b) if (!rc) rc = dalloc(s->allocs, &(p), (b))
     AL(s->xa, (size_t)h * 4);
     AL(s->xb, (size_t)h * 4);
@@ -657,21 +654,77 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     AL(s->state, (size_t)ST_N * 4);
     AL(s->attn_counter, (size_t)d.n_kv_heads * 4);
     AL(s->attn_part, (size_t)d.n_kv_heads * split * grp * (d.head_dim + 2) * 4);
-    AL(s->cta_best, (size_t)headgrid * 8 + 8);
+    AL(s->cta_best, (size_t)G * 8 + 8);
     AL(s->out_tokens, (size_t)max_ctx * 4 + 4);
     s->topk_scratch_bytes = fl_topk_scratch_bytes(d.vocab, 0);
     AL(s->topk_scratch, s->topk_scratch_bytes);
     AL(s->topk_ids, (size_t)d.vocab * 4);
     AL(s->topk_vals, (size_t)d.vocab * 4);
+    AL(s->bar, 16);
 #undef AL
     if (rc) {
         fl_session_destroy(s);
         return rc;
     }
-    if (cudaMallocHost(&s->h_state, ST_N * 4) != cudaSuccess || cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
+    if (cudaMallocHost(&s->h_state, ST_N * 4) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) {
         fl_session_destroy(s);
         return fail(FL_ERR_CUDA, "stream/pinned allocation failed");
     }
+    /* phase list */
+    PhaseList P;
+    build_phases(s, P);
+    s->n_phases = (int)P.ph.size();
+    s->phase_cls = P.cls;
+    s->phase_bytes = P.bytes;
+    rc = dalloc(s->allocs, &s->d_phases, P.ph.size() * sizeof(FlPhase));
+    if (!rc) rc = dalloc(s->allocs, &s->timestamps, (P.ph.size() + 1) * 8);
+    if (rc) {
+        fl_session_destroy(s);
+        return rc;
+    }
+    /* shared memory: weight ring of the largest unit + x-encoding / attention scratch */
+    int slot = 0, max_kb = 0;
+    for (const FlPhase& p : P.ph)
+        if (p.kind == FL_PH_MATVEC) {
+            for (int i = 0; i < p.mv.n_seg; i++) slot = std::max(slot, p.mv.seg[i].unit_bytes);
+            max_kb = std::max(max_kb, p.mv.n_kb);
+        }
+    slot = (slot + 127) & ~127;
+    const size_t xenc = (size_t)max_kb * 8 * (FL_XENC_LIMB_BYTES + 32 + 8);
+    const size_t attn = (size_t)(grp * d.head_dim + FL_TK_WARPS * grp * 2 + FL_TK_WARPS * grp * d.head_dim) * 4;
+    const size_t scratch = std::max(xenc, attn);
+    int n_slots = 2;
+    while (fl_token_smem_bytes(n_slots + 1, slot, scratch) <= (size_t)max_dyn) n_slots++;
+    if (fl_token_smem_bytes(n_slots, slot, scratch) > (size_t)max_dyn) {
+        fl_session_destroy(s);
+        return fail(FL_ERR_UNSUPPORTED, "shared memory budget exceeded (x encoding %zu B)", xenc);
+    }
+    FlTokenArgs& ta = s->ta;
+    memset(&ta, 0, sizeof ta);
+    ta.phases = s->d_phases;
+    ta.n_phases = s->n_phases;
+    ta.n_slots = n_slots;
+    ta.slot_bytes = slot;
+    ta.scratch_bytes = scratch;
+    ta.bar = s->bar;
+    ta.err = s->state + ST_ERR;
+    ta.timestamps = s->timestamps;
+    ta.advance = 1;
+    ta.token = s->state + ST_TOKEN;
+    ta.pos = s->state + ST_POS;
+    ta.out_tokens = s->out_tokens;
+    ta.step = s->state + ST_STEP;
+    s->tk_smem = fl_token_smem_bytes(n_slots, slot, scratch);
+    s->tk_grid = G;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fl_token_kernel_ptr(), 32 * (FL_TK_WARPS + 1),
+                                                      s->tk_smem) != cudaSuccess ||
+        per_sm < 1) {
+        fl_session_destroy(s);
+        return fail(FL_ERR_UNSUPPORTED, "the token kernel does not fit one CTA per SM");
+    }
+    cudaMemcpyAsync(s->d_phases, P.ph.data(), P.ph.size() * sizeof(FlPhase), cudaMemcpyHostToDevice, s->st);
     cudaMemsetAsync(s->state, 0, ST_N * 4, s->st);
     cudaMemsetAsync(s->attn_counter, 0, (size_t)d.n_kv_heads * 4, s->st);
     cudaMemsetAsync(s->kc, 0, kv_bytes, s->st);
@@ -680,18 +733,13 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
         fl_session_destroy(s);
         return fail(FL_ERR_CUDA, "session init failed");
     }
-    if (fl_mv_configure() != cudaSuccess) {
-        fl_session_destroy(s);
-        return fail(FL_ERR_CUDA, "matvec kernel configuration failed");
-    }
     /* capture the token step once */
-    Recorder rec;
     cudaGraph_t g = nullptr;
     if (cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
         fl_session_destroy(s);
         return fail(FL_ERR_CUDA, "graph capture failed to start");
     }
-    rc = record_step(s, true, rec);
+    rc = enqueue_step(s);
     cudaError_t ce = cudaStreamEndCapture(s->st, &g);
     if (rc || ce != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
@@ -704,7 +752,7 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
         fl_session_destroy(s);
         return fail(FL_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
     }
-    s->launches = rec.launches;
+    s->launches = 1;
     *out = s;
     return FL_OK;
 }
@@ -743,7 +791,7 @@ static int check_device_err(fl_session* s)
     if (err == 0) return FL_OK;
     int32_t zero = 0;
     cudaMemcpy(s->state + ST_ERR, &zero, 4, cudaMemcpyHostToDevice);
-    if (err == 1) return fail(FL_ERR_TIMEOUT, "a bounded device wait expired (bulk copy did not complete)");
+    if (err == 1) return fail(FL_ERR_TIMEOUT, "a bounded device wait expired");
     return fail(FL_ERR_ARG, "device reported error %d", err);
 }
 
@@ -826,6 +874,8 @@ extern "C" int fl_time_decode(fl_session* s, int32_t token, int32_t start_pos, i
     return run_steps(s, token, start_pos, n_steps, ms);
 }
 
+/* One step, with the phase boundaries read from the globaltimer stamps the
+ * kernel records (CTA 0, after each grid barrier). */
 extern "C" int fl_profile_step(fl_session* s, int32_t token, int32_t position, double* ms, double* bytes,
                                int32_t* launches)
 {
@@ -836,35 +886,24 @@ extern "C" int fl_profile_step(fl_session* s, int32_t token, int32_t position, d
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
     int rc = set_state(s, token, position);
     if (rc) return rc;
-    std::vector<cudaEvent_t> ev;
-    std::vector<int> cls;
-    std::vector<double> by;
-    Recorder rec;
-    rec.ev = &ev;
-    rec.cls = &cls;
-    rec.bytes = &by;
-    cudaEvent_t e0;
-    CK(cudaEventCreate(&e0));
-    CK(cudaEventRecord(e0, s->st));
-    rc = record_step(s, false, rec);
-    if (rc) return rc;
+    CK(cudaGraphLaunch(s->graph, s->st));
     CK(cudaStreamSynchronize(s->st));
-    for (int i = 0; i < FL_PROF_N; i++) { ms[i] = 0; bytes[i] = 0; }
-    cudaEvent_t prev = e0;
-    for (size_t i = 0; i < ev.size(); i++) {
-        float t = 0;
-        cudaEventElapsedTime(&t, prev, ev[i]);
-        ms[cls[i]] += t;
-        bytes[cls[i]] += by[i];
-        ms[FL_PROF_STEP] += t;
-        bytes[FL_PROF_STEP] += by[i];
-        prev = ev[i];
-    }
-    for (auto e : ev) cudaEventDestroy(e);
-    cudaEventDestroy(e0);
-    if (launches) *launches = (int32_t)ev.size();
     rc = check_device_err(s);
     if (rc) return rc;
+    std::vector<uint64_t> ts((size_t)s->n_phases + 1);
+    CK(cudaMemcpy(ts.data(), s->timestamps, ts.size() * 8, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < FL_PROF_N; i++) {
+        ms[i] = 0;
+        bytes[i] = 0;
+    }
+    for (int p = 0; p < s->n_phases; p++) {
+        const double t = (double)(ts[(size_t)p + 1] - ts[(size_t)p]) * 1e-6;
+        ms[s->phase_cls[(size_t)p]] += t;
+        bytes[s->phase_cls[(size_t)p]] += s->phase_bytes[(size_t)p];
+        ms[FL_PROF_STEP] += t;
+        bytes[FL_PROF_STEP] += s->phase_bytes[(size_t)p];
+    }
+    if (launches) *launches = s->launches;
     s->cur_len = position + 1;
     return FL_OK;
 }
@@ -946,6 +985,7 @@ extern "C" int fl_matvec(int32_t type, const void* w, uint64_t nbytes, int32_t r
         if (e == cudaSuccess) e = cudaMemset(derr, 0, 16);
         if (e == cudaSuccess) {
             FlMvArgs a = base_args(nullptr, dm, cols);
+            fl_mv_ring_config(a);
             a.err = derr;
             a.in_mode = FL_IN_PLAIN;
             a.x = dx;
@@ -964,5 +1004,17 @@ extern "C" int fl_matvec(int32_t type, const void* w, uint64_t nbytes, int32_t r
     for (void* p : al) cudaFree(p);
     if (rc) return rc;
     if (e != cudaSuccess) return fail(FL_ERR_CUDA, "fl_matvec: %s", cudaGetErrorString(e));
+    return FL_OK;
+}
+
+/* Per-phase device milliseconds of the most recent step (diagnostics; phase
+ * order: embed, then per layer qkv, attention, wo, gate/up, down, then head). */
+extern "C" int fl_session_phase_ms(fl_session* s, double* out, int32_t cap, int32_t* n)
+{
+    if (!s || !out || !n) return fail(FL_ERR_ARG, "null argument");
+    std::vector<uint64_t> ts((size_t)s->n_phases + 1);
+    CK(cudaMemcpy(ts.data(), s->timestamps, ts.size() * 8, cudaMemcpyDeviceToHost));
+    *n = s->n_phases;
+    for (int p = 0; p < s->n_phases && p < cap; p++) out[p] = (double)(ts[(size_t)p + 1] - ts[(size_t)p]) * 1e-6;
     return FL_OK;
 }
