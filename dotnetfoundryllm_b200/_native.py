@@ -99,6 +99,8 @@ INTERNAL_API = [
     ("fl_repack", C.c_int, [C.POINTER(FlMatrixLayout), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]),
     ("fl_emulate_matvec", C.c_int, [C.POINTER(FlMatrixLayout), C.c_void_p, C.c_void_p, C.c_void_p]),
     ("fl_session_phase_ms", C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
+    ("fl_session_cta_done_ms", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.POINTER(C.c_int32)]),
+    ("fl_session_detail", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
 ]
 
 GEN_API = [

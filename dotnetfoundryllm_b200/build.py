@@ -24,9 +24,11 @@ CSRC = PKG / "csrc"
 LIB = PKG / "_lib"
 OBJ = PKG / "_build"
 
-CUDA_SOURCES = ["fl_matvec.cu", "fl_misc.cu", "fl_token.cu", "fl_runtime.cu"]
+CUDA_SOURCES = ["fl_matvec.cu", "fl_misc.cu", "fl_token.cu", "fl_token_hd64.cu", "fl_token_hd128.cu",
+                "fl_token_hd256.cu", "fl_runtime.cu"]
 HOST_SOURCES = ["fl_repack.cpp"]
-HEADERS = ["fl_layout.h", "fl_decode.h", "fl_device.cuh", "fl_kernels.h", "fl_repack.h", "fl_mv_core.cuh", "fl_dequant.cuh"]
+HEADERS = ["fl_layout.h", "fl_decode.h", "fl_device.cuh", "fl_kernels.h", "fl_repack.h", "fl_mv_core.cuh", "fl_dequant.cuh",
+           "fl_token.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -51,6 +51,27 @@ __device__ __forceinline__ uint64_t fl_globaltimer()
 
 /* Bounded wait on an mbarrier phase: gives up after ~2 s (or 2^26 polls),
  * records FL_DEV_ERR_TIMEOUT in *err and returns false.  Never traps. */
+/* Non-blocking test of a phase's completion. */
+__device__ __forceinline__ bool fl_mbar_test(uint64_t* bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        " .reg .pred p;\n"
+        " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(fl_smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ void fl_mbar_arrive(uint64_t* bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fl_smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool fl_mbar_wait(uint64_t* bar, uint32_t parity, int* err)
 {
     if (fl_mbar_try_wait(bar, parity)) return true;
@@ -74,6 +95,12 @@ __device__ __forceinline__ void fl_bulk_g2s(void* sdst, const void* gsrc, uint32
         : "memory");
 }
 
+/* Asks L2 to fetch [p, p + bytes) (16-byte aligned, size a multiple of 16). */
+__device__ __forceinline__ void fl_prefetch_l2(const void* p, uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 /* Orders this thread's earlier generic-proxy shared accesses before later
  * async-proxy (bulk copy) writes to the same shared memory. */
 __device__ __forceinline__ void fl_fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -87,13 +114,13 @@ template <bool SIGNED_A>
 __device__ __forceinline__ void fl_mma_i8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
 {
     if constexpr (SIGNED_A) {
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
             "{%10,%10,%10,%10};\n"
             : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
     } else {
-        asm volatile(
+        asm(
             "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
             "{%10,%10,%10,%10};\n"
             : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])

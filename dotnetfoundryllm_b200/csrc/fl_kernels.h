@@ -113,7 +113,8 @@ struct FlAttnArgs {
 };
 
 /* ── the persistent token kernel (fl_token.cu) ─────────────────────────── */
-#define FL_TK_WARPS 15
+#define FL_TK_WARPS 16
+#define FL_TK_MAX_TILES 256      /* 16-row tiles of one matvec phase per CTA */
 
 enum { FL_PH_EMBED = 0, FL_PH_MATVEC = 1, FL_PH_ATTN = 2 };
 
@@ -133,6 +134,9 @@ struct FlTokenArgs {
     int32_t* bar;                /* grid barrier counter, zeroed before each launch */
     int* err;
     uint64_t* timestamps;        /* [n_phases + 1] globaltimer at each phase start, CTA 0 */
+    uint64_t* cta_done;          /* [n_phases][grid] globaltimer when each CTA finished the phase, or NULL */
+    uint64_t* detail;            /* CTA 0, or NULL: [n_phases][warps][4] (units done: globaltimer, cycles
+                                    waiting for weights, waits, units) then [n_phases] prologue done */
     /* device-resident decode loop */
     int32_t advance;
     int32_t* token;
@@ -141,10 +145,13 @@ struct FlTokenArgs {
     int32_t* step;
 };
 
+/* The instance for (head_dim, query heads per kv head), or NULL when none is
+ * built (head_dim 64/128/256, group <= 8; <= 4 for head_dim 256). */
+const void* fl_token_kernel_ptr(int head_dim, int group);
 size_t fl_token_smem_bytes(int n_slots, int slot_bytes, size_t scratch_bytes);
-cudaError_t fl_token_configure(int* max_dyn_smem);
-cudaError_t fl_launch_token(const FlTokenArgs& ta, int grid, size_t smem, cudaStream_t st);
-const void* fl_token_kernel_ptr();
+/* Opts the instance into the largest dynamic shared memory (before capture). */
+cudaError_t fl_token_configure(const void* kernel, int* max_dyn_smem);
+cudaError_t fl_launch_token(const void* kernel, const FlTokenArgs& ta, int grid, size_t smem, cudaStream_t st);
 
 /* Bit-exact block dequantization (fl_dequant). */
 cudaError_t fl_launch_dequant(int32_t ggml_type, const uint8_t* src, int64_t n_blocks, float* dst, cudaStream_t st);

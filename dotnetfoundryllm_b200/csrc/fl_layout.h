@@ -91,11 +91,17 @@ enum fl_fmt {
 #define FL_Q8K_QS 64        /* 4096 B as Q8_0 */
 #define FL_Q8K_UNIT 4160
 
-/* x-vector encoding in shared memory: per chunk of 32 inputs, 3 int8 limbs
- * (x ≈ s*(X0 + X1/128 + X2/16384)) in B-fragment order [limb][t][8 B]
- * (4 bytes of even values then 4 bytes of odd values of word t), plus a float4
- * of half sums {sum(x[0:16]), 0, sum(x[16:32]), 0} indexed by t. */
+/* x-vector encoding in shared memory, per chunk of 32 inputs:
+ *  - 3 int8 limbs (x ≈ s*(X0 + X1/128 + X2/16384)) in B-fragment order
+ *    [limb][t][8 B] (4 bytes of even values then 4 bytes of odd values of word t);
+ *  - [t] short2 limb sums of lane t's two MMA output columns over its half
+ *    chunk: t even (S0, S1), t odd (S2, 0), half = t >> 1 (|S| <= 16*127);
+ *  - [half] float sums of the 16 inputs of each half. */
 #define FL_XENC_LIMB_BYTES 96
-#define FL_XENC_SX_BYTES 16
+#define FL_XENC_LSUM_BYTES 16
+#define FL_XENC_HSUM_BYTES 8
+#define FL_XENC_CHUNK_BYTES (FL_XENC_LIMB_BYTES + FL_XENC_LSUM_BYTES + FL_XENC_HSUM_BYTES)
+/* zero bytes read by lanes whose B column is not theirs (8 chunks apart) */
+#define FL_XENC_ZERO_BYTES (8 * FL_XENC_LIMB_BYTES)
 
 #endif

@@ -31,10 +31,10 @@ __host__ __device__ inline Layout smem_layout(int n_kb, int n_slots, int slot_by
     Layout L;
     const size_t nc = (size_t)n_kb * 8;
     L.xl = 0;                                   /* [chunk][limb 0..2][t][8 B] */
-    L.xs = L.xl + nc * FL_XENC_LIMB_BYTES;      /* [chunk][t] int2 limb sums of the lane's half */
-    L.xsum = L.xs + nc * 32;                    /* [chunk][half] float sums */
-    L.zero = L.xsum + nc * 8;                   /* 16 zero bytes */
-    L.ring = (L.zero + 16 + 127) & ~(size_t)127;
+    L.xs = L.xl + nc * FL_XENC_LIMB_BYTES;      /* [chunk][t] short2 limb sums of the lane's half */
+    L.xsum = L.xs + nc * FL_XENC_LSUM_BYTES;    /* [chunk][half] float sums */
+    L.zero = L.xsum + nc * FL_XENC_HSUM_BYTES;  /* zero B fragments */
+    L.ring = (L.zero + FL_XENC_ZERO_BYTES + 127) & ~(size_t)127;
     L.bars = L.ring + (size_t)FL_MV_WARPS * n_slots * slot_bytes;
     L.red = L.bars + (size_t)FL_MV_WARPS * n_slots * 8;
     L.cnt = L.red + (size_t)kRedSlots * FL_MV_WARPS * 16 * 4;
@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(FL_MV_THREADS, 1) fl_mv_kernel(const __grid_co
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     const Layout Ls = smem_layout(a.n_kb, a.n_slots, a.slot_bytes);
     uint8_t* xl = smem + Ls.xl;
-    int2* xs = reinterpret_cast<int2*>(smem + Ls.xs);
+    short2* xs = reinterpret_cast<short2*>(smem + Ls.xs);
     float* xsum = reinterpret_cast<float*>(smem + Ls.xsum);
     uint8_t* zero = smem + Ls.zero;
     uint8_t* ring = smem + Ls.ring;
@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(FL_MV_THREADS, 1) fl_mv_kernel(const __grid_co
         cnt[tid] = 0;
         done[tid] = 0;
     }
-    if (tid < 16) zero[tid] = 0;
+    for (int i = tid; i < FL_XENC_ZERO_BYTES; i += FL_MV_THREADS) zero[i] = 0;
     fl_fence_mbar_init();
     __syncthreads();
 
@@ -126,8 +126,7 @@ __global__ void __launch_bounds__(FL_MV_THREADS, 1) fl_mv_kernel(const __grid_co
 
     const int limb = g & 3;
     const bool bval = (limb < 3) && ((g >> 2) == (t >> 1));
-    const uint8_t* bptr = bval ? xl + (limb * 4 + t) * 8 : zero;
-    const int bstride = bval ? FL_XENC_LIMB_BYTES : 0;
+    const uint8_t* bptr = xl + (limb * 4 + t) * 8;
     const float wlane = ((t & 1) ? (1.0f / 16384.0f) : 1.0f) * xscale;
 
     float best_v = 0.0f;
@@ -142,7 +141,8 @@ __global__ void __launch_bounds__(FL_MV_THREADS, 1) fl_mv_kernel(const __grid_co
             const int slot = j % a.n_slots;
             fl_mbar_wait(&wbar[slot], (uint32_t)((j / a.n_slots) & 1), a.err);
             const uint8_t* u = wring + (size_t)slot * a.slot_bytes;
-            process_any(sg.fmt, sg.expanded, u, warp + FL_MV_WARPS * kk, bptr, bstride, xs, xsum, lane, A);
+            process_any(sg.fmt, sg.expanded, u, warp + FL_MV_WARPS * kk,
+                        unit_bptr(bptr, bval, zero, warp + FL_MV_WARPS * kk), xs, xsum, lane, A);
             __syncwarp();
             if (lane == 0 && j + a.n_slots < total) {
                 fl_fence_proxy_async();

@@ -59,23 +59,21 @@ struct Prolog {
     }
 };
 
-/* Lane l encodes word (c = l>>2, t = l&3) of k-block kb: 8 input values into
- * 3 limbs (B-fragment order), the limb sums of its half-chunk and the float
- * half sums. */
-__device__ __forceinline__ void encode_kblock(const Prolog& P, int kb, float inv, int lane, uint8_t* xl, int2* xs,
+/* Lane l encodes word (c = l>>2, t = l&3) of k-block kb — the input values
+ * kb*256 + 8l .. kb*256 + 8l + 7, given in v — into 3 limbs (B-fragment
+ * order), the limb sums of its half-chunk and the float half sums. */
+__device__ __forceinline__ void encode_values(const float (&v)[8], int kb, float inv, int lane, uint8_t* xl, short2* xs,
                                               float* xsum)
 {
     const int c = lane >> 2, t = lane & 3;
     const int cg = kb * 8 + c;
-    const int base = cg * 32 + t * 8;
     uint32_t lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
     int sl[3] = {0, 0, 0};
     float hs = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
-        const float v = P.value(base + i);
-        hs += v;
-        float y = __fmul_rn(v, inv);
+        hs += v[i];
+        float y = __fmul_rn(v[i], inv);
 #pragma unroll
         for (int l = 0; l < 3; l++) {
             const float tq = __fadd_rn(y, kMagic);
@@ -94,8 +92,18 @@ __device__ __forceinline__ void encode_kblock(const Prolog& P, int kb, float inv
 #pragma unroll
     for (int l = 0; l < 3; l++) sl[l] += __shfl_xor_sync(0xffffffffu, sl[l], 1);
     hs += __shfl_xor_sync(0xffffffffu, hs, 1);
-    xs[cg * 4 + t] = (t & 1) ? make_int2(sl[2], 0) : make_int2(sl[0], sl[1]);
+    xs[cg * 4 + t] = (t & 1) ? make_short2((short)sl[2], 0) : make_short2((short)sl[0], (short)sl[1]);
     if ((t & 1) == 0) xsum[cg * 2 + (t >> 1)] = hs;
+}
+
+__device__ __forceinline__ void encode_kblock(const Prolog& P, int kb, float inv, int lane, uint8_t* xl, short2* xs,
+                                              float* xsum)
+{
+    float v[8];
+    const int base = kb * 256 + lane * 8;
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = P.value(base + i);
+    encode_values(v, kb, inv, lane, xl, xs, xsum);
 }
 
 struct Acc {
@@ -107,26 +115,63 @@ __device__ __forceinline__ uint32_t byte_of(uint32_t w, int k) { return (w >> (8
 __device__ __forceinline__ int sbyte_of(uint32_t w, int k) { return (int)(int8_t)((w >> (8 * k)) & 0xFFu); }
 __device__ __forceinline__ float h2f(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)bits16)); }
 
-/* One unit (16 rows x 256 columns) in shared memory: 8 int8 MMAs plus the
- * scale arithmetic of the format. */
-template <int FMT, bool EXP>
-__device__ __forceinline__ void process_unit(const uint8_t* __restrict__ u, int kb, const uint8_t* __restrict__ bptr,
-                                             int bstride, const int2* __restrict__ xs, const float* __restrict__ xsum,
-                                             int lane, Acc& A)
+/* One unit (16 rows x 256 columns) in shared memory.  Its bytes are first
+ * copied to registers and `release()` is called — the slot may then be
+ * refilled while this unit is computed — then come the 8 int8 MMAs and the
+ * scale arithmetic of the format.  (With expanded headers the per-chunk float
+ * pairs are read as the chunks go, so the slot is released at the end.)
+ *
+ * bp: this lane's B fragment of chunk 0 of the unit's k-block (chunk c at
+ * bp + c * FL_XENC_LIMB_BYTES), or a zero area for lanes whose column is not
+ * theirs. */
+template <int FMT, bool EXP, typename Release>
+__device__ __forceinline__ void process_unit(const uint8_t* __restrict__ u, int kb, const uint8_t* __restrict__ bp,
+                                             const short2* __restrict__ xs, const float* __restrict__ xsum, int lane,
+                                             Acc& A, Release&& release)
 {
     const int g = lane >> 2, t = lane & 3, h = t >> 1;
     constexpr bool NIB = FMT == FL_FMT_Q4K || FMT == FL_FMT_Q5K || FMT == FL_FMT_Q6K || FMT == FL_FMT_Q4_0;
     constexpr bool SIGNED = FMT == FL_FMT_Q8_0 || FMT == FL_FMT_Q8K;
+    constexpr int NW4 = NIB ? 4 : 8; /* uint4 words of quants per lane */
     const fl_unit_off o = fl_offsets(FMT, EXP);
-    const uint8_t* bp = bptr + (size_t)(kb * 8) * bstride;
-    const int2* xsk = xs + kb * 8 * 4 + t;
+    const short2* xsk = xs + kb * 8 * 4 + t;
 
-    /* per-unit scale state */
-    uint32_t scw0[4] = {0, 0, 0, 0}, scw1[4] = {0, 0, 0, 0}; /* raw header words of rows g, g+8 */
+    /* ── stage the unit in registers ── */
+    uint4 W[NW4];
+    uint32_t H5[4] = {0, 0, 0, 0};
+    uint2 H6[4] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
+#pragma unroll
+    for (int i = 0; i < NW4; i++) W[i] = *reinterpret_cast<const uint4*>(u + o.qs + (i * 32 + lane) * 16);
+    if constexpr (FMT == FL_FMT_Q5K) {
+#pragma unroll
+        for (int s = 0; s < 4; s++) H5[s] = *reinterpret_cast<const uint32_t*>(u + o.qh + (s * 32 + lane) * 4);
+    }
+    if constexpr (FMT == FL_FMT_Q6K) {
+#pragma unroll
+        for (int s = 0; s < 4; s++) H6[s] = *reinterpret_cast<const uint2*>(u + o.qh + (s * 32 + lane) * 8);
+    }
+    uint4 h0 = make_uint4(0, 0, 0, 0), h1 = h0; /* header words of rows g, g+8 */
+    float dd0 = 0.0f, dd1 = 0.0f;               /* Q6_K / Q8_K super-block scales */
+    if constexpr (!EXP) {
+        if constexpr (FMT == FL_FMT_Q6K) {
+            h0 = *reinterpret_cast<const uint4*>(u + FL_Q6K_SC + g * 16);
+            h1 = *reinterpret_cast<const uint4*>(u + FL_Q6K_SC + (g + 8) * 16);
+            dd0 = h2f(*reinterpret_cast<const uint16_t*>(u + FL_Q6K_D + g * 2));
+            dd1 = h2f(*reinterpret_cast<const uint16_t*>(u + FL_Q6K_D + (g + 8) * 2));
+        } else if constexpr (FMT == FL_FMT_Q8K) {
+            dd0 = *reinterpret_cast<const float*>(u + g * 4);
+            dd1 = *reinterpret_cast<const float*>(u + (g + 8) * 4);
+        } else {
+            h0 = *reinterpret_cast<const uint4*>(u + g * 16);
+            h1 = *reinterpret_cast<const uint4*>(u + (g + 8) * 16);
+        }
+        release();
+    }
+
+    /* ── per-unit scale state ── */
+    uint32_t scw0[4] = {0, 0, 0, 0}, scw1[4] = {0, 0, 0, 0};
     if constexpr (!EXP) {
         if constexpr (FMT == FL_FMT_Q4K || FMT == FL_FMT_Q5K) {
-            const uint4 h0 = *reinterpret_cast<const uint4*>(u + g * 16);
-            const uint4 h1 = *reinterpret_cast<const uint4*>(u + (g + 8) * 16);
             /* packed DecodeKScaleMin: 4 scales per word */
             scw0[0] = h0.y & 0x3F3F3F3Fu;
             scw0[1] = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
@@ -145,74 +190,55 @@ __device__ __forceinline__ void process_unit(const uint8_t* __restrict__ u, int 
             const float M1 = fmaf((float)byte_of(mw1, ka), sa, (float)byte_of(mw1, ka + 1) * sb);
             A.m0 = fmaf(h2f(h0.x >> 16), M0, A.m0);
             A.m1 = fmaf(h2f(h1.x >> 16), M1, A.m1);
-            scw0[2] = h0.x; /* keep d in slot 2 */
-            scw1[2] = h1.x;
-        } else if constexpr (FMT == FL_FMT_Q6K) {
-            const uint4 s0 = *reinterpret_cast<const uint4*>(u + FL_Q6K_SC + g * 16);
-            const uint4 s1 = *reinterpret_cast<const uint4*>(u + FL_Q6K_SC + (g + 8) * 16);
-            scw0[0] = s0.x; scw0[1] = s0.y; scw0[2] = s0.z; scw0[3] = s0.w;
-            scw1[0] = s1.x; scw1[1] = s1.y; scw1[2] = s1.z; scw1[3] = s1.w;
-        } else if constexpr (FMT == FL_FMT_Q8_0 || FMT == FL_FMT_Q4_0) {
-            const uint4 d0 = *reinterpret_cast<const uint4*>(u + g * 16);
-            const uint4 d1 = *reinterpret_cast<const uint4*>(u + (g + 8) * 16);
-            scw0[0] = d0.x; scw0[1] = d0.y; scw0[2] = d0.z; scw0[3] = d0.w;
-            scw1[0] = d1.x; scw1[1] = d1.y; scw1[2] = d1.z; scw1[3] = d1.w;
+        } else {
+            scw0[0] = h0.x; scw0[1] = h0.y; scw0[2] = h0.z; scw0[3] = h0.w;
+            scw1[0] = h1.x; scw1[1] = h1.y; scw1[2] = h1.z; scw1[3] = h1.w;
         }
     }
 
     int ia0 = 0, ia1 = 0, ib0 = 0, ib1 = 0; /* int32 accumulators: rows g, g+8 x limb pair */
 #pragma unroll
     for (int s = 0; s < 4; s++) {
-        uint4 W = make_uint4(0, 0, 0, 0), V0 = W, V1 = W;
-        uint32_t H5 = 0;
-        uint2 H6 = make_uint2(0, 0);
-        if constexpr (NIB) {
-            W = *reinterpret_cast<const uint4*>(u + o.qs + (s * 32 + lane) * 16);
-            if constexpr (FMT == FL_FMT_Q5K) H5 = *reinterpret_cast<const uint32_t*>(u + o.qh + (s * 32 + lane) * 4);
-            if constexpr (FMT == FL_FMT_Q6K) H6 = *reinterpret_cast<const uint2*>(u + o.qh + (s * 32 + lane) * 8);
-        } else {
-            V0 = *reinterpret_cast<const uint4*>(u + o.qs + ((s * 2 + 0) * 32 + lane) * 16);
-            V1 = *reinterpret_cast<const uint4*>(u + o.qs + ((s * 2 + 1) * 32 + lane) * 16);
-        }
 #pragma unroll
         for (int cc = 0; cc < 2; cc++) {
             const int c = 2 * s + cc;
             uint32_t a[4];
             if constexpr (NIB) {
-                const uint32_t wg = cc ? W.z : W.x, wg8 = cc ? W.w : W.y;
+                const uint4 Ws = W[s];
+                const uint32_t wg = cc ? Ws.z : Ws.x, wg8 = cc ? Ws.w : Ws.y;
                 a[0] = wg & 0x0F0F0F0Fu;
                 a[2] = (wg >> 4) & 0x0F0F0F0Fu;
                 a[1] = wg8 & 0x0F0F0F0Fu;
                 a[3] = (wg8 >> 4) & 0x0F0F0F0Fu;
                 if constexpr (FMT == FL_FMT_Q5K) {
                     const int j0 = 2 * cc, j1 = 2 * cc + 1; /* words of rows g, g+8 */
-                    a[0] |= fl_shift_bits(H5, 2 * j0, 4, 0x10101010u);
-                    a[2] |= fl_shift_bits(H5, 2 * j0 + 1, 4, 0x10101010u);
-                    a[1] |= fl_shift_bits(H5, 2 * j1, 4, 0x10101010u);
-                    a[3] |= fl_shift_bits(H5, 2 * j1 + 1, 4, 0x10101010u);
+                    a[0] |= fl_shift_bits(H5[s], 2 * j0, 4, 0x10101010u);
+                    a[2] |= fl_shift_bits(H5[s], 2 * j0 + 1, 4, 0x10101010u);
+                    a[1] |= fl_shift_bits(H5[s], 2 * j1, 4, 0x10101010u);
+                    a[3] |= fl_shift_bits(H5[s], 2 * j1 + 1, 4, 0x10101010u);
                 }
                 if constexpr (FMT == FL_FMT_Q6K) {
-                    const uint32_t Hc = cc ? H6.y : H6.x;
+                    const uint32_t Hc = cc ? H6[s].y : H6[s].x;
                     a[0] |= (Hc << 4) & 0x30303030u;
                     a[2] |= (Hc << 2) & 0x30303030u;
                     a[1] |= Hc & 0x30303030u;
                     a[3] |= (Hc >> 2) & 0x30303030u;
                 }
             } else {
-                const uint4 V = cc ? V1 : V0;
+                const uint4 V = W[c];
                 a[0] = V.x;
                 a[2] = V.y;
                 a[1] = V.z;
                 a[3] = V.w;
             }
-            const uint2 b = *reinterpret_cast<const uint2*>(bp + (size_t)c * bstride);
+            const uint2 b = *reinterpret_cast<const uint2*>(bp + c * FL_XENC_LIMB_BYTES);
             int d[4];
             fl_mma_i8<SIGNED>(d, a, b.x, b.y);
             if constexpr ((FMT == FL_FMT_Q6K || FMT == FL_FMT_Q4_0) && !EXP) {
                 /* (q - off) x = q x - off * sum(x): integer correction per limb
                  * (expanded headers carry the offset in `sub` instead) */
                 constexpr int off = FMT == FL_FMT_Q6K ? 32 : 8;
-                const int2 S = xsk[c * 4];
+                const short2 S = xsk[c * 4];
                 d[0] -= off * S.x;
                 d[1] -= off * S.y;
                 d[2] -= off * S.x;
@@ -261,41 +287,47 @@ __device__ __forceinline__ void process_unit(const uint8_t* __restrict__ u, int 
     }
     if constexpr (!EXP) {
         if constexpr (FMT == FL_FMT_Q4K || FMT == FL_FMT_Q5K) {
-            A.res0 = fmaf(h2f(scw0[2] & 0xFFFFu), fmaf((float)ia1, 1.0f / 128.0f, (float)ia0), A.res0);
-            A.res1 = fmaf(h2f(scw1[2] & 0xFFFFu), fmaf((float)ib1, 1.0f / 128.0f, (float)ib0), A.res1);
-        } else if constexpr (FMT == FL_FMT_Q6K) {
-            const float d0 = h2f(*reinterpret_cast<const uint16_t*>(u + FL_Q6K_D + g * 2));
-            const float d1 = h2f(*reinterpret_cast<const uint16_t*>(u + FL_Q6K_D + (g + 8) * 2));
-            A.res0 = fmaf(d0, fmaf((float)ia1, 1.0f / 128.0f, (float)ia0), A.res0);
-            A.res1 = fmaf(d1, fmaf((float)ib1, 1.0f / 128.0f, (float)ib0), A.res1);
-        } else if constexpr (FMT == FL_FMT_Q8K) {
-            const float d0 = *reinterpret_cast<const float*>(u + g * 4);
-            const float d1 = *reinterpret_cast<const float*>(u + (g + 8) * 4);
-            A.res0 = fmaf(d0, fmaf((float)ia1, 1.0f / 128.0f, (float)ia0), A.res0);
-            A.res1 = fmaf(d1, fmaf((float)ib1, 1.0f / 128.0f, (float)ib0), A.res1);
+            A.res0 = fmaf(h2f(h0.x & 0xFFFFu), fmaf((float)ia1, 1.0f / 128.0f, (float)ia0), A.res0);
+            A.res1 = fmaf(h2f(h1.x & 0xFFFFu), fmaf((float)ib1, 1.0f / 128.0f, (float)ib0), A.res1);
+        } else if constexpr (FMT == FL_FMT_Q6K || FMT == FL_FMT_Q8K) {
+            A.res0 = fmaf(dd0, fmaf((float)ia1, 1.0f / 128.0f, (float)ia0), A.res0);
+            A.res1 = fmaf(dd1, fmaf((float)ib1, 1.0f / 128.0f, (float)ib0), A.res1);
         }
+    } else {
+        release();
     }
 }
 
-__device__ __forceinline__ void process_any(int fmt, int expanded, const uint8_t* u, int kb, const uint8_t* bptr,
-                                            int bstride, const int2* xs, const float* xsum, int lane, Acc& A)
+struct NoRelease {
+    __device__ __forceinline__ void operator()() const {}
+};
+
+/* The unit's B-fragment base for this lane (see process_unit). */
+__device__ __forceinline__ const uint8_t* unit_bptr(const uint8_t* bptr, bool bval, const uint8_t* zero, int kb)
 {
+    return bval ? bptr + (size_t)kb * 8 * FL_XENC_LIMB_BYTES : zero;
+}
+
+__device__ __forceinline__ void process_any(int fmt, int expanded, const uint8_t* u, int kb, const uint8_t* bp,
+                                            const short2* xs, const float* xsum, int lane, Acc& A)
+{
+    NoRelease r;
     if (expanded) {
         switch (fmt) {
-        case FL_FMT_Q4K: process_unit<FL_FMT_Q4K, true>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
-        case FL_FMT_Q5K: process_unit<FL_FMT_Q5K, true>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
-        case FL_FMT_Q6K: process_unit<FL_FMT_Q6K, true>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
-        default: process_unit<FL_FMT_Q8K, true>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
+        case FL_FMT_Q4K: process_unit<FL_FMT_Q4K, true>(u, kb, bp, xs, xsum, lane, A, r); break;
+        case FL_FMT_Q5K: process_unit<FL_FMT_Q5K, true>(u, kb, bp, xs, xsum, lane, A, r); break;
+        case FL_FMT_Q6K: process_unit<FL_FMT_Q6K, true>(u, kb, bp, xs, xsum, lane, A, r); break;
+        default: process_unit<FL_FMT_Q8K, true>(u, kb, bp, xs, xsum, lane, A, r); break;
         }
         return;
     }
     switch (fmt) {
-    case FL_FMT_Q4K: process_unit<FL_FMT_Q4K, false>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
-    case FL_FMT_Q5K: process_unit<FL_FMT_Q5K, false>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
-    case FL_FMT_Q6K: process_unit<FL_FMT_Q6K, false>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
-    case FL_FMT_Q8_0: process_unit<FL_FMT_Q8_0, false>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
-    case FL_FMT_Q4_0: process_unit<FL_FMT_Q4_0, false>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
-    default: process_unit<FL_FMT_Q8K, false>(u, kb, bptr, bstride, xs, xsum, lane, A); break;
+    case FL_FMT_Q4K: process_unit<FL_FMT_Q4K, false>(u, kb, bp, xs, xsum, lane, A, r); break;
+    case FL_FMT_Q5K: process_unit<FL_FMT_Q5K, false>(u, kb, bp, xs, xsum, lane, A, r); break;
+    case FL_FMT_Q6K: process_unit<FL_FMT_Q6K, false>(u, kb, bp, xs, xsum, lane, A, r); break;
+    case FL_FMT_Q8_0: process_unit<FL_FMT_Q8_0, false>(u, kb, bp, xs, xsum, lane, A, r); break;
+    case FL_FMT_Q4_0: process_unit<FL_FMT_Q4_0, false>(u, kb, bp, xs, xsum, lane, A, r); break;
+    default: process_unit<FL_FMT_Q8K, false>(u, kb, bp, xs, xsum, lane, A, r); break;
     }
 }
 

@@ -108,9 +108,12 @@ struct fl_session {
     std::vector<double> phase_bytes;
     int32_t* bar = nullptr;
     uint64_t* timestamps = nullptr;
+    uint64_t* cta_done = nullptr;
+    uint64_t* detail = nullptr;
     FlTokenArgs ta;
     size_t tk_smem = 0;
     int tk_grid = 0;
+    const void* tk_kernel = nullptr;
     std::vector<void*> allocs;
 };
 
@@ -609,7 +612,7 @@ static void build_phases(fl_session* s, PhaseList& P)
 static int enqueue_step(fl_session* s)
 {
     CK(cudaMemsetAsync(s->bar, 0, 4, s->st));
-    CK(fl_launch_token(s->ta, s->tk_grid, s->tk_smem, s->st));
+    CK(fl_launch_token(s->tk_kernel, s->ta, s->tk_grid, s->tk_smem, s->st));
     return FL_OK;
 }
 
@@ -625,15 +628,19 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     const fl_model_desc& d = m->d;
     if (max_ctx <= 0 || max_ctx > d.max_ctx) max_ctx = d.max_ctx;
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    const void* tk_kernel = fl_token_kernel_ptr(d.head_dim, d.n_heads / d.n_kv_heads);
+    if (!tk_kernel)
+        return fail(FL_ERR_UNSUPPORTED, "no token kernel for head_dim %d with %d query heads per kv head", d.head_dim,
+                    d.n_heads / d.n_kv_heads);
     int max_dyn = 0;
-    if (fl_token_configure(&max_dyn) != cudaSuccess) return fail(FL_ERR_CUDA, "token kernel configuration failed");
+    if (fl_token_configure(tk_kernel, &max_dyn) != cudaSuccess) return fail(FL_ERR_CUDA, "token kernel configuration failed");
     fl_session* s = new fl_session();
     s->m = m;
     s->max_ctx = max_ctx;
     const int h = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim, grp = d.n_heads / d.n_kv_heads;
     const int G = m->sm_count;
-    /* attention items (kv head, split): about one per SM */
-    int split = (G + d.n_kv_heads - 1) / d.n_kv_heads;
+    /* attention items (kv head, split): at most one per SM */
+    int split = G / d.n_kv_heads;
     if (split > max_ctx) split = max_ctx;
     if (split < 1) split = 1;
     s->attn_split = split;
@@ -679,20 +686,31 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     s->phase_bytes = P.bytes;
     rc = dalloc(s->allocs, &s->d_phases, P.ph.size() * sizeof(FlPhase));
     if (!rc) rc = dalloc(s->allocs, &s->timestamps, (P.ph.size() + 1) * 8);
+    if (!rc) rc = dalloc(s->allocs, &s->cta_done, P.ph.size() * (size_t)G * 8);
+    if (!rc) rc = dalloc(s->allocs, &s->detail, P.ph.size() * (size_t)(FL_TK_WARPS * 4 + 1) * 8);
     if (rc) {
         fl_session_destroy(s);
         return rc;
     }
     /* shared memory: weight ring of the largest unit + x-encoding / attention scratch */
-    int slot = 0, max_kb = 0;
+    int slot = 0, max_kb = 0, max_tiles = 0;
     for (const FlPhase& p : P.ph)
         if (p.kind == FL_PH_MATVEC) {
             for (int i = 0; i < p.mv.n_seg; i++) slot = std::max(slot, p.mv.seg[i].unit_bytes);
             max_kb = std::max(max_kb, p.mv.n_kb);
+            max_tiles = std::max(max_tiles, (p.mv.n_tiles + G - 1) / G);
         }
+    if (max_tiles > FL_TK_MAX_TILES) {
+        fl_session_destroy(s);
+        return fail(FL_ERR_UNSUPPORTED, "a projection has %d row tiles per SM (limit %d)", max_tiles, FL_TK_MAX_TILES);
+    }
     slot = (slot + 127) & ~127;
-    const size_t xenc = (size_t)max_kb * 8 * (FL_XENC_LIMB_BYTES + 32 + 8);
-    const size_t attn = (size_t)(grp * d.head_dim + FL_TK_WARPS * grp * 2 + FL_TK_WARPS * grp * d.head_dim) * 4;
+    const size_t xenc = (size_t)max_kb * 8 * FL_XENC_CHUNK_BYTES;
+    /* attention: q, per-warp outputs, reductions, the scores of one item */
+    const int span = d.sliding_window > 0 ? std::min(max_ctx, d.sliding_window) : max_ctx;
+    const int per_max = (span + s->attn_split - 1) / s->attn_split;
+    const size_t attn =
+        (size_t)(grp * d.head_dim + FL_TK_WARPS * grp * d.head_dim + FL_TK_WARPS * 8 + per_max * grp) * 4;
     const size_t scratch = std::max(xenc, attn);
     int n_slots = 2;
     while (fl_token_smem_bytes(n_slots + 1, slot, scratch) <= (size_t)max_dyn) n_slots++;
@@ -710,6 +728,8 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     ta.bar = s->bar;
     ta.err = s->state + ST_ERR;
     ta.timestamps = s->timestamps;
+    ta.cta_done = s->cta_done;
+    ta.detail = s->detail;
     ta.advance = 1;
     ta.token = s->state + ST_TOKEN;
     ta.pos = s->state + ST_POS;
@@ -717,8 +737,9 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     ta.step = s->state + ST_STEP;
     s->tk_smem = fl_token_smem_bytes(n_slots, slot, scratch);
     s->tk_grid = G;
+    s->tk_kernel = tk_kernel;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fl_token_kernel_ptr(), 32 * (FL_TK_WARPS + 1),
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tk_kernel, 32 * FL_TK_WARPS,
                                                       s->tk_smem) != cudaSuccess ||
         per_sm < 1) {
         fl_session_destroy(s);
@@ -1009,6 +1030,36 @@ extern "C" int fl_matvec(int32_t type, const void* w, uint64_t nbytes, int32_t r
 
 /* Per-phase device milliseconds of the most recent step (diagnostics; phase
  * order: embed, then per layer qkv, attention, wo, gate/up, down, then head). */
+/* Per phase p < n_phases - 1 and CTA b: ms from the phase's start (CTA 0) to
+ * the moment CTA b finished its share of it, out[p * grid + b]. */
+extern "C" int fl_session_cta_done_ms(fl_session* s, double* out, int64_t cap, int32_t* grid)
+{
+    if (!s || !out || !grid) return fail(FL_ERR_ARG, "null argument");
+    const int G = s->tk_grid;
+    std::vector<uint64_t> ts((size_t)s->n_phases + 1), done((size_t)s->n_phases * G);
+    CK(cudaMemcpy(ts.data(), s->timestamps, ts.size() * 8, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(done.data(), s->cta_done, done.size() * 8, cudaMemcpyDeviceToHost));
+    *grid = G;
+    for (int p = 0; p + 1 < s->n_phases; p++)
+        for (int b = 0; b < G; b++)
+            if ((int64_t)p * G + b < cap) out[(size_t)p * G + b] = ((double)done[(size_t)p * G + b] - (double)ts[p]) * 1e-6;
+    return FL_OK;
+}
+
+/* The raw per-warp matvec counters of CTA 0 (FlTokenArgs.detail) and the
+ * phase start stamps: out = [n_phases + 1] starts, then the detail array. */
+extern "C" int fl_session_detail(fl_session* s, uint64_t* out, int64_t cap, int32_t* n_phases, int32_t* n_warps)
+{
+    if (!s || !out || !n_phases || !n_warps) return fail(FL_ERR_ARG, "null argument");
+    const size_t nd = (size_t)s->n_phases * (FL_TK_WARPS * 4 + 1), nt = (size_t)s->n_phases + 1;
+    if ((int64_t)(nd + nt) > cap) return fail(FL_ERR_ARG, "need %zu entries", nd + nt);
+    CK(cudaMemcpy(out, s->timestamps, nt * 8, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(out + nt, s->detail, nd * 8, cudaMemcpyDeviceToHost));
+    *n_phases = s->n_phases;
+    *n_warps = FL_TK_WARPS;
+    return FL_OK;
+}
+
 extern "C" int fl_session_phase_ms(fl_session* s, double* out, int32_t cap, int32_t* n)
 {
     if (!s || !out || !n) return fail(FL_ERR_ARG, "null argument");

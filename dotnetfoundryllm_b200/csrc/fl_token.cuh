@@ -1,0 +1,848 @@
+/*
+ * fl_token.cuh — one decode step (IForwardPass.Forward + greedy ArgMax) as one
+ * persistent cooperative kernel.
+ *
+ * The step is a list of phases (embedding row, then per layer: QKV matvec,
+ * attention, output projection, gate/up, down; then the LM head), the same
+ * ops as LlamaForwardPass.Forward (src/DotNetFoundryLLM.Architectures/
+ * LlamaForwardPass.cs:82-130) and its Mistral/Gemma2/Qwen2 copies.  One CTA
+ * per SM runs all of them, 16 warps each:
+ *
+ *  - in a matvec phase the CTA's units (16 rows x 256 columns of weights) are
+ *    split into 16 contiguous ranges, one per warp (stream-K inside the CTA).
+ *    A tile inside one warp's range is finished by that warp alone; the at
+ *    most two tiles a range shares with its neighbours are summed in warp
+ *    order by whichever contributor finishes last, so every result is
+ *    deterministic;
+ *  - each warp streams its own units HBM → shared memory with 1-D bulk async
+ *    copies into a private ring of mbarrier slots.  Its lane 0 refills a slot
+ *    as soon as the unit in it has been copied to registers, running ahead
+ *    through the warp's ranges of the following matvec phases, so the next
+ *    projection's weights are in flight while the current phase drains and the
+ *    grid synchronizes;
+ *  - phases are separated by a grid barrier (arrival counter in global memory,
+ *    bounded spin); data produced by an earlier phase is read through L2.
+ *
+ * All CTAs must be resident at once: the kernel is launched cooperatively with
+ * one CTA per SM.  Every wait is bounded and records FL_DEV_ERR_TIMEOUT instead
+ * of hanging.
+ */
+#ifndef FL_TOKEN_CUH
+#define FL_TOKEN_CUH
+
+#include "fl_mv_core.cuh"
+
+namespace fltk {
+namespace { /* internal linkage: the header is compiled into several units */
+
+using namespace flcore;
+
+constexpr int NW = FL_TK_WARPS;          /* warps */
+constexpr int NC = NW * 32;              /* threads */
+constexpr int NT = NC;
+constexpr int TCNT = FL_TK_MAX_TILES;    /* per-CTA tiles of one phase */
+
+/* Lane 0's cursor over its warp's units of every matvec phase, in the order the
+ * warp consumes them (kept in shared memory, one per warp). */
+struct FeedState {
+    const uint8_t* src; /* next unit */
+    int p;              /* its phase */
+    int run;            /* units left in the current run (consecutive k-blocks of one tile) */
+    int left;           /* units of the warp's range in phase p after the current run */
+    int it;             /* CTA-local tile index of the current run */
+    int slot;           /* ring slot of the next unit */
+    uint32_t bytes;     /* unit size of the current run */
+};
+
+struct TkLayout {
+    size_t ring, full, scratch, zero, outbox, tcnt, best, misc, feed, args, args_stride, total;
+};
+
+/* n_slots is per warp. */
+__host__ __device__ inline TkLayout tk_layout(int n_slots, int slot_bytes, size_t scratch_bytes)
+{
+    TkLayout L;
+    L.ring = 0;
+    L.full = L.ring + (size_t)NW * n_slots * slot_bytes;
+    L.scratch = (L.full + (size_t)NW * n_slots * 8 + 127) & ~(size_t)127;
+    L.zero = L.scratch + ((scratch_bytes + 15) & ~(size_t)15);
+    L.outbox = L.zero + FL_XENC_ZERO_BYTES;          /* [NW][2][16] floats */
+    L.tcnt = L.outbox + (size_t)NW * 2 * 16 * 4;     /* [TCNT] ints */
+    L.best = L.tcnt + (size_t)TCNT * 4;              /* [NW][2] */
+    L.misc = L.best + NW * 8;                        /* 64 floats */
+    L.feed = (L.misc + 64 * 4 + 15) & ~(size_t)15;   /* [NW] FeedState */
+    L.args = L.feed + ((NW * sizeof(FeedState) + 15) & ~(size_t)15); /* staged phase arguments */
+    const size_t args = sizeof(FlMvArgs) > sizeof(FlAttnArgs) ? sizeof(FlMvArgs) : sizeof(FlAttnArgs);
+    L.args_stride = (args + 15) / 16 * 16;           /* two buffers: phases alternate */
+    L.total = L.args + 2 * L.args_stride;
+    return L;
+}
+
+__device__ __forceinline__ void consumer_sync() { __syncthreads(); }
+
+__device__ __forceinline__ int ld_acquire(const int* p)
+{
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+/* All CTAs finish phase k before any starts phase k+1.  Bounded: gives up after
+ * ~2 s, records a timeout and lets the kernel run to its end. */
+__device__ void grid_sync(int* bar, int target, int* err, uint64_t* done_stamp)
+{
+    consumer_sync();
+    if (threadIdx.x == 0) {
+        if (done_stamp) *done_stamp = fl_globaltimer();
+        __threadfence();
+        atomicAdd(bar, 1);
+        if (ld_acquire(bar) < target) {
+            const uint64_t t0 = fl_globaltimer();
+            for (uint32_t it = 0;; it++) {
+                if (ld_acquire(bar) >= target) break;
+                __nanosleep(64);
+                if ((it & 63u) == 0 && (fl_globaltimer() - t0 > 2000000000ull || it > (1u << 26))) {
+                    atomicExch(err, FL_DEV_ERR_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __threadfence();
+    }
+    consumer_sync();
+}
+
+/* Block reduction over the consumer threads (sum, max). */
+__device__ __forceinline__ void consumer_sum_max(float& s, float& m, float* scratch)
+{
+    s = fl_warp_sum(s);
+    m = fl_warp_max(m);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    consumer_sync();
+    if (lane == 0) {
+        scratch[warp] = s;
+        scratch[32 + warp] = m;
+    }
+    consumer_sync();
+    float ts = 0.0f, tm = 0.0f;
+    for (int w = 0; w < NW; w++) {
+        ts += scratch[w];
+        tm = fmaxf(tm, scratch[32 + w]);
+    }
+    s = ts;
+    m = tm;
+}
+
+/* Copies a phase's argument block into shared memory (read there by the hot
+ * loops); published by the barrier that follows. */
+__device__ __forceinline__ void copy_words(void* dst, const void* src, size_t bytes)
+{
+    const int n = (int)(bytes / 4);
+    for (int i = threadIdx.x; i < n; i += NC)
+        reinterpret_cast<uint32_t*>(dst)[i] = reinterpret_cast<const uint32_t*>(src)[i];
+}
+
+/* The CTA's U units of a phase (tile-major: unit i = tile i / n_kb, k-block
+ * i % n_kb) split into NW contiguous ranges, the first `rem` of length q+1. */
+struct Split {
+    int q, rem;
+    __device__ __forceinline__ int lo(int w) const { return w * q + (w < rem ? w : rem); }
+    __device__ __forceinline__ int len(int w) const { return q + (w < rem ? 1 : 0); }
+    /* the warp whose range holds unit i */
+    __device__ __forceinline__ int owner(int i) const
+    {
+        const int big = rem * (q + 1);
+        return i < big ? i / (q + 1) : rem + (q > 0 ? (i - big) / q : 0);
+    }
+};
+
+/* ── phases ─────────────────────────────────────────────────────────────── */
+
+__device__ void phase_embed(const FlEmbedArgs& e, int* err)
+{
+    /* TokenEmbedding.AsSpan(tokenId * h, h).CopyTo(_x) (LlamaForwardPass.cs:96) */
+    int tok = __ldcg(e.token);
+    if (tok < 0 || tok >= e.vocab) {
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(err, FL_DEV_ERR_TOKEN);
+        tok = 0;
+    }
+    const int stride = gridDim.x * NW * 32;
+    for (int i = blockIdx.x * NW * 32 + threadIdx.x; i < e.hidden; i += stride)
+        e.x[i] = fl_dequant_elem(e.ggml_type, e.raw, (int64_t)tok * e.hidden + i);
+    for (int i = blockIdx.x * NW * 32 + threadIdx.x; i < e.zero_n; i += stride) e.zero_buf[i] = 0.0f;
+}
+
+template <int PER>
+__device__ __forceinline__ void load_row(const float* p, float (&v)[PER])
+{
+    if constexpr (PER == 2) {
+        const float2 a = __ldcg(reinterpret_cast<const float2*>(p));
+        v[0] = a.x;
+        v[1] = a.y;
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; i += 4) {
+            const float4 a = __ldcg(reinterpret_cast<const float4*>(p + i));
+            v[i] = a.x;
+            v[i + 1] = a.y;
+            v[i + 2] = a.z;
+            v[i + 3] = a.w;
+        }
+    }
+}
+
+template <int PER>
+__device__ __forceinline__ void load_row_smem(const float* p, float (&v)[PER])
+{
+    if constexpr (PER == 2) {
+        const float2 a = *reinterpret_cast<const float2*>(p);
+        v[0] = a.x;
+        v[1] = a.y;
+    } else {
+#pragma unroll
+        for (int i = 0; i < PER; i += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(p + i);
+            v[i] = a.x;
+            v[i + 1] = a.y;
+            v[i + 2] = a.z;
+            v[i + 3] = a.w;
+        }
+    }
+}
+
+/* Attention for items (kv head, split) b, b+G, ... in two passes over the
+ * item's keys:
+ *  1. scores: head_dim/32 lanes per key (32 dims each, log2 of that many
+ *     shuffles to combine), for all query heads of the group; then the
+ *     CTA-wide maximum and the softmax weights exp(s - max) of every score;
+ *  2. values: lanes own head_dim/32 dims, warps split the keys, the weights
+ *     come from shared memory; the warps' sums are added in warp order.
+ * The item's (max, sum, unnormalized output) goes to global memory; the last
+ * item of a kv head merges the splits in split order.
+ * ComputeAttention: LlamaForwardPass.cs:158-211; MistralForwardPass.cs:186-240;
+ * Gemma2ForwardPass.cs:126-185. */
+template <int HD, int GMAX>
+__device__ void phase_attn_t(const FlAttnArgs& a, float* scr)
+{
+    const int grp = a.n_heads / a.n_kv; /* query heads per kv head, <= GMAX */
+    constexpr int LPK = HD / 32;  /* lanes per key in pass 1, 8 float4 chunks each */
+    constexpr int KPW = 32 / LPK; /* keys per warp per round */
+    constexpr int PER = HD / 32;  /* dims per lane in pass 2 */
+    constexpr int VB = 16 / PER;  /* keys per warp in flight in pass 2 */
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = lane % LPK;
+    const int kv_dim = a.n_kv * HD;
+    float* sq = scr;                      /* [grp][HD] */
+    float* sacc = sq + grp * HD;          /* [NW][grp][HD] */
+    float* sred = sacc + NW * grp * HD;   /* [NW][GMAX] */
+    float* sp = sred + NW * GMAX;         /* [keys][grp] scores, then weights */
+    __shared__ int s_last;
+    __shared__ float s_M[8], s_L[8];
+    const int seq = __ldcg(a.pos) + 1;
+    int start = 0;
+    if (a.window < seq) start = seq - a.window;
+    const int per = (seq - start + a.n_split - 1) / a.n_split;
+    const float inv_cap = a.softcap > 0.0f ? 1.0f / a.softcap : 0.0f;
+    const int n_items = a.n_kv * a.n_split;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const int kvh = item / a.n_split, split = item % a.n_split;
+        const int k0 = start + split * per;
+        const int n = max(0, min(seq, k0 + per) - k0);
+        for (int i = threadIdx.x; i < grp * HD; i += NC) sq[i] = __ldcg(a.q + (size_t)kvh * grp * HD + i);
+        consumer_sync();
+
+        /* pass 1: scores */
+        float mloc[GMAX];
+#pragma unroll
+        for (int h = 0; h < GMAX; h++) mloc[h] = -INFINITY;
+        for (int base = 0; base < n; base += NW * KPW) {
+            const int kk = base + warp * KPW + lane / LPK;
+            float acc[GMAX];
+#pragma unroll
+            for (int h = 0; h < GMAX; h++) acc[h] = 0.0f;
+            if (kk < n) {
+                const float* kr = a.k_cache + (size_t)(k0 + kk) * kv_dim + (size_t)kvh * HD;
+                float4 kv[8];
+#pragma unroll
+                for (int c = 0; c < 8; c++) kv[c] = __ldcg(reinterpret_cast<const float4*>(kr) + c * LPK + qd);
+#pragma unroll
+                for (int c = 0; c < 8; c++)
+#pragma unroll
+                    for (int h = 0; h < GMAX; h++) {
+                        if (h >= grp) break;
+                        const float4 q4 = reinterpret_cast<const float4*>(sq + h * HD)[c * LPK + qd];
+                        acc[h] = fmaf(q4.x, kv[c].x, acc[h]);
+                        acc[h] = fmaf(q4.y, kv[c].y, acc[h]);
+                        acc[h] = fmaf(q4.z, kv[c].z, acc[h]);
+                        acc[h] = fmaf(q4.w, kv[c].w, acc[h]);
+                    }
+            }
+#pragma unroll
+            for (int h = 0; h < GMAX; h++)
+#pragma unroll
+                for (int o = 1; o < LPK; o <<= 1) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], o);
+            if (kk < n) {
+#pragma unroll
+                for (int h = 0; h < GMAX; h++) {
+                    if (h >= grp) break;
+                    float sc = __fmul_rn(acc[h], a.scale);
+                    if (a.softcap > 0.0f) sc = __fmul_rn(tanhf(__fmul_rn(sc, inv_cap)), a.softcap);
+                    if (qd == 0) sp[kk * grp + h] = sc;
+                    mloc[h] = fmaxf(mloc[h], sc);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < GMAX; h++) {
+            const float m = fl_warp_max(mloc[h]);
+            if (lane == 0) sred[warp * GMAX + h] = m;
+        }
+        consumer_sync();
+        if (threadIdx.x < grp) {
+            float M = -INFINITY;
+            for (int w = 0; w < NW; w++) M = fmaxf(M, sred[w * GMAX + threadIdx.x]);
+            s_M[threadIdx.x] = M;
+        }
+        consumer_sync();
+        /* softmax weights exp(s - max) and their sums, head by head */
+        for (int h = 0; h < grp; h++) {
+            const float M = s_M[h];
+            float l = 0.0f;
+            for (int t = threadIdx.x; t < n; t += NC) {
+                const float p = __expf(sp[t * grp + h] - M);
+                sp[t * grp + h] = p;
+                l += p;
+            }
+            l = fl_warp_sum(l);
+            if (lane == 0) sred[warp * GMAX + h] = l;
+        }
+        consumer_sync();
+        if (threadIdx.x < grp) {
+            float L = 0.0f;
+            for (int w = 0; w < NW; w++) L += sred[w * GMAX + threadIdx.x];
+            s_L[threadIdx.x] = L;
+        }
+
+        /* pass 2: weighted values */
+        const int d0 = lane * PER;
+        float o[GMAX][PER];
+#pragma unroll
+        for (int h = 0; h < GMAX; h++)
+#pragma unroll
+            for (int p = 0; p < PER; p++) o[h][p] = 0.0f;
+        for (int t0 = warp; t0 < n; t0 += VB * NW) {
+            float vv[VB][PER];
+#pragma unroll
+            for (int j = 0; j < VB; j++) {
+                const int t = t0 + j * NW;
+                if (t < n) load_row<PER>(a.v_cache + (size_t)(k0 + t) * kv_dim + (size_t)kvh * HD + d0, vv[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < VB; j++) {
+                const int t = t0 + j * NW;
+                if (t < n) {
+#pragma unroll
+                    for (int h = 0; h < GMAX; h++) {
+                        if (h >= grp) break;
+                        const float pw = sp[t * grp + h];
+#pragma unroll
+                        for (int p = 0; p < PER; p++) o[h][p] = fmaf(pw, vv[j][p], o[h][p]);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < GMAX; h++) {
+            if (h >= grp) break;
+#pragma unroll
+            for (int p = 0; p < PER; p++) sacc[(warp * grp + h) * HD + d0 + p] = o[h][p];
+        }
+        consumer_sync();
+        float* part = a.part + (size_t)item * grp * (HD + 2);
+        for (int i = threadIdx.x; i < grp * HD; i += NC) {
+            const int h = i / HD, d = i % HD;
+            float O = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; w++) O += sacc[(w * grp + h) * HD + d];
+            part[h * (HD + 2) + 2 + d] = O;
+            if (d == 0) {
+                part[h * (HD + 2)] = n > 0 ? s_M[h] : -INFINITY;
+                part[h * (HD + 2) + 1] = s_L[h];
+            }
+        }
+        __threadfence();
+        consumer_sync();
+        if (threadIdx.x == 0) s_last = atomicAdd(&a.counter[kvh], 1) == a.n_split - 1;
+        consumer_sync();
+        if (s_last) {
+            __threadfence();
+            /* merge the splits: stage (m, l) of every split, then the weighted sum */
+            const float* pk = a.part + (size_t)kvh * a.n_split * grp * (HD + 2);
+            float* w_s = sacc;                         /* [n_split][grp] maxima, then weights */
+            float* l_s = sacc + a.n_split * grp;       /* [n_split][grp] sums */
+            for (int i = threadIdx.x; i < a.n_split * grp; i += NC) {
+                w_s[i] = __ldcg(&pk[(size_t)i * (HD + 2)]);
+                l_s[i] = __ldcg(&pk[(size_t)i * (HD + 2) + 1]);
+            }
+            consumer_sync();
+            if (threadIdx.x < grp) {
+                const int h = threadIdx.x;
+                float M = -INFINITY;
+                for (int s = 0; s < a.n_split; s++) M = fmaxf(M, w_s[s * grp + h]);
+                float Ls = 0.0f;
+                for (int s = 0; s < a.n_split; s++) {
+                    const float ms = w_s[s * grp + h];
+                    const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
+                    Ls = fmaf(l_s[s * grp + h], f, Ls);
+                    w_s[s * grp + h] = f;
+                }
+                s_L[h] = Ls;
+            }
+            consumer_sync();
+            float amax = 0.0f;
+            for (int i = threadIdx.x; i < grp * HD; i += NC) {
+                const int h = i / HD, d = i % HD;
+                float O = 0.0f;
+#pragma unroll 16
+                for (int s = 0; s < a.n_split; s++)
+                    O = fmaf(__ldcg(&pk[((size_t)s * grp + h) * (HD + 2) + 2 + d]), w_s[s * grp + h], O);
+                const float ov = s_L[h] > 0.0f ? O / s_L[h] : 0.0f;
+                a.out[((size_t)kvh * grp + h) * HD + d] = ov;
+                amax = fmaxf(amax, fabsf(ov));
+            }
+            amax = fl_warp_max(amax);
+            if (lane == 0) atomicMax(reinterpret_cast<int*>(a.out_absmax), __float_as_int(amax));
+            if (threadIdx.x == 0) a.counter[kvh] = 0;
+        }
+        consumer_sync();
+    }
+}
+
+/* Asks L2 for the cached keys and values the CTA's attention items will read
+ * (every position before the current one; the current row is written by the
+ * QKV phase), so that the attention phase reads them from L2.  Same item
+ * split as phase_attn_t. */
+__device__ void prefetch_attn_kv(const FlAttnArgs& a)
+{
+    const int pos = __ldcg(a.pos);
+    const int seq = pos + 1;
+    int start = 0;
+    if (a.window < seq) start = seq - a.window;
+    const int per = (seq - start + a.n_split - 1) / a.n_split;
+    const int kv_dim = a.n_kv * a.head_dim;
+    const uint32_t row_bytes = (uint32_t)a.head_dim * 4;
+    for (int item = blockIdx.x; item < a.n_kv * a.n_split; item += gridDim.x) {
+        const int kvh = item / a.n_split, split = item % a.n_split;
+        const int k0 = start + split * per, k1 = min(pos, k0 + per);
+        for (int i = threadIdx.x; i < 2 * (k1 - k0); i += NC) {
+            const float* base = (i & 1) ? a.v_cache : a.k_cache;
+            fl_prefetch_l2(base + (size_t)(k0 + (i >> 1)) * kv_dim + (size_t)kvh * a.head_dim, row_bytes);
+        }
+    }
+}
+
+/* A warp's private weight ring: S slots of slot_bytes with one full barrier
+ * each.  The warp is both producer and consumer of its ring: lane 0 refills a
+ * slot once the warp has copied the unit in it to registers. */
+struct WarpRing {
+    uint8_t* base;
+    uint64_t* full;
+    int S, slot_bytes;
+};
+
+__device__ __forceinline__ int my_tiles_of(const FlMvArgs& a)
+{
+    const int G = gridDim.x;
+    return a.n_tiles > (int)blockIdx.x ? (a.n_tiles - (int)blockIdx.x + G - 1) / G : 0;
+}
+
+/* Moves the cursor to the warp's next run of units: the next tile of its
+ * range in the current phase, or the start of its range in the next matvec
+ * phase.  False once every unit has been issued. */
+__device__ __forceinline__ bool feed_advance(const FlTokenArgs& ta, FeedState& F, int warp)
+{
+    int kb = 0;
+    if (F.left > 0) {
+        F.it++;
+    } else {
+        for (;;) {
+            if (F.p + 1 >= ta.n_phases) {
+                F.p = ta.n_phases;
+                return false;
+            }
+            F.p++;
+            if (ta.phases[F.p].kind != FL_PH_MATVEC) continue;
+            const FlMvArgs& a = ta.phases[F.p].mv;
+            const int U = my_tiles_of(a) * a.n_kb;
+            const Split S{U / NW, U % NW};
+            const int len = S.len(warp);
+            if (len == 0) continue;
+            const int lo = S.lo(warp);
+            F.it = lo / a.n_kb;
+            kb = lo - F.it * a.n_kb;
+            F.left = len;
+            break;
+        }
+    }
+    const FlMvArgs& a = ta.phases[F.p].mv;
+    const int n_kb = a.n_kb;
+    const int run = min(n_kb - kb, F.left);
+    F.left -= run;
+    F.run = run;
+    const int tile = (int)blockIdx.x + F.it * (int)gridDim.x;
+    const FlMvSeg& sg = a.seg[seg_of(a, tile)];
+    F.bytes = (uint32_t)sg.unit_bytes;
+    F.src = sg.w + ((size_t)(tile - sg.tile0) * n_kb + kb) * F.bytes;
+    return true;
+}
+
+/* Lane 0: issues the copy of the warp's next unit into the next ring slot. */
+__device__ __forceinline__ void feed(const FlTokenArgs& ta, const WarpRing& R, FeedState& F, int warp)
+{
+    if (F.run == 0 && !feed_advance(ta, F, warp)) return;
+    const int slot = F.slot;
+    const uint32_t bytes = F.bytes;
+    const uint8_t* src = F.src;
+    fl_mbar_expect_tx(&R.full[slot], bytes);
+    fl_bulk_g2s(R.base + (size_t)slot * R.slot_bytes, src, bytes, &R.full[slot]);
+    F.src = src + bytes;
+    F.run--;
+    F.slot = slot + 1 == R.S ? 0 : slot + 1;
+}
+
+/* n consecutive units (k-blocks kb0..kb0+n-1 of one tile) of format FMT.  A
+ * unit's slot is refilled as soon as its bytes are in registers. */
+/* Per-warp counters of a matvec phase (reported for CTA 0 when profiling). */
+struct UnitStats {
+    uint64_t wait_cycles;
+    uint32_t waits, units;
+};
+
+template <int FMT, bool EXP>
+__device__ __forceinline__ void run_units(const FlTokenArgs& ta, const WarpRing& R, FeedState& f, int& cslot,
+                                          uint32_t& cpar, int n, int kb0, const uint8_t* bptr, bool bval,
+                                          const uint8_t* zero, const short2* xs, const float* xsum, int lane,
+                                          int warp, Acc& A, UnitStats& st)
+{
+    for (int k = 0; k < n; k++) {
+        if (!fl_mbar_test(&R.full[cslot], cpar)) {
+            const long long t0 = clock64();
+            fl_mbar_wait(&R.full[cslot], cpar, ta.err);
+            st.wait_cycles += (uint64_t)(clock64() - t0);
+            st.waits++;
+        }
+        st.units++;
+        const int kb = kb0 + k;
+        process_unit<FMT, EXP>(R.base + (size_t)cslot * R.slot_bytes, kb, unit_bptr(bptr, bval, zero, kb), xs, xsum,
+                               lane, A, [&]() {
+                                   __syncwarp();
+                                   if (lane == 0) {
+                                       fl_fence_proxy_async();
+                                       feed(ta, R, f, warp);
+                                   }
+                               });
+        if (++cslot == R.S) {
+            cslot = 0;
+            cpar ^= 1u;
+        }
+    }
+}
+
+template <int HD, int GMAX>
+__global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__ FlTokenArgs ta)
+{
+    extern __shared__ __align__(128) uint8_t smem[];
+    const TkLayout Ls = tk_layout(ta.n_slots, ta.slot_bytes, ta.scratch_bytes);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+    const int G = gridDim.x;
+    const WarpRing R{smem + Ls.ring + (size_t)warp * ta.n_slots * ta.slot_bytes,
+                     reinterpret_cast<uint64_t*>(smem + Ls.full) + warp * ta.n_slots, ta.n_slots, ta.slot_bytes};
+    uint8_t* scratch = smem + Ls.scratch;
+    uint8_t* zero = smem + Ls.zero;
+    float* outbox = reinterpret_cast<float*>(smem + Ls.outbox);
+    int* tcnt = reinterpret_cast<int*>(smem + Ls.tcnt);
+    float* best = reinterpret_cast<float*>(smem + Ls.best);
+    float* misc = reinterpret_cast<float*>(smem + Ls.misc);
+    FeedState& f = reinterpret_cast<FeedState*>(smem + Ls.feed)[warp];
+
+    if (lane == 0) {
+        for (int i = 0; i < R.S; i++) fl_mbar_init(&R.full[i], 1);
+        f.src = nullptr;
+        f.p = -1;
+        f.run = f.left = f.it = f.slot = 0;
+        f.bytes = 0;
+    }
+    for (int i = tid; i < TCNT; i += NT) tcnt[i] = 0;
+    for (int i = tid; i < FL_XENC_ZERO_BYTES; i += NT) zero[i] = 0;
+    fl_fence_mbar_init();
+    __syncthreads();
+
+    /* the weights do not depend on the step's data: start streaming now */
+    if (lane == 0)
+        for (int k = 0; k < R.S; k++) feed(ta, R, f, warp);
+    int cslot = 0;
+    uint32_t cpar = 0;
+
+    float best_v = 0.0f;
+    int best_i = 0x7fffffff;
+    for (int p = 0; p < ta.n_phases; p++) {
+        const int kind = ta.phases[p].kind;
+        /* this phase's arguments into the buffer phase p-2 used (every warp
+         * passed the barrier after it), published by the barrier below */
+        uint8_t* abuf = smem + Ls.args + (size_t)(p & 1) * Ls.args_stride;
+        if (kind == FL_PH_MATVEC) {
+            copy_words(abuf, &ta.phases[p].mv, sizeof(FlMvArgs));
+            if (p + 1 < ta.n_phases && ta.phases[p + 1].kind == FL_PH_ATTN) prefetch_attn_kv(ta.phases[p + 1].at);
+        } else if (kind == FL_PH_ATTN) {
+            copy_words(abuf, &ta.phases[p].at, sizeof(FlAttnArgs));
+        }
+        if (p > 0) grid_sync(ta.bar, p * G, ta.err, ta.cta_done ? ta.cta_done + (size_t)(p - 1) * G + blockIdx.x : nullptr);
+        else consumer_sync();
+        if (ta.timestamps && blockIdx.x == 0 && tid == 0) ta.timestamps[p] = fl_globaltimer();
+        if (kind == FL_PH_EMBED) {
+            phase_embed(ta.phases[p].em, ta.err);
+            continue;
+        }
+        if (kind == FL_PH_ATTN) {
+            phase_attn_t<HD, GMAX>(*reinterpret_cast<const FlAttnArgs*>(abuf), reinterpret_cast<float*>(scratch));
+            continue;
+        }
+        /* ── matvec phase ── */
+        const FlMvArgs& a = *reinterpret_cast<const FlMvArgs*>(abuf);
+        const int n_kb = a.n_kb;
+        uint8_t* xl = scratch;
+        const size_t nc = (size_t)n_kb * 8;
+        short2* xs = reinterpret_cast<short2*>(scratch + nc * FL_XENC_LIMB_BYTES);
+        float* xsum = reinterpret_cast<float*>(scratch + nc * (FL_XENC_LIMB_BYTES + FL_XENC_LSUM_BYTES));
+        Prolog P{a.in_mode, a.K, a.x, a.norm_w, a.pend, a.pend_w, 1.0f, 1.0f};
+        /* normed inputs of up to RK k-blocks per warp stay in registers
+         * between the norm reduction and the encoding */
+        constexpr int RK = 2;
+        const bool in_regs = a.in_mode != FL_IN_PLAIN && n_kb <= RK * NW;
+        float xv[RK][8];
+        float amax;
+        if (a.in_mode == FL_IN_PLAIN) {
+            amax = __ldcg(a.absmax);
+        } else {
+            float ss = 0.0f, mx = 0.0f;
+            if (a.in_mode == FL_IN_GEMMA_RESID) {
+                float sp = 0.0f, dummy = 0.0f;
+                for (int i = tid; i < a.K; i += NC) {
+                    const float v = __ldcg(a.pend + i);
+                    sp = fmaf(v, v, sp);
+                }
+                consumer_sum_max(sp, dummy, misc);
+                P.rms_p = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(sp, (float)a.K), 1e-6f));
+            }
+            if (in_regs) {
+                /* x*w per element (the norm's scale 1/rms is applied after the
+                 * reduction; the 21-bit encoding absorbs the changed rounding) */
+#pragma unroll
+                for (int r = 0; r < RK; r++) {
+                    const int base = (warp + r * NW) * 256 + lane * 8;
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int idx = base + i;
+                        float y = 0.0f;
+                        if (idx < a.K) {
+                            const float xi = a.in_mode == FL_IN_GEMMA_RESID ? P.resid(idx) : __ldcg(a.x + idx);
+                            if (a.in_mode == FL_IN_GEMMA_RESID && blockIdx.x == 0) a.resid_out[idx] = xi;
+                            const float wi = a.in_mode == FL_IN_RMSNORM ? a.norm_w[idx] : __fadd_rn(a.norm_w[idx], 1.0f);
+                            ss = fmaf(xi, xi, ss);
+                            y = xi * wi;
+                            mx = fmaxf(mx, fabsf(y));
+                        }
+                        xv[r][i] = y;
+                    }
+                }
+            } else {
+                for (int i = tid; i < a.K; i += NC) {
+                    const float xi = a.in_mode == FL_IN_GEMMA_RESID ? P.resid(i) : __ldcg(a.x + i);
+                    if (a.in_mode == FL_IN_GEMMA_RESID && blockIdx.x == 0) a.resid_out[i] = xi;
+                    const float wi = a.in_mode == FL_IN_RMSNORM ? a.norm_w[i] : __fadd_rn(a.norm_w[i], 1.0f);
+                    ss = fmaf(xi, xi, ss);
+                    mx = fmaxf(mx, fabsf(xi * wi));
+                }
+            }
+            consumer_sum_max(ss, mx, misc);
+            P.rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps));
+            amax = P.rms * mx * 1.00001f;
+        }
+        const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+        const float xscale = amax / 127.0f;
+        if (in_regs) {
+#pragma unroll
+            for (int r = 0; r < RK; r++) {
+                const int kb = warp + r * NW;
+                if (kb < n_kb) {
+                    float v[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[i] = xv[r][i] * P.rms;
+                    encode_values(v, kb, inv, lane, xl, xs, xsum);
+                }
+            }
+        } else {
+            for (int kb = warp; kb < n_kb; kb += NW) encode_kblock(P, kb, inv, lane, xl, xs, xsum);
+        }
+        consumer_sync();
+        const int pos = a.epi == FL_EPI_QKV ? __ldcg(a.pos) : 0;
+        const int limb = g & 3;
+        const bool bval = (limb < 3) && ((g >> 2) == (t >> 1));
+        const uint8_t* bptr = xl + (limb * 4 + t) * 8;
+        const float wlane = ((t & 1) ? (1.0f / 16384.0f) : 1.0f) * xscale;
+        const int Uph = my_tiles_of(a) * n_kb;
+        const Split S{Uph / NW, Uph % NW};
+        const int lo = S.lo(warp), hi = lo + S.len(warp);
+        const int first_it = lo / n_kb;
+        UnitStats st{0, 0, 0};
+        if (ta.detail && blockIdx.x == 0 && tid == 0) ta.detail[(size_t)ta.n_phases * NW * 4 + p] = fl_globaltimer();
+
+        int i0 = lo;
+        while (i0 < hi) {
+            /* one tile: the units [i0, i1) of this warp's range inside it */
+            const int it = i0 / n_kb;
+            const int i1 = min(hi, (it + 1) * n_kb);
+            const int tile = (int)blockIdx.x + it * G;
+            const int si = seg_of(a, tile);
+            const FlMvSeg& sg = a.seg[si];
+            const int c = i1 - i0, kb0 = i0 - it * n_kb;
+            Acc A{0.0f, 0.0f, 0.0f, 0.0f};
+#define FL_RUN(F, E) run_units<F, E>(ta, R, f, cslot, cpar, c, kb0, bptr, bval, zero, xs, xsum, lane, warp, A, st)
+            if (sg.expanded) {
+                switch (sg.fmt) {
+                case FL_FMT_Q4K: FL_RUN(FL_FMT_Q4K, true); break;
+                case FL_FMT_Q5K: FL_RUN(FL_FMT_Q5K, true); break;
+                case FL_FMT_Q6K: FL_RUN(FL_FMT_Q6K, true); break;
+                default: FL_RUN(FL_FMT_Q8K, true); break;
+                }
+            } else {
+                switch (sg.fmt) {
+                case FL_FMT_Q4K: FL_RUN(FL_FMT_Q4K, false); break;
+                case FL_FMT_Q5K: FL_RUN(FL_FMT_Q5K, false); break;
+                case FL_FMT_Q6K: FL_RUN(FL_FMT_Q6K, false); break;
+                case FL_FMT_Q8_0: FL_RUN(FL_FMT_Q8_0, false); break;
+                case FL_FMT_Q4_0: FL_RUN(FL_FMT_Q4_0, false); break;
+                default: FL_RUN(FL_FMT_Q8K, false); break;
+                }
+            }
+#undef FL_RUN
+            i0 = i1;
+            float v0 = fmaf(A.res0, wlane, -A.m0), v1 = fmaf(A.res1, wlane, -A.m1);
+            v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+            v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+            v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
+            v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+            float v;
+            if (c == n_kb) {
+                /* the whole tile is in this warp: lane r (mod 16) takes row r */
+                const float a0 = __shfl_sync(0xffffffffu, v0, (lane & 7) * 4);
+                const float a1 = __shfl_sync(0xffffffffu, v1, (lane & 7) * 4);
+                v = (lane & 8) ? a1 : a0;
+            } else {
+                /* a tile shared with the neighbouring range(s): outbox slot 0
+                 * holds the partial of the range's first tile, slot 1 its last */
+                float* mine = outbox + ((size_t)warp * 2 + (it == first_it ? 0 : 1)) * 16;
+                if (t == 0) {
+                    mine[g] = v0;
+                    mine[g + 8] = v1;
+                }
+                __threadfence_block();
+                __syncwarp();
+                int last = 0;
+                if (lane == 0) last = atomicAdd(&tcnt[it], c) + c == n_kb;
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (!last) continue;
+                __threadfence_block();
+                const int wa = S.owner(it * n_kb), wb = S.owner((it + 1) * n_kb - 1);
+                v = 0.0f;
+                for (int w = wa; w <= wb; w++) {
+                    const int fw = S.lo(w) / n_kb;
+                    const volatile float* ov = outbox + ((size_t)w * 2 + (it == fw ? 0 : 1)) * 16;
+                    v += ov[lane & 15];
+                }
+                if (lane == 0) tcnt[it] = 0;
+            }
+            epilogue_any(a, sg, si, tile, lane, v, pos, best_v, best_i);
+        }
+        if (ta.detail && blockIdx.x == 0 && lane == 0) {
+            uint64_t* d = ta.detail + ((size_t)p * NW + warp) * 4;
+            d[0] = fl_globaltimer();
+            d[1] = st.wait_cycles;
+            d[2] = st.waits;
+            d[3] = st.units;
+        }
+
+        if (a.epi == FL_EPI_LOGITS) {
+            /* greedy ArgMax (TensorPrimitives.IndexOfMax): per CTA, then across CTAs */
+            __shared__ int s_last;
+            if (lane == 0) {
+                best[warp * 2] = best_v;
+                best[warp * 2 + 1] = __int_as_float(best_i);
+            }
+            consumer_sync();
+            if (tid == 0) {
+                float bv = 0.0f;
+                int bi = 0x7fffffff;
+                for (int w = 0; w < NW; w++) {
+                    const float bw = best[w * 2];
+                    const int iw = __float_as_int(best[w * 2 + 1]);
+                    if (iw != 0x7fffffff && (bi == 0x7fffffff || fl_argmax_better(bw, iw, bv, bi))) {
+                        bv = bw;
+                        bi = iw;
+                    }
+                }
+                a.cta_best[blockIdx.x * 2] = bv;
+                a.cta_best[blockIdx.x * 2 + 1] = __int_as_float(bi);
+                __threadfence();
+                s_last = atomicAdd(a.counter, 1) == G - 1;
+            }
+            consumer_sync();
+            if (s_last && warp == 0) {
+                __threadfence();
+                float bv = 0.0f;
+                int bi = 0x7fffffff;
+                for (int b = lane; b < G; b += 32) {
+                    const float bw = __ldcg(&a.cta_best[b * 2]);
+                    const int iw = __float_as_int(__ldcg(&a.cta_best[b * 2 + 1]));
+                    if (iw != 0x7fffffff && (bi == 0x7fffffff || fl_argmax_better(bw, iw, bv, bi))) {
+                        bv = bw;
+                        bi = iw;
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (oi != 0x7fffffff && (bi == 0x7fffffff || fl_argmax_better(ov, oi, bv, bi))) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                if (lane == 0) {
+                    *a.argmax_out = bi;
+                    *a.counter = 0;
+                    /* the device-resident decode loop: next token, next position */
+                    if (ta.advance) {
+                        const int s = __ldcg(ta.step);
+                        if (ta.out_tokens) ta.out_tokens[s] = bi;
+                        *ta.step = s + 1;
+                        *ta.token = bi;
+                        *ta.pos = __ldcg(ta.pos) + 1;
+                    }
+                    if (ta.timestamps) ta.timestamps[ta.n_phases] = fl_globaltimer();
+                }
+            }
+        }
+    }
+}
+
+/* Kernel of the (head_dim, largest group) instances compiled in this unit. */
+template <int HD, int GMAX>
+const void* kernel_ptr()
+{
+    return reinterpret_cast<const void*>(fl_token_kernel<HD, GMAX>);
+}
+
+} // namespace
+} // namespace fltk
+
+#endif
