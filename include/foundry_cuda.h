@@ -2,7 +2,7 @@
  * foundry_cuda.h — C ABI of the B200 token-loop backend for DotNetFoundryLLM.
  *
  * Plain C: opaque handles, pointers and sizes; no CUDA or torch types.  The
- * C# side binds these with [LibraryImport].
+ * C# side binds these with [LibraryImport] in a CudaForwardPass : IForwardPass.
  *
  * Each entry point names the reference interface it replaces (paths inside
  * justinamiller/DotNetFoundryLLM v1.0.0).
@@ -144,9 +144,11 @@ int fl_dequant(int32_t ggml_type, const void* src, uint64_t nbytes, float* dst, 
 int fl_matvec(int32_t ggml_type, const void* w, uint64_t nbytes, int32_t rows, int32_t cols, const float* x,
               float* y);
 
-/* Timing helpers for the benchmark: run the token step eagerly with CUDA
- * events around each kernel class on the session stream; fills
- * ms[class] and bytes[class] (algorithmic bytes) for FL_PROF_* classes. */
+/* Timing helpers for the benchmark: runs one token step and reads the
+ * device timestamps the token kernel takes at every phase boundary; fills
+ * ms[class] (time spent in phases of that class) and bytes[class]
+ * (algorithmic bytes) for the FL_PROF_* classes, and *launches with the
+ * kernels one step launches. */
 #define FL_PROF_MATVEC 0
 #define FL_PROF_ATTN 1
 #define FL_PROF_OTHER 2

@@ -13,7 +13,9 @@
  * every known-answer vector the reference's own xUnit tests hold
  * (tests/golden/reference_kats.json).  Q6_K/Q8_K, non-zero K-quant blocks
  * and forward-pass logits are not pinned by any reference test; for those the
- * restatement is the golden (see the parity notes in DESIGN.md).
+ * restatement is the golden (parity unpinned: it follows the reference's
+ * operation order, and the reference's TensorPrimitives reductions are
+ * ISA-dependent, so forward-pass parity is judged by tolerance).
  */
 #ifndef FL_ORACLE_H
 #define FL_ORACLE_H
