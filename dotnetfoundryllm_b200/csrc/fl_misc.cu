@@ -9,6 +9,7 @@
 #include "fl_dequant.cuh"
 #include "fl_device.cuh"
 #include "fl_kernels.h"
+#include "../../include/foundry_cuda.h"
 
 namespace {
 
@@ -119,4 +120,25 @@ cudaError_t fl_launch_topk(const float* logits, int32_t n, int32_t k, int32_t* i
     int* ci = reinterpret_cast<int*>(scratch + (size_t)cap * 4);
     fl_topk_kernel<<<1, 1024, 0, st>>>(logits, n, k, ids, vals, ck, ci, cap);
     return cudaGetLastError();
+}
+
+/* Scratch of fl_topk_device: candidate keys and indices for n <= FL_TOPK_DEVICE_MAX_N. */
+static __device__ __align__(256) uint8_t g_topk_device_scratch[(size_t)FL_TOPK_DEVICE_MAX_N * 8];
+
+cudaError_t fl_launch_topk_static(const float* logits, int32_t n, int32_t k, int32_t* ids, float* vals,
+                                  cudaStream_t st)
+{
+    /* address of the scratch per device, looked up on the first call */
+    static void* addr[FL_MAX_DEVICES] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= FL_MAX_DEVICES) return cudaErrorInvalidDevice;
+    void* p = __atomic_load_n(&addr[dev], __ATOMIC_ACQUIRE);
+    if (!p) {
+        e = cudaGetSymbolAddress(&p, g_topk_device_scratch);
+        if (e != cudaSuccess) return e;
+        __atomic_store_n(&addr[dev], p, __ATOMIC_RELEASE);
+    }
+    return fl_launch_topk(logits, n, k, ids, vals, static_cast<uint8_t*>(p), (size_t)FL_TOPK_DEVICE_MAX_N * 8, st);
 }

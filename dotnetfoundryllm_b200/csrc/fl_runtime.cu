@@ -943,6 +943,17 @@ extern "C" int fl_topk(fl_session* s, int32_t k, int32_t* ids, float* vals, floa
     return FL_OK;
 }
 
+extern "C" int fl_topk_device(const float* logits, int32_t n, int32_t k, int32_t* ids, float* vals, void* stream)
+{
+    if (!logits || !ids || !vals) return fail(FL_ERR_ARG, "null argument");
+    if (n < 1 || n > FL_TOPK_DEVICE_MAX_N)
+        return fail(FL_ERR_ARG, "n = %d is outside [1, %d], the size of the static top-k scratch", n,
+                    FL_TOPK_DEVICE_MAX_N);
+    if (k < 1 || k > n) return fail(FL_ERR_ARG, "k must be in [1, %d]", n);
+    CK(fl_launch_topk_static(logits, n, k, ids, vals, static_cast<cudaStream_t>(stream)));
+    return FL_OK;
+}
+
 /* ── stateless helpers ──────────────────────────────────────────────────── */
 extern "C" int fl_dequant(int32_t type, const void* src, uint64_t nbytes, float* dst, uint64_t dst_len)
 {

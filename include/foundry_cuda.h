@@ -131,6 +131,25 @@ int fl_topk(fl_session* s, int32_t k, int32_t* ids, float* vals, float* threshol
 
 void fl_session_destroy(fl_session* s);
 
+/* Allocation-free top-k.  No counterpart in the reference: its sampler works
+ * on a managed logits array (TopKSampler.ApplyTopK, TopKSampler.cs:42-71);
+ * this entry point serves callers that keep logits on the device and must not
+ * allocate per call.  Same selection and order as fl_topk (value descending,
+ * index ascending): logits, ids and vals are DEVICE pointers (n floats in, k
+ * ints and k floats out), enqueued on `stream` (a cudaStream_t; NULL = the
+ * legacy default stream) without synchronizing.
+ * - Scratch: a file-scope device array of FL_TOPK_DEVICE_MAX_N * 8 bytes
+ *   (2 MiB) per device; n > FL_TOPK_DEVICE_MAX_N returns FL_ERR_ARG.  Nothing
+ *   in it has to start at zero.  No cudaMalloc, cudaFree or allocating library
+ *   call is made.
+ * - The first call on each device looks the scratch address up
+ *   (cudaGetSymbolAddress); make that first call outside any stream capture.
+ * - All calls on one device share the scratch: calls that overlap in time
+ *   (different streams or threads, or a call whose previous kernel has not
+ *   finished on another stream) race and may return wrong results. */
+#define FL_TOPK_DEVICE_MAX_N 262144
+int fl_topk_device(const float* logits, int32_t n, int32_t k, int32_t* ids, float* vals, void* stream);
+
 /* Dequantizer.Dequantize (Dequantizer.cs:488-504) on the device, bit-exact:
  * src is host memory with whole blocks, dst receives the F32 values.
  * Returns FL_ERR_ARG for a length that is not a multiple of the block size or a
