@@ -116,7 +116,8 @@ struct FlAttnArgs {
 #define FL_TK_WARPS 16
 #define FL_TK_MAX_TILES 256      /* 16-row tiles of one matvec phase per CTA */
 
-enum { FL_PH_EMBED = 0, FL_PH_MATVEC = 1, FL_PH_ATTN = 2 };
+/* FL_PH_ATTN writes per-split partials; FL_PH_ATTN_COMBINE merges them (same args). */
+enum { FL_PH_EMBED = 0, FL_PH_MATVEC = 1, FL_PH_ATTN = 2, FL_PH_ATTN_COMBINE = 3 };
 
 struct FlPhase {
     int32_t kind;
@@ -126,8 +127,18 @@ struct FlPhase {
     FlEmbedArgs em;
 };
 
+/* What the weight stream needs of one matvec phase, in one 64-byte line. */
+struct __align__(64) FlFeedPhase {
+    int32_t n_kb, n_tiles, n_seg, pad;
+    int32_t tile0[FL_MV_MAX_SEG];
+    int32_t unit_bytes[FL_MV_MAX_SEG];
+    const uint8_t* w[FL_MV_MAX_SEG];
+};
+
 struct FlTokenArgs {
     const FlPhase* phases;       /* device array */
+    const FlFeedPhase* feed;     /* [n_feed] the matvec phases, in order */
+    int32_t n_feed;
     int32_t n_phases;
     int32_t n_slots, slot_bytes; /* weight ring */
     size_t scratch_bytes;        /* x encoding / attention scratch */

@@ -103,6 +103,7 @@ struct fl_session {
     int attn_split = 1;
     /* the token step: phase list + persistent kernel configuration */
     FlPhase* d_phases = nullptr;
+    FlFeedPhase* d_feed = nullptr;
     int n_phases = 0;
     std::vector<int> phase_cls;
     std::vector<double> phase_bytes;
@@ -541,6 +542,10 @@ static void build_phases(fl_session* s, PhaseList& P)
         P.ph.push_back(at);
         P.cls.push_back(CLS_ATTN);
         P.bytes.push_back(0.0);
+        at.kind = FL_PH_ATTN_COMBINE;
+        P.ph.push_back(at);
+        P.cls.push_back(CLS_ATTN);
+        P.bytes.push_back(0.0);
 
         /* output projection + residual (Gemma: post-attention norm first) */
         a = base_args(s, L.wo, qd);
@@ -684,7 +689,23 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     s->n_phases = (int)P.ph.size();
     s->phase_cls = P.cls;
     s->phase_bytes = P.bytes;
+    std::vector<FlFeedPhase> feed;
+    for (const FlPhase& p : P.ph)
+        if (p.kind == FL_PH_MATVEC) {
+            FlFeedPhase f;
+            memset(&f, 0, sizeof f);
+            f.n_kb = p.mv.n_kb;
+            f.n_tiles = p.mv.n_tiles;
+            f.n_seg = p.mv.n_seg;
+            for (int i = 0; i < p.mv.n_seg; i++) {
+                f.tile0[i] = p.mv.seg[i].tile0;
+                f.unit_bytes[i] = p.mv.seg[i].unit_bytes;
+                f.w[i] = p.mv.seg[i].w;
+            }
+            feed.push_back(f);
+        }
     rc = dalloc(s->allocs, &s->d_phases, P.ph.size() * sizeof(FlPhase));
+    if (!rc) rc = dalloc(s->allocs, &s->d_feed, feed.size() * sizeof(FlFeedPhase));
     if (!rc) rc = dalloc(s->allocs, &s->timestamps, (P.ph.size() + 1) * 8);
     if (!rc) rc = dalloc(s->allocs, &s->cta_done, P.ph.size() * (size_t)G * 8);
     if (!rc) rc = dalloc(s->allocs, &s->detail, P.ph.size() * (size_t)(FL_TK_WARPS * 4 + 1) * 8);
@@ -721,6 +742,8 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     FlTokenArgs& ta = s->ta;
     memset(&ta, 0, sizeof ta);
     ta.phases = s->d_phases;
+    ta.feed = s->d_feed;
+    ta.n_feed = (int)feed.size();
     ta.n_phases = s->n_phases;
     ta.n_slots = n_slots;
     ta.slot_bytes = slot;
@@ -746,6 +769,7 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
         return fail(FL_ERR_UNSUPPORTED, "the token kernel does not fit one CTA per SM");
     }
     cudaMemcpyAsync(s->d_phases, P.ph.data(), P.ph.size() * sizeof(FlPhase), cudaMemcpyHostToDevice, s->st);
+    cudaMemcpyAsync(s->d_feed, feed.data(), feed.size() * sizeof(FlFeedPhase), cudaMemcpyHostToDevice, s->st);
     cudaMemsetAsync(s->state, 0, ST_N * 4, s->st);
     cudaMemsetAsync(s->attn_counter, 0, (size_t)d.n_kv_heads * 4, s->st);
     cudaMemsetAsync(s->kc, 0, kv_bytes, s->st);

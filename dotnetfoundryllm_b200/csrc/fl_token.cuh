@@ -156,6 +156,35 @@ struct Split {
     }
 };
 
+/* 8 consecutive floats p[base .. base+8) (zero beyond n), one vector load
+ * pair when they are all in range: through L2 (data written by an earlier
+ * phase) or through the read-only path (weights). */
+__device__ __forceinline__ void load8_cg(const float* p, int base, int n, float (&o)[8])
+{
+    if (base + 8 <= n) {
+        const float4 u = __ldcg(reinterpret_cast<const float4*>(p + base));
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(p + base) + 1);
+        o[0] = u.x; o[1] = u.y; o[2] = u.z; o[3] = u.w;
+        o[4] = v.x; o[5] = v.y; o[6] = v.z; o[7] = v.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = base + i < n ? __ldcg(p + base + i) : 0.0f;
+    }
+}
+
+__device__ __forceinline__ void load8(const float* p, int base, int n, float (&o)[8])
+{
+    if (base + 8 <= n) {
+        const float4 u = __ldg(reinterpret_cast<const float4*>(p + base));
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p + base) + 1);
+        o[0] = u.x; o[1] = u.y; o[2] = u.z; o[3] = u.w;
+        o[4] = v.x; o[5] = v.y; o[6] = v.z; o[7] = v.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = base + i < n ? __ldg(p + base + i) : 0.0f;
+    }
+}
+
 /* ── phases ─────────────────────────────────────────────────────────────── */
 
 __device__ void phase_embed(const FlEmbedArgs& e, int* err)
@@ -217,8 +246,8 @@ __device__ __forceinline__ void load_row_smem(const float* p, float (&v)[PER])
  *     CTA-wide maximum and the softmax weights exp(s - max) of every score;
  *  2. values: lanes own head_dim/32 dims, warps split the keys, the weights
  *     come from shared memory; the warps' sums are added in warp order.
- * The item's (max, sum, unnormalized output) goes to global memory; the last
- * item of a kv head merges the splits in split order.
+ * The item's (max, sum, unnormalized output) goes to global memory; the
+ * combine phase merges the splits.
  * ComputeAttention: LlamaForwardPass.cs:158-211; MistralForwardPass.cs:186-240;
  * Gemma2ForwardPass.cs:126-185. */
 template <int HD, int GMAX>
@@ -235,7 +264,6 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr)
     float* sacc = sq + grp * HD;          /* [NW][grp][HD] */
     float* sred = sacc + NW * grp * HD;   /* [NW][GMAX] */
     float* sp = sred + NW * GMAX;         /* [keys][grp] scores, then weights */
-    __shared__ int s_last;
     __shared__ float s_M[8], s_L[8];
     const int seq = __ldcg(a.pos) + 1;
     int start = 0;
@@ -369,51 +397,58 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr)
                 part[h * (HD + 2) + 1] = s_L[h];
             }
         }
-        __threadfence();
-        consumer_sync();
-        if (threadIdx.x == 0) s_last = atomicAdd(&a.counter[kvh], 1) == a.n_split - 1;
-        consumer_sync();
-        if (s_last) {
-            __threadfence();
-            /* merge the splits: stage (m, l) of every split, then the weighted sum */
-            const float* pk = a.part + (size_t)kvh * a.n_split * grp * (HD + 2);
-            float* w_s = sacc;                         /* [n_split][grp] maxima, then weights */
-            float* l_s = sacc + a.n_split * grp;       /* [n_split][grp] sums */
-            for (int i = threadIdx.x; i < a.n_split * grp; i += NC) {
-                w_s[i] = __ldcg(&pk[(size_t)i * (HD + 2)]);
-                l_s[i] = __ldcg(&pk[(size_t)i * (HD + 2) + 1]);
+        consumer_sync(); /* the item's shared memory is reused by the next item */
+    }
+}
+
+/* The combine phase: query head hq's output from its splits' partials (one
+ * CTA per query head, NC/HD threads per output element, split order kept),
+ * plus the |max| the next projection's encoding needs. */
+template <int HD, int GMAX>
+__device__ void phase_attn_combine(const FlAttnArgs& a, float* scr)
+{
+    constexpr int TPO = NC / HD; /* threads per output dim */
+    const int grp = a.n_heads / a.n_kv, S = a.n_split;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t sstride = (size_t)grp * (HD + 2);
+    float* w_s = scr;             /* [S] split weights, [S] = total weight */
+    float* red = scr + S + 1;     /* [TPO][HD] */
+    for (int hq = blockIdx.x; hq < a.n_heads; hq += gridDim.x) {
+        const int kvh = hq / grp, h = hq % grp;
+        const float* base = a.part + ((size_t)kvh * S * grp + h) * (HD + 2);
+        if (warp == 0) {
+            float M = -INFINITY;
+            for (int s = lane; s < S; s += 32) M = fmaxf(M, __ldcg(base + s * sstride));
+            M = fl_warp_max(M);
+            float L = 0.0f;
+            for (int s = lane; s < S; s += 32) {
+                const float ms = __ldcg(base + s * sstride);
+                const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
+                w_s[s] = f;
+                L = fmaf(__ldcg(base + s * sstride + 1), f, L);
             }
-            consumer_sync();
-            if (threadIdx.x < grp) {
-                const int h = threadIdx.x;
-                float M = -INFINITY;
-                for (int s = 0; s < a.n_split; s++) M = fmaxf(M, w_s[s * grp + h]);
-                float Ls = 0.0f;
-                for (int s = 0; s < a.n_split; s++) {
-                    const float ms = w_s[s * grp + h];
-                    const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
-                    Ls = fmaf(l_s[s * grp + h], f, Ls);
-                    w_s[s * grp + h] = f;
-                }
-                s_L[h] = Ls;
-            }
-            consumer_sync();
-            float amax = 0.0f;
-            for (int i = threadIdx.x; i < grp * HD; i += NC) {
-                const int h = i / HD, d = i % HD;
-                float O = 0.0f;
-#pragma unroll 16
-                for (int s = 0; s < a.n_split; s++)
-                    O = fmaf(__ldcg(&pk[((size_t)s * grp + h) * (HD + 2) + 2 + d]), w_s[s * grp + h], O);
-                const float ov = s_L[h] > 0.0f ? O / s_L[h] : 0.0f;
-                a.out[((size_t)kvh * grp + h) * HD + d] = ov;
-                amax = fmaxf(amax, fabsf(ov));
-            }
-            amax = fl_warp_max(amax);
-            if (lane == 0) atomicMax(reinterpret_cast<int*>(a.out_absmax), __float_as_int(amax));
-            if (threadIdx.x == 0) a.counter[kvh] = 0;
+            L = fl_warp_sum(L);
+            if (lane == 0) w_s[S] = L;
         }
         consumer_sync();
+        const int d = threadIdx.x % HD, j = threadIdx.x / HD;
+        float O = 0.0f;
+        for (int s = j; s < S; s += TPO) O = fmaf(__ldcg(base + s * sstride + 2 + d), w_s[s], O);
+        red[j * HD + d] = O;
+        consumer_sync();
+        float amax = 0.0f;
+        if (j == 0) {
+            float t = 0.0f;
+#pragma unroll
+            for (int q = 0; q < TPO; q++) t += red[q * HD + d];
+            const float L = w_s[S];
+            const float ov = L > 0.0f ? t / L : 0.0f;
+            a.out[(size_t)hq * HD + d] = ov;
+            amax = fabsf(ov);
+        }
+        amax = fl_warp_max(amax);
+        if (lane == 0 && warp * 32 < HD) atomicMax(reinterpret_cast<int*>(a.out_absmax), __float_as_int(amax));
+        consumer_sync(); /* w_s and red are reused by the next head */
     }
 }
 
@@ -456,42 +491,53 @@ __device__ __forceinline__ int my_tiles_of(const FlMvArgs& a)
 }
 
 /* Moves the cursor to the warp's next run of units: the next tile of its
- * range in the current phase, or the start of its range in the next matvec
- * phase.  False once every unit has been issued. */
+ * range in the current matvec phase, or the start of its range in the next
+ * one (F.p indexes ta.feed, the matvec phases in order).  False once every
+ * unit has been issued. */
 __device__ __forceinline__ bool feed_advance(const FlTokenArgs& ta, FeedState& F, int warp)
 {
     int kb = 0;
+    const FlFeedPhase* fp = ta.feed + (F.p < 0 ? 0 : F.p);
     if (F.left > 0) {
         F.it++;
     } else {
         for (;;) {
-            if (F.p + 1 >= ta.n_phases) {
-                F.p = ta.n_phases;
+            if (F.p + 1 >= ta.n_feed) {
+                F.p = ta.n_feed;
                 return false;
             }
             F.p++;
-            if (ta.phases[F.p].kind != FL_PH_MATVEC) continue;
-            const FlMvArgs& a = ta.phases[F.p].mv;
-            const int U = my_tiles_of(a) * a.n_kb;
+            fp = ta.feed + F.p;
+            const int G = gridDim.x;
+            const int tiles = fp->n_tiles > (int)blockIdx.x ? (fp->n_tiles - (int)blockIdx.x + G - 1) / G : 0;
+            const int U = tiles * fp->n_kb;
             const Split S{U / NW, U % NW};
             const int len = S.len(warp);
             if (len == 0) continue;
             const int lo = S.lo(warp);
-            F.it = lo / a.n_kb;
-            kb = lo - F.it * a.n_kb;
+            F.it = lo / fp->n_kb;
+            kb = lo - F.it * fp->n_kb;
             F.left = len;
             break;
         }
     }
-    const FlMvArgs& a = ta.phases[F.p].mv;
-    const int n_kb = a.n_kb;
+    const int n_kb = fp->n_kb;
     const int run = min(n_kb - kb, F.left);
     F.left -= run;
     F.run = run;
     const int tile = (int)blockIdx.x + F.it * (int)gridDim.x;
-    const FlMvSeg& sg = a.seg[seg_of(a, tile)];
-    F.bytes = (uint32_t)sg.unit_bytes;
-    F.src = sg.w + ((size_t)(tile - sg.tile0) * n_kb + kb) * F.bytes;
+    const int n_seg = fp->n_seg;
+    int t0 = fp->tile0[0], ub = fp->unit_bytes[0];
+    const uint8_t* w = fp->w[0];
+#pragma unroll
+    for (int i = 1; i < FL_MV_MAX_SEG; i++)
+        if (i < n_seg && tile >= fp->tile0[i]) {
+            t0 = fp->tile0[i];
+            ub = fp->unit_bytes[i];
+            w = fp->w[i];
+        }
+    F.bytes = (uint32_t)ub;
+    F.src = w + ((size_t)(tile - t0) * n_kb + kb) * F.bytes;
     return true;
 }
 
@@ -592,7 +638,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         if (kind == FL_PH_MATVEC) {
             copy_words(abuf, &ta.phases[p].mv, sizeof(FlMvArgs));
             if (p + 1 < ta.n_phases && ta.phases[p + 1].kind == FL_PH_ATTN) prefetch_attn_kv(ta.phases[p + 1].at);
-        } else if (kind == FL_PH_ATTN) {
+        } else if (kind == FL_PH_ATTN || kind == FL_PH_ATTN_COMBINE) {
             copy_words(abuf, &ta.phases[p].at, sizeof(FlAttnArgs));
         }
         if (p > 0) grid_sync(ta.bar, p * G, ta.err, ta.cta_done ? ta.cta_done + (size_t)(p - 1) * G + blockIdx.x : nullptr);
@@ -606,6 +652,10 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
             phase_attn_t<HD, GMAX>(*reinterpret_cast<const FlAttnArgs*>(abuf), reinterpret_cast<float*>(scratch));
             continue;
         }
+        if (kind == FL_PH_ATTN_COMBINE) {
+            phase_attn_combine<HD, GMAX>(*reinterpret_cast<const FlAttnArgs*>(abuf), reinterpret_cast<float*>(scratch));
+            continue;
+        }
         /* ── matvec phase ── */
         const FlMvArgs& a = *reinterpret_cast<const FlMvArgs*>(abuf);
         const int n_kb = a.n_kb;
@@ -614,17 +664,18 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         short2* xs = reinterpret_cast<short2*>(scratch + nc * FL_XENC_LIMB_BYTES);
         float* xsum = reinterpret_cast<float*>(scratch + nc * (FL_XENC_LIMB_BYTES + FL_XENC_LSUM_BYTES));
         Prolog P{a.in_mode, a.K, a.x, a.norm_w, a.pend, a.pend_w, 1.0f, 1.0f};
-        /* normed inputs of up to RK k-blocks per warp stay in registers
-         * between the norm reduction and the encoding */
-        constexpr int RK = 2;
-        const bool in_regs = a.in_mode != FL_IN_PLAIN && n_kb <= RK * NW;
-        float xv[RK][8];
+        /* The warp's k-blocks are kb = warp + r*NW; lane l encodes inputs
+         * kb*256 + 8l .. +8.  With up to RK k-blocks per warp every input load
+         * of the prologue is issued at once and the values stay in registers
+         * until they are encoded. */
+        constexpr int RK = 4;
+        const bool in_regs = n_kb <= RK * NW;
         float amax;
-        if (a.in_mode == FL_IN_PLAIN) {
-            amax = __ldcg(a.absmax);
-        } else {
-            float ss = 0.0f, mx = 0.0f;
-            if (a.in_mode == FL_IN_GEMMA_RESID) {
+        if (in_regs) {
+            const int mode = a.in_mode;
+            float xv[RK][8];
+            const float am_plain = mode == FL_IN_PLAIN ? __ldcg(a.absmax) : 0.0f;
+            if (mode == FL_IN_GEMMA_RESID) {
                 float sp = 0.0f, dummy = 0.0f;
                 for (int i = tid; i < a.K; i += NC) {
                     const float v = __ldcg(a.pend + i);
@@ -633,28 +684,76 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                 consumer_sum_max(sp, dummy, misc);
                 P.rms_p = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(sp, (float)a.K), 1e-6f));
             }
-            if (in_regs) {
-                /* x*w per element (the norm's scale 1/rms is applied after the
-                 * reduction; the 21-bit encoding absorbs the changed rounding) */
+#pragma unroll
+            for (int r = 0; r < RK; r++) {
+                const int base = (warp + r * NW) * 256 + lane * 8;
+                load8_cg(a.x, base, a.K, xv[r]);
+            }
+            if (mode == FL_IN_PLAIN) {
+                amax = am_plain;
+            } else {
+                float ss = 0.0f, mx = 0.0f;
 #pragma unroll
                 for (int r = 0; r < RK; r++) {
                     const int base = (warp + r * NW) * 256 + lane * 8;
+                    if (base >= a.K) continue;
+                    float w[8];
+                    load8(a.norm_w, base, a.K, w);
+                    if (mode == FL_IN_GEMMA_RESID) {
+                        /* x' = x + GemmaRmsNorm(pend, pend_w), kept by CTA 0 */
+                        float pe[8], pw[8];
+                        load8_cg(a.pend, base, a.K, pe);
+                        load8(a.pend_w, base, a.K, pw);
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+                            xv[r][i] = __fadd_rn(xv[r][i], __fmul_rn(__fmul_rn(pe[i], P.rms_p), __fadd_rn(pw[i], 1.0f)));
+                        if (blockIdx.x == 0)
+#pragma unroll
+                            for (int i = 0; i < 8; i++)
+                                if (base + i < a.K) a.resid_out[base + i] = xv[r][i];
+                    }
 #pragma unroll
                     for (int i = 0; i < 8; i++) {
-                        const int idx = base + i;
-                        float y = 0.0f;
-                        if (idx < a.K) {
-                            const float xi = a.in_mode == FL_IN_GEMMA_RESID ? P.resid(idx) : __ldcg(a.x + idx);
-                            if (a.in_mode == FL_IN_GEMMA_RESID && blockIdx.x == 0) a.resid_out[idx] = xi;
-                            const float wi = a.in_mode == FL_IN_RMSNORM ? a.norm_w[idx] : __fadd_rn(a.norm_w[idx], 1.0f);
-                            ss = fmaf(xi, xi, ss);
-                            y = xi * wi;
-                            mx = fmaxf(mx, fabsf(y));
-                        }
-                        xv[r][i] = y;
+                        const float xi = xv[r][i];
+                        const float wi = mode == FL_IN_RMSNORM ? w[i] : __fadd_rn(w[i], 1.0f);
+                        ss = fmaf(xi, xi, ss);
+                        /* x*w per element; the norm's 1/rms scales it after the
+                         * reduction (the 21-bit encoding absorbs the rounding) */
+                        xv[r][i] = base + i < a.K ? xi * wi : 0.0f;
+                        mx = fmaxf(mx, fabsf(xv[r][i]));
                     }
                 }
+                consumer_sum_max(ss, mx, misc);
+                P.rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps));
+                amax = P.rms * mx * 1.00001f;
+            }
+            const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
+            const float scale = mode == FL_IN_PLAIN ? 1.0f : P.rms;
+#pragma unroll
+            for (int r = 0; r < RK; r++) {
+                const int kb = warp + r * NW;
+                if (kb < n_kb) {
+                    float v[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[i] = xv[r][i] * scale;
+                    encode_values(v, kb, inv, lane, xl, xs, xsum);
+                }
+            }
+        } else {
+            /* long inputs: one k-block at a time */
+            if (a.in_mode == FL_IN_PLAIN) {
+                amax = __ldcg(a.absmax);
             } else {
+                float ss = 0.0f, mx = 0.0f;
+                if (a.in_mode == FL_IN_GEMMA_RESID) {
+                    float sp = 0.0f, dummy = 0.0f;
+                    for (int i = tid; i < a.K; i += NC) {
+                        const float v = __ldcg(a.pend + i);
+                        sp = fmaf(v, v, sp);
+                    }
+                    consumer_sum_max(sp, dummy, misc);
+                    P.rms_p = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(sp, (float)a.K), 1e-6f));
+                }
                 for (int i = tid; i < a.K; i += NC) {
                     const float xi = a.in_mode == FL_IN_GEMMA_RESID ? P.resid(i) : __ldcg(a.x + i);
                     if (a.in_mode == FL_IN_GEMMA_RESID && blockIdx.x == 0) a.resid_out[i] = xi;
@@ -662,27 +761,14 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                     ss = fmaf(xi, xi, ss);
                     mx = fmaxf(mx, fabsf(xi * wi));
                 }
+                consumer_sum_max(ss, mx, misc);
+                P.rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps));
+                amax = P.rms * mx * 1.00001f;
             }
-            consumer_sum_max(ss, mx, misc);
-            P.rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps));
-            amax = P.rms * mx * 1.00001f;
-        }
-        const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
-        const float xscale = amax / 127.0f;
-        if (in_regs) {
-#pragma unroll
-            for (int r = 0; r < RK; r++) {
-                const int kb = warp + r * NW;
-                if (kb < n_kb) {
-                    float v[8];
-#pragma unroll
-                    for (int i = 0; i < 8; i++) v[i] = xv[r][i] * P.rms;
-                    encode_values(v, kb, inv, lane, xl, xs, xsum);
-                }
-            }
-        } else {
+            const float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
             for (int kb = warp; kb < n_kb; kb += NW) encode_kblock(P, kb, inv, lane, xl, xs, xsum);
         }
+        const float xscale = amax / 127.0f;
         consumer_sync();
         const int pos = a.epi == FL_EPI_QKV ? __ldcg(a.pos) : 0;
         const int limb = g & 3;
