@@ -286,7 +286,7 @@ def run_ours(args, ws, rank, local):
         cpu = {"tok_s": None, "threads": 0} if args.no_cpu_baseline else cpu_sample(img, pos_timed)
         traffic = None
         tf = ROOT / "profiles" / "traffic.json"
-        if tf.exists():
+        if tf.exists() and not args.layers and args.prompt == PROMPT:
             traffic = json.loads(tf.read_text()).get(CONFIG)
         result = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
