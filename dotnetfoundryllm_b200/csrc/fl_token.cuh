@@ -87,27 +87,27 @@ __device__ __forceinline__ int ld_acquire(const int* p)
     return v;
 }
 
-/* All CTAs finish phase k before any starts phase k+1.  Bounded: gives up after
+/* All CTAs finish phase k before any starts phase k+1.  Thread 0 arrives with
+ * a release reduction (cumulative over the CTA's writes, ordered before it by
+ * the CTA barrier) and polls with acquire loads.  Bounded: gives up after
  * ~2 s, records a timeout and lets the kernel run to its end. */
 __device__ void grid_sync(int* bar, int target, int* err, uint64_t* done_stamp)
 {
     consumer_sync();
     if (threadIdx.x == 0) {
         if (done_stamp) *done_stamp = fl_globaltimer();
-        __threadfence();
-        atomicAdd(bar, 1);
+        asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(bar) : "memory");
         if (ld_acquire(bar) < target) {
             const uint64_t t0 = fl_globaltimer();
             for (uint32_t it = 0;; it++) {
                 if (ld_acquire(bar) >= target) break;
-                __nanosleep(64);
-                if ((it & 63u) == 0 && (fl_globaltimer() - t0 > 2000000000ull || it > (1u << 26))) {
+                if (it > 256) __nanosleep(32);
+                if ((it & 255u) == 0 && (fl_globaltimer() - t0 > 2000000000ull || it > (1u << 26))) {
                     atomicExch(err, FL_DEV_ERR_TIMEOUT);
                     break;
                 }
             }
         }
-        __threadfence();
     }
     consumer_sync();
 }
@@ -251,8 +251,11 @@ __device__ __forceinline__ void load_row_smem(const float* p, float (&v)[PER])
  * ComputeAttention: LlamaForwardPass.cs:158-211; MistralForwardPass.cs:186-240;
  * Gemma2ForwardPass.cs:126-185. */
 template <int HD, int GMAX>
-__device__ void phase_attn_t(const FlAttnArgs& a, float* scr)
+__device__ void phase_attn_t(const FlAttnArgs& a, float* scr, uint64_t* stamps)
 {
+    /* profiling: CTA 0 records the end of each step of its first item */
+#define FL_STAMP(i) \
+    if (stamps && threadIdx.x == 0 && item == (int)blockIdx.x) stamps[i] = fl_globaltimer()
     const int grp = a.n_heads / a.n_kv; /* query heads per kv head, <= GMAX */
     constexpr int LPK = HD / 32;  /* lanes per key in pass 1, 8 float4 chunks each */
     constexpr int KPW = 32 / LPK; /* keys per warp per round */
@@ -277,6 +280,7 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr)
         const int n = max(0, min(seq, k0 + per) - k0);
         for (int i = threadIdx.x; i < grp * HD; i += NC) sq[i] = __ldcg(a.q + (size_t)kvh * grp * HD + i);
         consumer_sync();
+        FL_STAMP(0);
 
         /* pass 1: scores */
         float mloc[GMAX];
@@ -319,38 +323,29 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr)
                 }
             }
         }
+        FL_STAMP(1);
 #pragma unroll
         for (int h = 0; h < GMAX; h++) {
             const float m = fl_warp_max(mloc[h]);
             if (lane == 0) sred[warp * GMAX + h] = m;
         }
         consumer_sync();
+        FL_STAMP(2);
         if (threadIdx.x < grp) {
             float M = -INFINITY;
             for (int w = 0; w < NW; w++) M = fmaxf(M, sred[w * GMAX + threadIdx.x]);
             s_M[threadIdx.x] = M;
         }
         consumer_sync();
-        /* softmax weights exp(s - max) and their sums, head by head */
-        for (int h = 0; h < grp; h++) {
-            const float M = s_M[h];
-            float l = 0.0f;
-            for (int t = threadIdx.x; t < n; t += NC) {
-                const float p = __expf(sp[t * grp + h] - M);
-                sp[t * grp + h] = p;
-                l += p;
-            }
-            l = fl_warp_sum(l);
-            if (lane == 0) sred[warp * GMAX + h] = l;
+        FL_STAMP(3);
+        /* pass 2: weighted values; each warp forms the softmax weights
+         * exp(s - max) of its own keys and sums them */
+        float Mh[GMAX], lw[GMAX];
+#pragma unroll
+        for (int h = 0; h < GMAX; h++) {
+            Mh[h] = h < grp ? s_M[h] : 0.0f;
+            lw[h] = 0.0f;
         }
-        consumer_sync();
-        if (threadIdx.x < grp) {
-            float L = 0.0f;
-            for (int w = 0; w < NW; w++) L += sred[w * GMAX + threadIdx.x];
-            s_L[threadIdx.x] = L;
-        }
-
-        /* pass 2: weighted values */
         const int d0 = lane * PER;
         float o[GMAX][PER];
 #pragma unroll
@@ -371,7 +366,8 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr)
 #pragma unroll
                     for (int h = 0; h < GMAX; h++) {
                         if (h >= grp) break;
-                        const float pw = sp[t * grp + h];
+                        const float pw = __expf(sp[t * grp + h] - Mh[h]);
+                        lw[h] += pw;
 #pragma unroll
                         for (int p = 0; p < PER; p++) o[h][p] = fmaf(pw, vv[j][p], o[h][p]);
                     }
@@ -383,8 +379,16 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr)
             if (h >= grp) break;
 #pragma unroll
             for (int p = 0; p < PER; p++) sacc[(warp * grp + h) * HD + d0 + p] = o[h][p];
+            if (lane == 0) sred[warp * GMAX + h] = lw[h];
         }
         consumer_sync();
+        if (threadIdx.x < grp) {
+            float L = 0.0f;
+            for (int w = 0; w < NW; w++) L += sred[w * GMAX + threadIdx.x];
+            s_L[threadIdx.x] = L;
+        }
+        consumer_sync();
+        FL_STAMP(4);
         float* part = a.part + (size_t)item * grp * (HD + 2);
         for (int i = threadIdx.x; i < grp * HD; i += NC) {
             const int h = i / HD, d = i % HD;
@@ -398,7 +402,9 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr)
             }
         }
         consumer_sync(); /* the item's shared memory is reused by the next item */
+        FL_STAMP(5);
     }
+#undef FL_STAMP
 }
 
 /* The combine phase: query head hq's output from its splits' partials (one
@@ -649,7 +655,8 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
             continue;
         }
         if (kind == FL_PH_ATTN) {
-            phase_attn_t<HD, GMAX>(*reinterpret_cast<const FlAttnArgs*>(abuf), reinterpret_cast<float*>(scratch));
+            phase_attn_t<HD, GMAX>(*reinterpret_cast<const FlAttnArgs*>(abuf), reinterpret_cast<float*>(scratch),
+                                   ta.detail && blockIdx.x == 0 ? ta.detail + (size_t)p * NW * 4 : nullptr);
             continue;
         }
         if (kind == FL_PH_ATTN_COMBINE) {
