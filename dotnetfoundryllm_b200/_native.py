@@ -26,6 +26,7 @@ FL_ARCH_LLAMA, FL_ARCH_MISTRAL, FL_ARCH_GEMMA2, FL_ARCH_QWEN2 = 0, 1, 2, 3
 FL_PROF_MATVEC, FL_PROF_ATTN, FL_PROF_OTHER, FL_PROF_STEP, FL_PROF_N = 0, 1, 2, 3, 4
 
 FL_TOPK_DEVICE_MAX_N = 262144
+FL_TP_HANDLE_BYTES = 64
 
 
 class FlModelDesc(C.Structure):
@@ -88,6 +89,8 @@ PUBLIC_API = [
     ("fl_decode_greedy", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]),
     ("fl_topk", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("fl_topk_device", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("fl_session_tp_handle", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("fl_session_tp_connect", C.c_int, [C.c_void_p, C.c_void_p]),
     ("fl_session_destroy", None, [C.c_void_p]),
     ("fl_dequant", C.c_int, [C.c_int32, C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64]),
     ("fl_matvec", C.c_int, [C.c_int32, C.c_void_p, C.c_uint64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
@@ -104,6 +107,7 @@ INTERNAL_API = [
     ("fl_session_phase_ms", C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.POINTER(C.c_int32)]),
     ("fl_session_cta_done_ms", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.POINTER(C.c_int32)]),
     ("fl_session_detail", C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    ("fl_tp_slice", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
 ]
 
 GEN_API = [

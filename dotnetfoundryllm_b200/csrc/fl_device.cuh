@@ -95,6 +95,20 @@ __device__ __forceinline__ void fl_bulk_g2s(void* sdst, const void* gsrc, uint32
         : "memory");
 }
 
+/* System-scope release store / acquire load: flags between GPUs (peer memory
+ * mapped over NVLink). */
+__device__ __forceinline__ void fl_st_release_sys(int* p, int v)
+{
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int fl_ld_acquire_sys(const int* p)
+{
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 /* Asks L2 to fetch [p, p + bytes) (16-byte aligned, size a multiple of 16). */
 __device__ __forceinline__ void fl_prefetch_l2(const void* p, uint32_t bytes)
 {

@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #define FL_MV_MAX_SEG 3
+#define FL_TP_MAX 8        /* ranks of one tensor-parallel group */
 #define FL_MV_WARPS 8
 #define FL_MV_THREADS (FL_MV_WARPS * 32)
 
@@ -28,6 +29,8 @@ enum {
     FL_EPI_QKV = 2,     /* bias, RoPE, q store, K/V cache append */
     FL_EPI_GLU = 3,     /* act = silu|gelu(gate) * up over interleaved gate/up rows */
     FL_EPI_LOGITS = 4,  /* logits (+ final softcap) and greedy argmax */
+    FL_EPI_PARTIAL = 5, /* tensor parallel, row-parallel projection: push the partial
+                           output row to every rank's receive buffer (tp_out[q][row]) */
 };
 
 struct FlMvSeg {
@@ -72,6 +75,11 @@ struct FlMvArgs {
     int32_t* counter;
     int32_t* argmax_out;
     int* err;
+    /* tensor parallelism: PARTIAL epilogue → tp_out[q] = rank q's receive slot
+     * of this rank; LOGITS epilogue → tp_out[q] = rank q's full logits, rows
+     * offset by tp_row0 (the argmax index is global too).  tp_n = 0: off. */
+    int32_t tp_n, tp_row0;
+    float* tp_out[FL_TP_MAX];
 };
 
 /* Dynamic shared memory of a matvec launch. */
@@ -117,7 +125,15 @@ struct FlAttnArgs {
 #define FL_TK_MAX_TILES 256      /* 16-row tiles of one matvec phase per CTA */
 
 /* FL_PH_ATTN writes per-split partials; FL_PH_ATTN_COMBINE merges them (same args). */
-enum { FL_PH_EMBED = 0, FL_PH_MATVEC = 1, FL_PH_ATTN = 2, FL_PH_ATTN_COMBINE = 3 };
+enum { FL_PH_EMBED = 0, FL_PH_MATVEC = 1, FL_PH_ATTN = 2, FL_PH_ATTN_COMBINE = 3, FL_PH_TP_REDUCE = 4 };
+
+/* Tensor-parallel allreduce of a row-parallel projection's output: every rank
+ * signals exchange `k` of the step, waits for all, then sums the receive
+ * slots of `parity` in rank order into y (mode 0: y += sum, 1: y = sum). */
+struct FlTpArgs {
+    int32_t k, parity, mode, n;
+    float* y;
+};
 
 struct FlPhase {
     int32_t kind;
@@ -125,7 +141,15 @@ struct FlPhase {
     FlMvArgs mv;
     FlAttnArgs at;
     FlEmbedArgs em;
+    FlTpArgs tp;
 };
+
+/* A rank's exchange region (one device allocation, mapped by every peer):
+ * [FL_TP_MAX] int flags written by peers (epochs), [FL_TP_MAX][2] floats of
+ * argmax candidates, [2][FL_TP_MAX][recv_n] receive slots, [vocab] logits. */
+#define FL_TP_FLAGS_OFF 0
+#define FL_TP_BEST_OFF 128
+#define FL_TP_RECV_OFF 256
 
 /* What the weight stream needs of one matvec phase, in one 64-byte line. */
 struct __align__(64) FlFeedPhase {
@@ -154,6 +178,12 @@ struct FlTokenArgs {
     int32_t* pos;
     int32_t* out_tokens;
     int32_t* step;
+    /* tensor parallelism (tp_size 1 = off) */
+    int32_t tp_size, tp_rank;
+    int32_t tp_n_exchanges;      /* per step: 2 per layer + the argmax */
+    int32_t tp_recv_n;           /* floats per receive slot */
+    int32_t* tp_epoch;           /* device counter: epochs of earlier steps */
+    uint8_t* tp_peer[FL_TP_MAX]; /* every rank's exchange region (this rank's too) */
 };
 
 /* The instance for (head_dim, query heads per kv head), or NULL when none is

@@ -392,17 +392,27 @@ __device__ __forceinline__ void epilogue(const FlMvArgs& a, const FlMvSeg& sg, i
         }
         float m = fl_warp_max(fabsf(actv));
         if (lane == 0) atomicMax(reinterpret_cast<int*>(a.act_absmax), __float_as_int(m));
+    } else if constexpr (EPI == FL_EPI_PARTIAL) {
+        /* tensor parallel: this rank's share of the row, to every rank */
+        if (in_seg) {
+            const int row = sg.tile0 * 16 + row_local;
+            for (int q = 0; q < a.tp_n; q++) a.tp_out[q][row] = v;
+        }
     } else { /* FL_EPI_LOGITS */
         float val = v;
         int idx = 0x7fffffff;
-        const int row = sg.tile0 * 16 + row_local;
+        const int row = sg.tile0 * 16 + row_local + a.tp_row0;
         if (in_seg) {
             if (a.softcap > 0.0f) {
                 /* TensorOperations.SoftCap: x*(1/cap) -> tanh -> *cap */
                 float inv = 1.0f / a.softcap;
                 val = __fmul_rn(tanhf(__fmul_rn(val, inv)), a.softcap);
             }
-            a.y[row] = val;
+            if (a.tp_n > 0) {
+                for (int q = 0; q < a.tp_n; q++) a.tp_out[q][row] = val; /* full logits on every rank */
+            } else {
+                a.y[row] = val;
+            }
             idx = row;
         }
 #pragma unroll
@@ -441,6 +451,7 @@ __device__ __forceinline__ void epilogue_any(const FlMvArgs& a, const FlMvSeg& s
     case FL_EPI_RESID: epilogue<FL_EPI_RESID>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     case FL_EPI_QKV: epilogue<FL_EPI_QKV>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     case FL_EPI_GLU: epilogue<FL_EPI_GLU>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
+    case FL_EPI_PARTIAL: epilogue<FL_EPI_PARTIAL>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     default: epilogue<FL_EPI_LOGITS>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     }
 }

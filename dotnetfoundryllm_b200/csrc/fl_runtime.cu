@@ -68,6 +68,9 @@ struct Layer {
 struct fl_model {
     fl_model_desc d;
     int sm_count = 148;
+    /* tensor parallelism: this rank's share (T = 1: the whole model) */
+    int T = 1, rank = 0;
+    int nh_l = 0, nkv_l = 0, qd_l = 0, kvd_l = 0, ffn_l = 0, vocab_l = 0;
     std::vector<Layer> layers;
     uint8_t* emb_raw = nullptr;
     int emb_type = -1;
@@ -115,6 +118,15 @@ struct fl_session {
     size_t tk_smem = 0;
     int tk_grid = 0;
     const void* tk_kernel = nullptr;
+    int max_dyn = 0;
+    bool built = false;
+    /* tensor parallelism: this rank's exchange region and every rank's, mapped */
+    uint8_t* xchg = nullptr;
+    size_t xchg_bytes = 0, xchg_logits_off = 0;
+    int xchg_recv_n = 0;
+    int32_t* tp_epoch = nullptr;
+    uint8_t* tp_peer[FL_TP_MAX] = {};
+    void* tp_opened[FL_TP_MAX] = {};
     std::vector<void*> allocs;
 };
 
@@ -174,10 +186,23 @@ extern "C" int fl_model_create(const fl_model_desc* desc, fl_model** out)
     if (grp != 1 && grp != 2 && grp != 4 && grp != 8) return fail(FL_ERR_UNSUPPORTED, "GQA group %d", grp);
     if (d.hidden % 32 || d.ffn % 32 || (d.n_heads * d.head_dim) % 32)
         return fail(FL_ERR_UNSUPPORTED, "dimensions must be multiples of 32");
-    if (d.tp_size > 1) return fail(FL_ERR_UNSUPPORTED, "tensor parallelism is not built into this library yet");
+    const int T = d.tp_size < 1 ? 1 : d.tp_size;
+    if (T > FL_TP_MAX || (T & (T - 1))) return fail(FL_ERR_UNSUPPORTED, "tp_size %d (1, 2, 4 or 8)", T);
+    if (d.tp_rank < 0 || d.tp_rank >= T) return fail(FL_ERR_ARG, "tp_rank %d outside [0, %d)", d.tp_rank, T);
+    if (d.n_kv_heads % T || d.ffn % (8 * T) || d.vocab % (16 * T))
+        return fail(FL_ERR_UNSUPPORTED, "tp_size %d does not divide the kv heads (%d), FFN rows (%d) or vocabulary (%d)",
+                    T, d.n_kv_heads, d.ffn, d.vocab);
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice(%d) failed", d.device);
     fl_model* m = new fl_model();
     m->d = d;
+    m->T = T;
+    m->rank = T > 1 ? d.tp_rank : 0;
+    m->nh_l = d.n_heads / T;
+    m->nkv_l = d.n_kv_heads / T;
+    m->qd_l = m->nh_l * d.head_dim;
+    m->kvd_l = m->nkv_l * d.head_dim;
+    m->ffn_l = d.ffn / T;
+    m->vocab_l = d.vocab / T;
     m->layers.resize((size_t)d.n_layers);
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d.device) == cudaSuccess && sms > 0)
@@ -257,6 +282,42 @@ static int upload_matrix(fl_model* m, int type, int rows, int cols, const uint8_
     return FL_OK;
 }
 
+/* Tensor parallelism: this rank's rows [r0, r0 + n) of a row-major matrix
+ * (whole rows of GGUF blocks), or its columns [c0, c0 + n) of every row
+ * (whole blocks: the split must be a multiple of the block length). */
+static std::vector<uint8_t> slice_rows(const uint8_t* raw, int type, int cols, int r0, int n)
+{
+    const size_t rb = (size_t)cols / block_elems(type) * block_bytes(type);
+    return std::vector<uint8_t>(raw + (size_t)r0 * rb, raw + (size_t)(r0 + n) * rb);
+}
+
+static std::vector<uint8_t> slice_cols(const uint8_t* raw, int type, int rows, int cols, int c0, int n)
+{
+    const size_t rb = (size_t)cols / block_elems(type) * block_bytes(type);
+    const size_t b0 = (size_t)c0 / block_elems(type) * block_bytes(type);
+    const size_t nb = (size_t)n / block_elems(type) * block_bytes(type);
+    std::vector<uint8_t> out((size_t)rows * nb);
+    for (int r = 0; r < rows; r++) memcpy(out.data() + (size_t)r * nb, raw + (size_t)r * rb + b0, nb);
+    return out;
+}
+
+/* Internal (tests): the slice a rank keeps, rows (dim 0) or columns (dim 1). */
+extern "C" int fl_tp_slice(int32_t type, int32_t rows, int32_t cols, int32_t dim, int32_t rank, int32_t T,
+                           const void* src, void* dst)
+{
+    if (!block_elems(type) || T < 1 || rank < 0 || rank >= T) return fail(FL_ERR_ARG, "bad slice request");
+    std::vector<uint8_t> v;
+    if (dim == 0) {
+        if (rows % T) return fail(FL_ERR_ARG, "rows %d not divisible by %d", rows, T);
+        v = slice_rows(static_cast<const uint8_t*>(src), type, cols, rank * (rows / T), rows / T);
+    } else {
+        if (cols % T || (cols / T) % block_elems(type)) return fail(FL_ERR_ARG, "columns %d do not split by %d", cols, T);
+        v = slice_cols(static_cast<const uint8_t*>(src), type, rows, cols, rank * (cols / T), cols / T);
+    }
+    memcpy(dst, v.data(), v.size());
+    return FL_OK;
+}
+
 static bool parse_layer(const char* name, int* layer, std::string* suffix)
 {
     if (strncmp(name, "blk.", 4) != 0) return false;
@@ -297,9 +358,12 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
         return FL_OK;
     }
     if (n == "output_norm.weight") return upload_vector(m, type, raw, nbytes, h, &m->out_norm);
+    const int T = m->T, rk = m->rank;
     if (n == "output.weight") {
         if (!mat_shape_ok(d.vocab, h)) return fail(FL_ERR_ARG, "output.weight shape mismatch");
-        return upload_matrix(m, type, d.vocab, h, raw, nullptr, nullptr, &m->output, (double)nbytes);
+        if (T == 1) return upload_matrix(m, type, d.vocab, h, raw, nullptr, nullptr, &m->output, (double)nbytes);
+        std::vector<uint8_t> part = slice_rows(raw, type, h, rk * m->vocab_l, m->vocab_l);
+        return upload_matrix(m, type, m->vocab_l, h, part.data(), nullptr, nullptr, &m->output, (double)part.size());
     }
     int l;
     std::string sfx;
@@ -310,23 +374,46 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
     if (sfx == "ffn_norm.weight") return upload_vector(m, type, raw, nbytes, h, &L.ffn_norm);
     if (sfx == "post_attn_norm.weight") return upload_vector(m, type, raw, nbytes, h, &L.post_attn_norm);
     if (sfx == "post_ffn_norm.weight") return upload_vector(m, type, raw, nbytes, h, &L.post_ffn_norm);
-    if (sfx == "attn_q.bias") return upload_vector(m, type, raw, nbytes, qd, &L.bq);
-    if (sfx == "attn_k.bias") return upload_vector(m, type, raw, nbytes, kvd, &L.bk);
-    if (sfx == "attn_v.bias") return upload_vector(m, type, raw, nbytes, kvd, &L.bv);
-    struct { const char* s; DevMatrix* dm; int rows, cols; } mats[] = {
-        {"attn_q.weight", &L.wq, qd, h}, {"attn_k.weight", &L.wk, kvd, h}, {"attn_v.weight", &L.wv, kvd, h},
-        {"attn_output.weight", &L.wo, h, qd}, {"ffn_down.weight", &L.down, h, f},
+    /* biases of this rank's heads (element slices of F32/F16 vectors) */
+    auto bias = [&](int full, int local, float** out) -> int {
+        if (T == 1) return upload_vector(m, type, raw, nbytes, full, out);
+        if (block_elems(type) != 1) return fail(FL_ERR_UNSUPPORTED, "%s: quantized bias with tensor parallelism", name);
+        const size_t eb = (size_t)block_bytes(type);
+        return upload_vector(m, type, raw + (size_t)rk * local * eb, (uint64_t)local * eb, local, out);
+    };
+    if (sfx == "attn_q.bias") return bias(qd, m->qd_l, &L.bq);
+    if (sfx == "attn_k.bias") return bias(kvd, m->kvd_l, &L.bk);
+    if (sfx == "attn_v.bias") return bias(kvd, m->kvd_l, &L.bv);
+    /* column-parallel (rows split: heads) and row-parallel (columns split) */
+    struct { const char* s; DevMatrix* dm; int rows, cols, split_cols, lrows, lcols; } mats[] = {
+        {"attn_q.weight", &L.wq, qd, h, 0, m->qd_l, h},
+        {"attn_k.weight", &L.wk, kvd, h, 0, m->kvd_l, h},
+        {"attn_v.weight", &L.wv, kvd, h, 0, m->kvd_l, h},
+        {"attn_output.weight", &L.wo, h, qd, 1, h, m->qd_l},
+        {"ffn_down.weight", &L.down, h, f, 1, h, m->ffn_l},
     };
     for (auto& e : mats) {
         if (sfx == e.s) {
             if (!mat_shape_ok(e.rows, e.cols)) return fail(FL_ERR_ARG, "%s shape mismatch", name);
-            return upload_matrix(m, type, e.rows, e.cols, raw, nullptr, nullptr, e.dm, (double)nbytes);
+            if (T == 1) return upload_matrix(m, type, e.rows, e.cols, raw, nullptr, nullptr, e.dm, (double)nbytes);
+            if (e.split_cols && e.lcols % block_elems(type))
+                return fail(FL_ERR_UNSUPPORTED, "%s: %d columns per rank are not whole blocks of type %d", name,
+                            e.lcols, type);
+            std::vector<uint8_t> part = e.split_cols ? slice_cols(raw, type, e.rows, e.cols, rk * e.lcols, e.lcols)
+                                                     : slice_rows(raw, type, e.cols, rk * e.lrows, e.lrows);
+            return upload_matrix(m, type, e.lrows, e.lcols, part.data(), nullptr, nullptr, e.dm, (double)part.size());
         }
     }
     if (sfx == "ffn_gate.weight" || sfx == "ffn_up.weight") {
         if (!mat_shape_ok(f, h)) return fail(FL_ERR_ARG, "%s shape mismatch", name);
         if (f % 8) return fail(FL_ERR_UNSUPPORTED, "feed_forward_length %d is not a multiple of 8", f);
         const bool is_gate = sfx == "ffn_gate.weight";
+        std::vector<uint8_t> part;
+        if (T > 1) {
+            part = slice_rows(raw, type, h, rk * m->ffn_l, m->ffn_l);
+            raw = part.data();
+            nbytes = part.size();
+        }
         if (L.stash_type < 0) {
             L.stash.assign(raw, raw + nbytes);
             L.stash_type = type;
@@ -338,13 +425,14 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
             return fail(FL_ERR_UNSUPPORTED, "ffn_gate and ffn_up of layer %d have different types", l);
         const uint8_t* gate = is_gate ? raw : L.stash.data();
         const uint8_t* up = is_gate ? L.stash.data() : raw;
-        /* interleave: tile T rows 0..7 = gate rows 8T.., rows 8..15 = up rows 8T.. */
-        std::vector<int32_t> map((size_t)2 * f);
-        for (int R = 0; R < 2 * f; R++) {
-            int T = R / 16, r = R % 16;
-            map[(size_t)R] = r < 8 ? (8 * T + r) : (-1 - (8 * T + r - 8));
+        /* interleave: tile t rows 0..7 = gate rows 8t.., rows 8..15 = up rows 8t.. */
+        const int fl = m->ffn_l;
+        std::vector<int32_t> map((size_t)2 * fl);
+        for (int R = 0; R < 2 * fl; R++) {
+            int t = R / 16, r = R % 16;
+            map[(size_t)R] = r < 8 ? (8 * t + r) : (-1 - (8 * t + r - 8));
         }
-        int rc = upload_matrix(m, type, 2 * f, h, gate, up, map.data(), &L.gate_up, 2.0 * (double)nbytes);
+        int rc = upload_matrix(m, type, 2 * fl, h, gate, up, map.data(), &L.gate_up, 2.0 * (double)nbytes);
         std::vector<uint8_t>().swap(L.stash);
         return rc;
     }
@@ -380,8 +468,9 @@ extern "C" int fl_model_finalize(fl_model* m)
         /* LoadTensorOptional("output.weight") ?? tokenEmbed (GgufModelLoader.cs:368-369) */
         std::vector<uint8_t> host((size_t)m->emb_bytes);
         CK(cudaMemcpy(host.data(), m->emb_raw, (size_t)m->emb_bytes, cudaMemcpyDeviceToHost));
-        int rc = upload_matrix(m, m->emb_type, d.vocab, d.hidden, host.data(), nullptr, nullptr, &m->output,
-                               (double)m->emb_bytes);
+        if (m->T > 1) host = slice_rows(host.data(), m->emb_type, d.hidden, m->rank * m->vocab_l, m->vocab_l);
+        int rc = upload_matrix(m, m->emb_type, m->vocab_l, d.hidden, host.data(), nullptr, nullptr, &m->output,
+                               (double)host.size());
         if (rc) return rc;
     }
     /* one embedding row per step */
@@ -451,9 +540,32 @@ static void build_phases(fl_session* s, PhaseList& P)
 {
     fl_model* m = s->m;
     const fl_model_desc& d = m->d;
-    const int h = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim;
+    const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, T = m->T;
     const bool gemma = d.arch == FL_ARCH_GEMMA2;
     int32_t* pos = s->state + ST_POS;
+    /* tensor parallelism: a row-parallel projection pushes its partial rows
+     * to every rank (receive slot [parity][this rank]), then an allreduce
+     * phase sums them into y */
+    auto tp_partial = [&](FlMvArgs& a, int parity) {
+        a.epi = FL_EPI_PARTIAL;
+        a.tp_n = T;
+        for (int q = 0; q < T; q++)
+            a.tp_out[q] = reinterpret_cast<float*>(s->tp_peer[q] + FL_TP_RECV_OFF) +
+                          ((size_t)parity * FL_TP_MAX + m->rank) * s->xchg_recv_n;
+    };
+    auto tp_reduce = [&](int k, int parity, int mode, float* y) {
+        FlPhase r;
+        memset(&r, 0, sizeof r);
+        r.kind = FL_PH_TP_REDUCE;
+        r.tp.k = k;
+        r.tp.parity = parity;
+        r.tp.mode = mode;
+        r.tp.n = h;
+        r.tp.y = y;
+        P.ph.push_back(r);
+        P.cls.push_back(CLS_OTHER);
+        P.bytes.push_back(0.0);
+    };
 
     FlPhase e;
     memset(&e, 0, sizeof e);
@@ -528,8 +640,8 @@ static void build_phases(fl_session* s, PhaseList& P)
         at.at.part = s->attn_part;
         at.at.counter = s->attn_counter;
         at.at.pos = pos;
-        at.at.n_heads = d.n_heads;
-        at.at.n_kv = d.n_kv_heads;
+        at.at.n_heads = m->nh_l;
+        at.at.n_kv = m->nkv_l;
         at.at.head_dim = d.head_dim;
         at.at.n_split = s->attn_split;
         int window = INT_MAX;
@@ -554,7 +666,9 @@ static void build_phases(fl_session* s, PhaseList& P)
         a.absmax = amax_att;
         a.epi = gemma ? FL_EPI_STORE : FL_EPI_RESID;
         a.y = gemma ? s->o : x;
+        if (T > 1) tp_partial(a, 0);
         P.add_mv(a, mat_bytes(L.wo));
+        if (T > 1) tp_reduce(2 * l, 0, gemma ? 1 : 0, gemma ? s->o : x);
 
         /* FFN: norm → gate/up → SiLU|GELU(gate)*up */
         a = base_args(s, L.gate_up, h);
@@ -574,19 +688,21 @@ static void build_phases(fl_session* s, PhaseList& P)
             std::swap(x, x_other);
         }
         a.epi = FL_EPI_GLU;
-        a.rows_total = d.ffn;
+        a.rows_total = m->ffn_l;
         a.act_gelu = gemma ? 1 : 0;
         a.act_out = s->act;
         a.act_absmax = amax_act;
         P.add_mv(a, mat_bytes(L.gate_up) + 4.0 * h);
 
-        a = base_args(s, L.down, d.ffn);
+        a = base_args(s, L.down, m->ffn_l);
         a.in_mode = FL_IN_PLAIN;
         a.x = s->act;
         a.absmax = amax_act;
         a.epi = gemma ? FL_EPI_STORE : FL_EPI_RESID;
         a.y = gemma ? s->o : x;
+        if (T > 1) tp_partial(a, 1);
         P.add_mv(a, mat_bytes(L.down));
+        if (T > 1) tp_reduce(2 * l + 1, 1, gemma ? 1 : 0, gemma ? s->o : x);
     }
     /* final norm + LM head + greedy argmax */
     FlMvArgs a = base_args(s, m->output, h);
@@ -607,6 +723,12 @@ static void build_phases(fl_session* s, PhaseList& P)
     a.epi = FL_EPI_LOGITS;
     a.y = s->logits;
     a.softcap = gemma ? d.final_softcap : 0.0f;
+    if (T > 1) {
+        /* vocabulary-parallel head: logits rows [rank*V/T, ...) to every rank */
+        a.tp_n = T;
+        a.tp_row0 = m->rank * m->vocab_l;
+        for (int q = 0; q < T; q++) a.tp_out[q] = reinterpret_cast<float*>(s->tp_peer[q] + s->xchg_logits_off);
+    }
     a.cta_best = s->cta_best;
     a.counter = s->state + ST_HEADCNT;
     a.argmax_out = s->state + ST_ARGMAX;
@@ -620,6 +742,8 @@ static int enqueue_step(fl_session* s)
     CK(fl_launch_token(s->tk_kernel, s->ta, s->tk_grid, s->tk_smem, s->st));
     return FL_OK;
 }
+
+static int session_build(fl_session* s);
 
 extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch, int32_t kv_dtype, fl_session** out)
 {
@@ -642,10 +766,13 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     fl_session* s = new fl_session();
     s->m = m;
     s->max_ctx = max_ctx;
-    const int h = d.hidden, qd = d.n_heads * d.head_dim, kvd = d.n_kv_heads * d.head_dim, grp = d.n_heads / d.n_kv_heads;
+    s->max_dyn = max_dyn;
+    s->tk_kernel = tk_kernel;
+    /* this rank's share of the model (the whole model without tensor parallelism) */
+    const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, grp = d.n_heads / d.n_kv_heads;
     const int G = m->sm_count;
     /* attention items (kv head, split): at most one per SM */
-    int split = G / d.n_kv_heads;
+    int split = G / m->nkv_l;
     if (split > max_ctx) split = max_ctx;
     if (split < 1) split = 1;
     s->attn_split = split;
@@ -658,14 +785,24 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     AL(s->o, (size_t)h * 4);
     AL(s->q, (size_t)qd * 4);
     AL(s->att, (size_t)qd * 4);
-    AL(s->act, (size_t)d.ffn * 4);
-    AL(s->logits, (size_t)d.vocab * 4);
+    AL(s->act, (size_t)m->ffn_l * 4);
+    if (m->T == 1) {
+        AL(s->logits, (size_t)d.vocab * 4);
+    } else {
+        /* the exchange region peers write into; the full logits live at its end */
+        s->xchg_recv_n = (h + 63) & ~63;
+        s->xchg_logits_off = FL_TP_RECV_OFF + (size_t)2 * FL_TP_MAX * s->xchg_recv_n * 4;
+        s->xchg_bytes = s->xchg_logits_off + (size_t)d.vocab * 4;
+        AL(s->xchg, s->xchg_bytes);
+        AL(s->tp_epoch, 16);
+        if (!rc) s->logits = reinterpret_cast<float*>(s->xchg + s->xchg_logits_off);
+    }
     AL(s->kc, kv_bytes);
     AL(s->vc, kv_bytes);
     AL(s->absmax, (size_t)s->n_absmax * 4);
     AL(s->state, (size_t)ST_N * 4);
-    AL(s->attn_counter, (size_t)d.n_kv_heads * 4);
-    AL(s->attn_part, (size_t)d.n_kv_heads * split * grp * (d.head_dim + 2) * 4);
+    AL(s->attn_counter, (size_t)m->nkv_l * 4);
+    AL(s->attn_part, (size_t)m->nkv_l * split * grp * (d.head_dim + 2) * 4);
     AL(s->cta_best, (size_t)G * 8 + 8);
     AL(s->out_tokens, (size_t)max_ctx * 4 + 4);
     s->topk_scratch_bytes = fl_topk_scratch_bytes(d.vocab, 0);
@@ -683,6 +820,39 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
         fl_session_destroy(s);
         return fail(FL_ERR_CUDA, "stream/pinned allocation failed");
     }
+    cudaMemsetAsync(s->state, 0, ST_N * 4, s->st);
+    cudaMemsetAsync(s->attn_counter, 0, (size_t)m->nkv_l * 4, s->st);
+    cudaMemsetAsync(s->kc, 0, kv_bytes, s->st);
+    cudaMemsetAsync(s->vc, 0, kv_bytes, s->st);
+    if (s->xchg) {
+        cudaMemsetAsync(s->xchg, 0, s->xchg_bytes, s->st);
+        cudaMemsetAsync(s->tp_epoch, 0, 16, s->st);
+    }
+    if (cudaStreamSynchronize(s->st) != cudaSuccess) {
+        fl_session_destroy(s);
+        return fail(FL_ERR_CUDA, "session init failed");
+    }
+    if (m->T > 1) { /* built by fl_session_tp_connect once the peers are mapped */
+        *out = s;
+        return FL_OK;
+    }
+    rc = session_build(s);
+    if (rc) {
+        fl_session_destroy(s);
+        return rc;
+    }
+    *out = s;
+    return FL_OK;
+}
+
+/* The phase list, the persistent kernel's configuration and the captured
+ * token graph (after the peers are mapped, with tensor parallelism). */
+static int session_build(fl_session* s)
+{
+    fl_model* m = s->m;
+    const fl_model_desc& d = m->d;
+    const int G = m->sm_count, grp = d.n_heads / d.n_kv_heads, max_ctx = s->max_ctx, max_dyn = s->max_dyn;
+    int rc = FL_OK;
     /* phase list */
     PhaseList P;
     build_phases(s, P);
@@ -709,10 +879,7 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     if (!rc) rc = dalloc(s->allocs, &s->timestamps, (P.ph.size() + 1) * 8);
     if (!rc) rc = dalloc(s->allocs, &s->cta_done, P.ph.size() * (size_t)G * 8);
     if (!rc) rc = dalloc(s->allocs, &s->detail, P.ph.size() * (size_t)(FL_TK_WARPS * 4 + 1) * 8);
-    if (rc) {
-        fl_session_destroy(s);
-        return rc;
-    }
+    if (rc) return rc;
     /* shared memory: weight ring of the largest unit + x-encoding / attention scratch */
     int slot = 0, max_kb = 0, max_tiles = 0;
     for (const FlPhase& p : P.ph)
@@ -721,10 +888,8 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
             max_kb = std::max(max_kb, p.mv.n_kb);
             max_tiles = std::max(max_tiles, (p.mv.n_tiles + G - 1) / G);
         }
-    if (max_tiles > FL_TK_MAX_TILES) {
-        fl_session_destroy(s);
+    if (max_tiles > FL_TK_MAX_TILES)
         return fail(FL_ERR_UNSUPPORTED, "a projection has %d row tiles per SM (limit %d)", max_tiles, FL_TK_MAX_TILES);
-    }
     slot = (slot + 127) & ~127;
     const size_t xenc = (size_t)max_kb * 8 * FL_XENC_CHUNK_BYTES;
     /* attention: q, per-warp outputs, reductions, the scores of one item */
@@ -735,10 +900,8 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     const size_t scratch = std::max(xenc, attn);
     int n_slots = 2;
     while (fl_token_smem_bytes(n_slots + 1, slot, scratch) <= (size_t)max_dyn) n_slots++;
-    if (fl_token_smem_bytes(n_slots, slot, scratch) > (size_t)max_dyn) {
-        fl_session_destroy(s);
+    if (fl_token_smem_bytes(n_slots, slot, scratch) > (size_t)max_dyn)
         return fail(FL_ERR_UNSUPPORTED, "shared memory budget exceeded (x encoding %zu B)", xenc);
-    }
     FlTokenArgs& ta = s->ta;
     memset(&ta, 0, sizeof ta);
     ta.phases = s->d_phases;
@@ -758,47 +921,38 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     ta.pos = s->state + ST_POS;
     ta.out_tokens = s->out_tokens;
     ta.step = s->state + ST_STEP;
+    if (m->T > 1) {
+        ta.tp_size = m->T;
+        ta.tp_rank = m->rank;
+        ta.tp_n_exchanges = 2 * d.n_layers + 1;
+        ta.tp_recv_n = s->xchg_recv_n;
+        ta.tp_epoch = s->tp_epoch;
+        for (int q = 0; q < m->T; q++) ta.tp_peer[q] = s->tp_peer[q];
+    }
     s->tk_smem = fl_token_smem_bytes(n_slots, slot, scratch);
     s->tk_grid = G;
-    s->tk_kernel = tk_kernel;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tk_kernel, 32 * FL_TK_WARPS,
-                                                      s->tk_smem) != cudaSuccess ||
-        per_sm < 1) {
-        fl_session_destroy(s);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, s->tk_kernel, 32 * FL_TK_WARPS, s->tk_smem) !=
+            cudaSuccess ||
+        per_sm < 1)
         return fail(FL_ERR_UNSUPPORTED, "the token kernel does not fit one CTA per SM");
-    }
-    cudaMemcpyAsync(s->d_phases, P.ph.data(), P.ph.size() * sizeof(FlPhase), cudaMemcpyHostToDevice, s->st);
-    cudaMemcpyAsync(s->d_feed, feed.data(), feed.size() * sizeof(FlFeedPhase), cudaMemcpyHostToDevice, s->st);
-    cudaMemsetAsync(s->state, 0, ST_N * 4, s->st);
-    cudaMemsetAsync(s->attn_counter, 0, (size_t)d.n_kv_heads * 4, s->st);
-    cudaMemsetAsync(s->kc, 0, kv_bytes, s->st);
-    cudaMemsetAsync(s->vc, 0, kv_bytes, s->st);
-    if (cudaStreamSynchronize(s->st) != cudaSuccess) {
-        fl_session_destroy(s);
-        return fail(FL_ERR_CUDA, "session init failed");
-    }
+    CK(cudaMemcpyAsync(s->d_phases, P.ph.data(), P.ph.size() * sizeof(FlPhase), cudaMemcpyHostToDevice, s->st));
+    CK(cudaMemcpyAsync(s->d_feed, feed.data(), feed.size() * sizeof(FlFeedPhase), cudaMemcpyHostToDevice, s->st));
+    CK(cudaStreamSynchronize(s->st));
     /* capture the token step once */
     cudaGraph_t g = nullptr;
-    if (cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
-        fl_session_destroy(s);
-        return fail(FL_ERR_CUDA, "graph capture failed to start");
-    }
+    CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
     rc = enqueue_step(s);
     cudaError_t ce = cudaStreamEndCapture(s->st, &g);
     if (rc || ce != cudaSuccess) {
         if (g) cudaGraphDestroy(g);
-        fl_session_destroy(s);
         return rc ? rc : fail(FL_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
     }
     ce = cudaGraphInstantiate(&s->graph, g, 0);
     cudaGraphDestroy(g);
-    if (ce != cudaSuccess) {
-        fl_session_destroy(s);
-        return fail(FL_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
-    }
+    if (ce != cudaSuccess) return fail(FL_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
     s->launches = 1;
-    *out = s;
+    s->built = true;
     return FL_OK;
 }
 
@@ -808,10 +962,48 @@ extern "C" void fl_session_destroy(fl_session* s)
     cudaSetDevice(s->m->d.device);
     if (s->st) cudaStreamSynchronize(s->st);
     if (s->graph) cudaGraphExecDestroy(s->graph);
+    for (void* p : s->tp_opened)
+        if (p) cudaIpcCloseMemHandle(p);
     for (void* p : s->allocs) cudaFree(p);
     if (s->h_state) cudaFreeHost(s->h_state);
     if (s->st) cudaStreamDestroy(s->st);
     delete s;
+}
+
+/* ── tensor parallelism: mapping the ranks' exchange regions ────────────── */
+extern "C" int fl_session_tp_handle(fl_session* s, void* handle)
+{
+    if (!s || !handle) return fail(FL_ERR_ARG, "null argument");
+    if (s->m->T == 1) return fail(FL_ERR_STATE, "the model is not tensor-parallel");
+    if (cudaSetDevice(s->m->d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, s->xchg));
+    static_assert(sizeof(cudaIpcMemHandle_t) == FL_TP_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle, &h, sizeof h);
+    return FL_OK;
+}
+
+extern "C" int fl_session_tp_connect(fl_session* s, const void* handles)
+{
+    if (!s || !handles) return fail(FL_ERR_ARG, "null argument");
+    fl_model* m = s->m;
+    if (m->T == 1) return fail(FL_ERR_STATE, "the model is not tensor-parallel");
+    if (s->built) return fail(FL_ERR_STATE, "the session is already connected");
+    if (cudaSetDevice(m->d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    for (int q = 0; q < m->T; q++) {
+        if (q == m->rank) {
+            s->tp_peer[q] = s->xchg;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)q * FL_TP_HANDLE_BYTES, sizeof h);
+        void* p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) return fail(FL_ERR_CUDA, "mapping rank %d's exchange region: %s", q, cudaGetErrorString(e));
+        s->tp_opened[q] = p;
+        s->tp_peer[q] = static_cast<uint8_t*>(p);
+    }
+    return session_build(s);
 }
 
 extern "C" int fl_session_reset(fl_session* s, int32_t seq_slot)
@@ -853,6 +1045,7 @@ static int set_state(fl_session* s, int token, int pos)
 extern "C" int fl_forward(fl_session* s, int32_t token, int32_t position, float* logits, int32_t* argmax)
 {
     if (!s) return fail(FL_ERR_ARG, "null session");
+    if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     const fl_model_desc& d = s->m->d;
     if ((uint32_t)token >= (uint32_t)d.vocab)
         return fail(FL_ERR_ARG, "Token id %d is outside the valid vocabulary range [0, %d].", token, d.vocab - 1);
@@ -876,6 +1069,7 @@ extern "C" int fl_forward(fl_session* s, int32_t token, int32_t position, float*
 
 static int run_steps(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, float* ms)
 {
+    if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     const fl_model_desc& d = s->m->d;
     if ((uint32_t)token >= (uint32_t)d.vocab) return fail(FL_ERR_ARG, "Token id %d is outside the vocabulary", token);
     if (start_pos < 0 || start_pos > s->cur_len || n_steps < 0 || start_pos + n_steps > s->max_ctx)
@@ -924,6 +1118,7 @@ extern "C" int fl_time_decode(fl_session* s, int32_t token, int32_t start_pos, i
 extern "C" int fl_profile_step(fl_session* s, int32_t token, int32_t position, double* ms, double* bytes,
                                int32_t* launches)
 {
+    if (s && !s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     if (!s || !ms || !bytes) return fail(FL_ERR_ARG, "null argument");
     const fl_model_desc& d = s->m->d;
     if ((uint32_t)token >= (uint32_t)d.vocab || position < 0 || position >= s->max_ctx || position > s->cur_len)
@@ -956,6 +1151,7 @@ extern "C" int fl_profile_step(fl_session* s, int32_t token, int32_t position, d
 extern "C" int fl_topk(fl_session* s, int32_t k, int32_t* ids, float* vals, float* threshold)
 {
     if (!s || !ids || !vals) return fail(FL_ERR_ARG, "null argument");
+    if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     const fl_model_desc& d = s->m->d;
     if (k < 1 || k > d.vocab) return fail(FL_ERR_ARG, "k must be in [1, %d]", d.vocab);
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");

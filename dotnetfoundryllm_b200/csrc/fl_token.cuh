@@ -481,6 +481,48 @@ __device__ void prefetch_attn_kv(const FlAttnArgs& a)
     }
 }
 
+/* ── tensor parallelism ─────────────────────────────────────────────────── */
+
+/* Exchange `epoch`: CTA 0 (when `signal`) tells every rank that this rank's
+ * pushes are done; every CTA then waits, bounded, until all ranks have said
+ * so.  Flags are written by the peers into this rank's own exchange region,
+ * so the wait polls local memory. */
+__device__ void tp_signal_wait(const FlTokenArgs& ta, int epoch, bool signal)
+{
+    if (threadIdx.x == 0) {
+        if (signal)
+            for (int q = 0; q < ta.tp_size; q++)
+                fl_st_release_sys(reinterpret_cast<int*>(ta.tp_peer[q] + FL_TP_FLAGS_OFF) + ta.tp_rank, epoch);
+        const int* fl = reinterpret_cast<const int*>(ta.tp_peer[ta.tp_rank] + FL_TP_FLAGS_OFF);
+        const uint64_t t0 = fl_globaltimer();
+        for (int q = 0; q < ta.tp_size; q++) {
+            for (uint32_t it = 0; fl_ld_acquire_sys(fl + q) < epoch; it++) {
+                if ((it & 255u) == 0 && fl_globaltimer() - t0 > 2000000000ull) {
+                    atomicExch(ta.err, FL_DEV_ERR_TIMEOUT);
+                    q = ta.tp_size;
+                    break;
+                }
+            }
+        }
+    }
+    consumer_sync();
+}
+
+/* The allreduce after a row-parallel projection: every rank has pushed its
+ * partial rows into every rank's receive slot; sum them in rank order (the
+ * same order on every rank, so all ranks get identical values). */
+__device__ void phase_tp_reduce(const FlTokenArgs& ta, const FlTpArgs& r, int epoch0)
+{
+    tp_signal_wait(ta, epoch0 + r.k + 1, blockIdx.x == 0);
+    const float* recv = reinterpret_cast<const float*>(ta.tp_peer[ta.tp_rank] + FL_TP_RECV_OFF) +
+                        (size_t)r.parity * FL_TP_MAX * ta.tp_recv_n;
+    for (int i = blockIdx.x * NC + threadIdx.x; i < r.n; i += gridDim.x * NC) {
+        float sum = 0.0f;
+        for (int q = 0; q < ta.tp_size; q++) sum += __ldcg(recv + (size_t)q * ta.tp_recv_n + i);
+        r.y[i] = r.mode ? sum : __fadd_rn(__ldcg(r.y + i), sum);
+    }
+}
+
 /* A warp's private weight ring: S slots of slot_bytes with one full barrier
  * each.  The warp is both producer and consumer of its ring: lane 0 refills a
  * slot once the warp has copied the unit in it to registers. */
@@ -636,6 +678,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
 
     float best_v = 0.0f;
     int best_i = 0x7fffffff;
+    const int tp_epoch0 = ta.tp_size > 1 ? __ldcg(ta.tp_epoch) : 0;
     for (int p = 0; p < ta.n_phases; p++) {
         const int kind = ta.phases[p].kind;
         /* this phase's arguments into the buffer phase p-2 used (every warp
@@ -646,6 +689,8 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
             if (p + 1 < ta.n_phases && ta.phases[p + 1].kind == FL_PH_ATTN) prefetch_attn_kv(ta.phases[p + 1].at);
         } else if (kind == FL_PH_ATTN || kind == FL_PH_ATTN_COMBINE) {
             copy_words(abuf, &ta.phases[p].at, sizeof(FlAttnArgs));
+        } else if (kind == FL_PH_TP_REDUCE) {
+            copy_words(abuf, &ta.phases[p].tp, sizeof(FlTpArgs));
         }
         if (p > 0) grid_sync(ta.bar, p * G, ta.err, ta.cta_done ? ta.cta_done + (size_t)(p - 1) * G + blockIdx.x : nullptr);
         else consumer_sync();
@@ -657,6 +702,10 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         if (kind == FL_PH_ATTN) {
             phase_attn_t<HD, GMAX>(*reinterpret_cast<const FlAttnArgs*>(abuf), reinterpret_cast<float*>(scratch),
                                    ta.detail && blockIdx.x == 0 ? ta.detail + (size_t)p * NW * 4 : nullptr);
+            continue;
+        }
+        if (kind == FL_PH_TP_REDUCE) {
+            phase_tp_reduce(ta, *reinterpret_cast<const FlTpArgs*>(abuf), tp_epoch0);
             continue;
         }
         if (kind == FL_PH_ATTN_COMBINE) {
@@ -863,6 +912,9 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
             d[2] = st.waits;
             d[3] = st.units;
         }
+        /* rows pushed to other GPUs are visible system-wide before this CTA
+         * reports the phase done */
+        if (a.tp_n > 0) __threadfence_system();
 
         if (a.epi == FL_EPI_LOGITS) {
             /* greedy ArgMax (TensorPrimitives.IndexOfMax): per CTA, then across CTAs */
@@ -908,6 +960,43 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                     if (oi != 0x7fffffff && (bi == 0x7fffffff || fl_argmax_better(ov, oi, bv, bi))) {
                         bv = ov;
                         bi = oi;
+                    }
+                }
+                if (lane == 0 && ta.tp_size > 1) {
+                    /* across ranks: each rank's best, in rank order */
+                    for (int q = 0; q < ta.tp_size; q++) {
+                        float* bq = reinterpret_cast<float*>(ta.tp_peer[q] + FL_TP_BEST_OFF) + 2 * ta.tp_rank;
+                        bq[0] = bv;
+                        bq[1] = __int_as_float(bi);
+                    }
+                    __threadfence_system();
+                }
+                if (ta.tp_size > 1) {
+                    __syncwarp();
+                    if (lane == 0) {
+                        const int epoch = tp_epoch0 + ta.tp_n_exchanges;
+                        for (int q = 0; q < ta.tp_size; q++)
+                            fl_st_release_sys(reinterpret_cast<int*>(ta.tp_peer[q] + FL_TP_FLAGS_OFF) + ta.tp_rank,
+                                              epoch);
+                        const int* fl = reinterpret_cast<const int*>(ta.tp_peer[ta.tp_rank] + FL_TP_FLAGS_OFF);
+                        const float* bb = reinterpret_cast<const float*>(ta.tp_peer[ta.tp_rank] + FL_TP_BEST_OFF);
+                        const uint64_t t0 = fl_globaltimer();
+                        bv = 0.0f;
+                        bi = 0x7fffffff;
+                        for (int q = 0; q < ta.tp_size; q++) {
+                            for (uint32_t it = 0; fl_ld_acquire_sys(fl + q) < epoch; it++)
+                                if ((it & 255u) == 0 && fl_globaltimer() - t0 > 2000000000ull) {
+                                    atomicExch(ta.err, FL_DEV_ERR_TIMEOUT);
+                                    break;
+                                }
+                            const float bw = __ldcg(bb + 2 * q);
+                            const int iw = __float_as_int(__ldcg(bb + 2 * q + 1));
+                            if (iw != 0x7fffffff && (bi == 0x7fffffff || fl_argmax_better(bw, iw, bv, bi))) {
+                                bv = bw;
+                                bi = iw;
+                            }
+                        }
+                        *ta.tp_epoch = epoch;
                     }
                 }
                 if (lane == 0) {

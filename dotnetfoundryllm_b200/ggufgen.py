@@ -80,6 +80,11 @@ SPECS = {
     # small variants of the other families for the parity tests
     "tiny-mistral": ModelSpec("tiny-mistral", "mistral", 4, 512, 8, 2, 1408, 32000, 512, rope_base=1000000.0,
                               window=48, types=_llama_types(matmul=T_Q8_0, token_embd=T_Q8_0, output=T_Q8_0)),
+    # tensor-parallel parity: every split (heads, FFN rows, vocabulary, Wo/down
+    # columns in whole 256-blocks) divides for 2, 4 and 8 ranks
+    "small-tp": ModelSpec("small-tp", "llama", 2, 2048, 16, 8, 4096, 32000, 512, rope_base=500000.0,
+                          types=_llama_types(matmul=T_Q4_K, token_embd=T_Q6_K, attn_v=T_Q6_K, ffn_down=T_Q6_K,
+                                             output=T_Q6_K)),
     "tiny-gemma2": ModelSpec("tiny-gemma2", "gemma2", 4, 512, 4, 2, 1536, 32000, 512, head_dim=256, window=40,
                              attn_softcap=50.0, final_softcap=30.0,
                              types=_llama_types(matmul=T_Q5_K, token_embd=T_Q6_K, output=T_Q6_K)),

@@ -31,7 +31,8 @@ def _i32(v: int) -> int:
     return v - (1 << 32) if v >= (1 << 31) else v
 
 
-def build_desc(g: GgufFile, device: int = 0, max_ctx: int | None = None) -> N.FlModelDesc:
+def build_desc(g: GgufFile, device: int = 0, max_ctx: int | None = None, tp_rank: int = 0,
+               tp_size: int = 1) -> N.FlModelDesc:
     arch = g.get_string("general.architecture", "llama")
     if arch not in ARCHS:
         raise NotSupportedError(f"Architecture '{arch}' is not supported. Supported: llama, mistral, gemma2, qwen2.")
@@ -77,15 +78,16 @@ def build_desc(g: GgufFile, device: int = 0, max_ctx: int | None = None) -> N.Fl
     else:
         d.attn_scale = float(np.float32(1.0) / np.sqrt(np.float32(d.head_dim)))
     d.device = device
-    d.tp_rank, d.tp_size = 0, 1
+    d.tp_rank, d.tp_size = tp_rank, tp_size
     d.nccl_id = None
     return d
 
 
-def load(gguf_image, device: int = 0, max_ctx: int | None = None) -> CudaModel:
-    """Parses a GGUF image (bytes / numpy / memmap) and uploads it."""
+def load(gguf_image, device: int = 0, max_ctx: int | None = None, tp_rank: int = 0, tp_size: int = 1) -> CudaModel:
+    """Parses a GGUF image (bytes / numpy / memmap) and uploads it (this rank's
+    shard when tp_size > 1: the shim slices the raw blocks)."""
     g = gguf_image if isinstance(gguf_image, GgufFile) else parse(gguf_image)
-    desc = build_desc(g, device, max_ctx)
+    desc = build_desc(g, device, max_ctx, tp_rank, tp_size)
     model = CudaModel(desc)
     try:
         for t in g.tensors:

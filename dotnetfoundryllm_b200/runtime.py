@@ -147,6 +147,21 @@ class CudaForwardPass:
             raise ObjectDisposedError("CudaForwardPass")
         return self._h
 
+    # ── tensor parallelism ──
+    def tp_handle(self) -> bytes:
+        """This rank's exchange-region handle (FL_TP_HANDLE_BYTES)."""
+        buf = (C.c_uint8 * N.FL_TP_HANDLE_BYTES)()
+        check(self.lib.fl_session_tp_handle(self.handle, buf), "fl_session_tp_handle")
+        return bytes(buf)
+
+    def tp_connect(self, handles: list[bytes]) -> None:
+        """Maps every rank's exchange region (handles in rank order)."""
+        blob = b"".join(handles)
+        if len(blob) != N.FL_TP_HANDLE_BYTES * len(handles):
+            raise ArgumentError("each handle is FL_TP_HANDLE_BYTES bytes")
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(self.lib.fl_session_tp_connect(self.handle, buf), "fl_session_tp_connect")
+
     @property
     def logits(self) -> np.ndarray:
         """IForwardPass.Logits: logits of the most recent forward call."""
@@ -257,3 +272,10 @@ def matvec(ggml_type: int, raw: np.ndarray, rows: int, cols: int, x: np.ndarray)
     y = np.zeros(rows, dtype=np.float32)
     check(N.cuda().fl_matvec(ggml_type, _ptr(raw), raw.size, rows, cols, _ptr(x), _ptr(y)), "fl_matvec")
     return y
+
+
+def connect_tensor_parallel(fwd, all_gather) -> None:
+    """Connects one rank's session to its peers: `all_gather(bytes)` must return
+    every rank's bytes in rank order (a torch.distributed gather, a file, ...)."""
+    handles = list(all_gather(fwd.tp_handle()))
+    fwd.tp_connect(handles)

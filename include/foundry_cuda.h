@@ -67,8 +67,8 @@ typedef struct fl_model_desc {
     float final_softcap;      /* Gemma2 FinalLogitSoftcap (0 = off) */
     float attn_scale;         /* 1/sqrt(head_dim), or Gemma2 QueryPreAttnScalar */
     int32_t device;           /* CUDA device ordinal for this rank */
-    int32_t tp_rank, tp_size; /* tensor parallelism inside one box (1 = off) */
-    const void* nccl_id;      /* 128-byte ncclUniqueId shared by all ranks when tp_size > 1 */
+    int32_t tp_rank, tp_size; /* tensor parallelism inside one box (1 = off); see fl_session_tp_connect */
+    const void* nccl_id;      /* reserved (NULL): ranks connect through fl_session_tp_connect */
 } fl_model_desc;
 
 /* Last error message of the calling thread ("" when none). */
@@ -102,6 +102,24 @@ void fl_model_destroy(fl_model* m);
  * pass allocates (LlamaForwardPass.cs:54-62).  The KV cache lives in HBM.
  * max_ctx <= 0 uses the model's MaxContextLength. */
 int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch, int32_t kv_dtype, fl_session** out);
+
+/* Tensor parallelism (fl_model_desc.tp_size = 2, 4 or 8; one process or
+ * thread per GPU, every rank with its own model and session).  No
+ * counterpart in the reference, which runs on one CPU.  The shim shards the
+ * weights as they are uploaded: attn_q/k/v, ffn_gate/up and output by rows
+ * (heads, FFN rows, vocabulary), attn_output and ffn_down by columns.  Ranks
+ * exchange partial sums and the argmax through each other's memory over
+ * NVLink inside the token kernel.  Before its first step a tensor-parallel
+ * session must be connected: every rank gets its FL_TP_HANDLE_BYTES handle,
+ * the caller gathers the handles of all ranks in rank order (any host-side
+ * channel) and passes the array to every rank's fl_session_tp_connect.  All
+ * ranks must then run the same calls (same tokens and positions) in step;
+ * a rank that stops makes the others' next step fail with FL_ERR_TIMEOUT
+ * after ~2 s.  Logits (fl_forward) and argmax are the full-vocabulary ones
+ * on every rank. */
+#define FL_TP_HANDLE_BYTES 64
+int fl_session_tp_handle(fl_session* s, void* handle);
+int fl_session_tp_connect(fl_session* s, const void* handles);
 
 /* KvCache.Clear (KvCache.cs:138-144). */
 int fl_session_reset(fl_session* s, int32_t seq_slot);
