@@ -22,8 +22,11 @@ fused dequant-matvecs, attention over the HBM KV cache, LM head and argmax).
   position plus the LM head, extrapolated to the full model.
 - ``--impl reference``: that CPU path alone, timed per step the same way.
 
-With N > 1 GPUs each rank decodes its own replica of the model (the tensor-
-parallel path is not built yet), so scaling is weak.
+With N > 1 GPUs (torchrun, one rank per GPU) the model is tensor-parallel by
+default: every rank holds 1/N of the weights and the ranks exchange partial
+sums and the argmax over NVLink inside the token kernel, so one decode stream
+runs N times wider (strong scaling).  ``--parallel replicas`` runs N
+independent replicas instead (weak scaling).
 """
 from __future__ import annotations
 
@@ -120,6 +123,17 @@ def dist_setup():
     return ws, rank, local
 
 
+def gather_bytes(b: bytes, ws: int) -> list[bytes]:
+    """Every rank's bytes in rank order (host-side channel for the TP handles)."""
+    import torch.distributed as dist
+    global _GLOO
+    if "_GLOO" not in globals():
+        _GLOO = dist.new_group(backend="gloo")
+    out = [None] * ws
+    dist.all_gather_object(out, b, group=_GLOO)
+    return out
+
+
 def allreduce_max(v: float, ws: int) -> float:
     if ws == 1:
         return v
@@ -131,9 +145,16 @@ def allreduce_max(v: float, ws: int) -> float:
 
 
 def barrier(ws: int):
+    """Host-synchronizing barrier (gloo): every rank's host thread leaves it
+    together, so no rank's first timed kernel waits on a late peer."""
     if ws > 1:
+        import torch
         import torch.distributed as dist
-        dist.barrier()
+        torch.cuda.synchronize()
+        global _GLOO
+        if "_GLOO" not in globals():
+            _GLOO = dist.new_group(backend="gloo")
+        dist.barrier(group=_GLOO)
 
 
 def spec(args):
@@ -232,8 +253,12 @@ def run_ours(args, ws, rank, local):
     from dotnetfoundryllm_b200 import loader, runtime
     img = model_image(args, ws, rank)
     max_ctx = args.prompt + args.warmup + 2 * args.steps + 64
-    model = loader.load(img, device=local, max_ctx=max_ctx)
+    tp = ws > 1 and args.parallel == "tp"
+    model = loader.load(img, device=local, max_ctx=max_ctx, tp_rank=rank if tp else 0, tp_size=ws if tp else 1)
     fwd = runtime.CudaForwardPass(model, max_ctx=max_ctx)
+    if tp:
+        runtime.connect_tensor_parallel(fwd, lambda b: gather_bytes(b, ws))
+    streams = 1 if tp else ws  # independent decode streams of the whole job
     from dotnetfoundryllm_b200 import ggufgen
     prompt = ggufgen.prompt_ids(args.prompt, model.desc.vocab, 0)
     kv = object()
@@ -251,9 +276,9 @@ def run_ours(args, ws, rank, local):
         pos += args.warmup
     launches = fwd.launches_per_step()
     clocks = ClockSampler(local) if rank == 0 else None
-    barrier(ws)
     if clocks:
         clocks.start()
+    barrier(ws)
     ms = fwd.time_decode(tok, pos, args.steps)
     clk = clocks.stop() if clocks else None
     ms_max = allreduce_max(ms, ws)
@@ -280,7 +305,7 @@ def run_ours(args, ws, rank, local):
     step_bytes = model.weight_bytes() + kv_bytes
     ms_per_step = ms_max / args.steps
     step_gbs = step_bytes / (ms_per_step / 1e3) / 1e9  # one launch per step
-    value = ws * args.steps / (ms_max / 1e3)
+    value = streams * args.steps / (ms_max / 1e3)
     result = None
     if rank == 0:
         cpu = {"tok_s": None, "threads": 0} if args.no_cpu_baseline else cpu_sample(img, pos_timed)
@@ -290,12 +315,13 @@ def run_ours(args, ws, rank, local):
             traffic = json.loads(tf.read_text()).get(CONFIG)
         result = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF, N(0,0.02) weights)",
             "config": {"workload": f"{CONFIG} Q4_K/Q6_K bs=1 greedy decode, positions {pos_timed}.."
                                    f"{pos_timed + args.steps - 1} after a {args.prompt}-token prompt",
-                       "model": CONFIG, "global_batch": ws, "seq_len": args.prompt,
-                       "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                       "model": CONFIG, "global_batch": streams, "seq_len": args.prompt,
+                       "parallelism": f"tp{ws}" if tp else (f"replicas x{ws}" if ws > 1 else "single GPU"),
                        "l2": "inputs larger than L2 (4.9 GB of weights per step)"},
             "roofline": {"bound": "hbm", "achieved": step_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": step_gbs / peaks["hbm_gbs"], "traffic": traffic,
@@ -306,12 +332,13 @@ def run_ours(args, ws, rank, local):
             "cpu_baseline": {"value": cpu["tok_s"], "unit": "tok/s", "cores": cpu["threads"], "kind": "port",
                              "sample": "oracle (C restatement of the reference CPU path, F32 weights) on 2 of 32 "
                                        f"decoder layers at position {pos_timed} + the LM head, layer time x16"},
-            "e2e": {"value": ws * args.steps / e2e_max, "unit": "tok/s", "h2d_bytes_per_step": 16,
-                    "d2h_bytes_per_step": 4},
+            "e2e": {"value": streams * args.steps / e2e_max, "unit": "tok/s", "h2d_bytes_per_step": 16 * ws,
+                    "d2h_bytes_per_step": 4 * ws},
             "gpu_launches": launches * args.steps,
             "clocks": clk,
             "prefill_reference_style_s": prefill_s,
         }
+    barrier(ws)  # no rank frees its exchange region while a peer may still use it
     fwd.close()
     model.close()
     return result
@@ -326,6 +353,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (default: the BASELINE 2048)")
     ap.add_argument("--layers", type=int, default=0, help="profiling only: fewer blocks, same matrix shapes")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="profiling only: skip the CPU sample")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
+                    help="N > 1: tensor parallelism (default) or independent replicas")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

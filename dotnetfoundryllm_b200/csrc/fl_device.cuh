@@ -109,6 +109,14 @@ __device__ __forceinline__ int fl_ld_acquire_sys(const int* p)
     return v;
 }
 
+/* Coherent (system-scope) load of a value another GPU may have written. */
+__device__ __forceinline__ float fl_ld_relaxed_sys(const float* p)
+{
+    float v;
+    asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+    return v;
+}
+
 /* Asks L2 to fetch [p, p + bytes) (16-byte aligned, size a multiple of 16). */
 __device__ __forceinline__ void fl_prefetch_l2(const void* p, uint32_t bytes)
 {

@@ -128,8 +128,8 @@ struct FlAttnArgs {
 enum { FL_PH_EMBED = 0, FL_PH_MATVEC = 1, FL_PH_ATTN = 2, FL_PH_ATTN_COMBINE = 3, FL_PH_TP_REDUCE = 4 };
 
 /* Tensor-parallel allreduce of a row-parallel projection's output: every rank
- * signals exchange `k` of the step, waits for all, then sums the receive
- * slots of `parity` in rank order into y (mode 0: y += sum, 1: y = sum). */
+ * signals exchange `k` of the step, waits for all, then sums every rank's
+ * partial slot of `parity` in rank order into y (mode 0: y += sum, 1: y = sum). */
 struct FlTpArgs {
     int32_t k, parity, mode, n;
     float* y;
@@ -146,7 +146,8 @@ struct FlPhase {
 
 /* A rank's exchange region (one device allocation, mapped by every peer):
  * [FL_TP_MAX] int flags written by peers (epochs), [FL_TP_MAX][2] floats of
- * argmax candidates, [2][FL_TP_MAX][recv_n] receive slots, [vocab] logits. */
+ * argmax candidates, [2][FL_TP_MAX][recv_n] partial-sum slots (a rank stores
+ * its own into [parity][rank]; peers read them), [vocab] logits. */
 #define FL_TP_FLAGS_OFF 0
 #define FL_TP_BEST_OFF 128
 #define FL_TP_RECV_OFF 256

@@ -547,11 +547,9 @@ static void build_phases(fl_session* s, PhaseList& P)
      * to every rank (receive slot [parity][this rank]), then an allreduce
      * phase sums them into y */
     auto tp_partial = [&](FlMvArgs& a, int parity) {
-        a.epi = FL_EPI_PARTIAL;
-        a.tp_n = T;
-        for (int q = 0; q < T; q++)
-            a.tp_out[q] = reinterpret_cast<float*>(s->tp_peer[q] + FL_TP_RECV_OFF) +
-                          ((size_t)parity * FL_TP_MAX + m->rank) * s->xchg_recv_n;
+        /* this rank's partial rows, in its own exchange region (peers pull them) */
+        a.epi = FL_EPI_STORE;
+        a.y = reinterpret_cast<float*>(s->xchg + FL_TP_RECV_OFF) + ((size_t)parity * FL_TP_MAX + m->rank) * s->xchg_recv_n;
     };
     auto tp_reduce = [&](int k, int parity, int mode, float* y) {
         FlPhase r;

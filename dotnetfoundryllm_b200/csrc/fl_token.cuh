@@ -508,17 +508,19 @@ __device__ void tp_signal_wait(const FlTokenArgs& ta, int epoch, bool signal)
     consumer_sync();
 }
 
-/* The allreduce after a row-parallel projection: every rank has pushed its
- * partial rows into every rank's receive slot; sum them in rank order (the
- * same order on every rank, so all ranks get identical values). */
+/* The allreduce after a row-parallel projection: every rank has stored its
+ * partial rows in its own exchange region; after the flag exchange each CTA
+ * reads its rows from every rank (over NVLink for the peers) and sums them in
+ * rank order (the same order on every rank, so all ranks get identical
+ * values). */
 __device__ void phase_tp_reduce(const FlTokenArgs& ta, const FlTpArgs& r, int epoch0)
 {
     tp_signal_wait(ta, epoch0 + r.k + 1, blockIdx.x == 0);
-    const float* recv = reinterpret_cast<const float*>(ta.tp_peer[ta.tp_rank] + FL_TP_RECV_OFF) +
-                        (size_t)r.parity * FL_TP_MAX * ta.tp_recv_n;
+    const size_t off = FL_TP_RECV_OFF + ((size_t)r.parity * FL_TP_MAX) * ta.tp_recv_n * 4;
     for (int i = blockIdx.x * NC + threadIdx.x; i < r.n; i += gridDim.x * NC) {
         float sum = 0.0f;
-        for (int q = 0; q < ta.tp_size; q++) sum += __ldcg(recv + (size_t)q * ta.tp_recv_n + i);
+        for (int q = 0; q < ta.tp_size; q++)
+            sum += fl_ld_relaxed_sys(reinterpret_cast<const float*>(ta.tp_peer[q] + off) + (size_t)q * ta.tp_recv_n + i);
         r.y[i] = r.mode ? sum : __fadd_rn(__ldcg(r.y + i), sum);
     }
 }
@@ -836,6 +838,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         const int lo = S.lo(warp), hi = lo + S.len(warp);
         const int first_it = lo / n_kb;
         UnitStats st{0, 0, 0};
+        bool pushed = false; /* this thread stored epilogue rows (to peers, with tensor parallelism) */
         if (ta.detail && blockIdx.x == 0 && tid == 0) ta.detail[(size_t)ta.n_phases * NW * 4 + p] = fl_globaltimer();
 
         int i0 = lo;
@@ -904,6 +907,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                 if (lane == 0) tcnt[it] = 0;
             }
             epilogue_any(a, sg, si, tile, lane, v, pos, best_v, best_i);
+            pushed |= lane < 16;
         }
         if (ta.detail && blockIdx.x == 0 && lane == 0) {
             uint64_t* d = ta.detail + ((size_t)p * NW + warp) * 4;
@@ -913,8 +917,8 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
             d[3] = st.units;
         }
         /* rows pushed to other GPUs are visible system-wide before this CTA
-         * reports the phase done */
-        if (a.tp_n > 0) __threadfence_system();
+         * reports the phase done (only the lanes that stored them fence) */
+        if (a.tp_n > 0 && pushed) __threadfence_system();
 
         if (a.epi == FL_EPI_LOGITS) {
             /* greedy ArgMax (TensorPrimitives.IndexOfMax): per CTA, then across CTAs */
