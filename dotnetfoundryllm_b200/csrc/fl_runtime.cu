@@ -183,7 +183,7 @@ extern "C" int fl_model_create(const fl_model_desc* desc, fl_model** out)
     if (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256)
         return fail(FL_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128, 256)", d.head_dim);
     int grp = d.n_heads / d.n_kv_heads;
-    if (grp != 1 && grp != 2 && grp != 4 && grp != 8) return fail(FL_ERR_UNSUPPORTED, "GQA group %d", grp);
+    if (grp > 8 || (d.head_dim == 256 && grp > 4)) return fail(FL_ERR_UNSUPPORTED, "GQA group %d", grp);
     if (d.hidden % 32 || d.ffn % 32 || (d.n_heads * d.head_dim) % 32)
         return fail(FL_ERR_UNSUPPORTED, "dimensions must be multiples of 32");
     const int T = d.tp_size < 1 ? 1 : d.tp_size;

@@ -80,6 +80,12 @@ SPECS = {
     # small variants of the other families for the parity tests
     "tiny-mistral": ModelSpec("tiny-mistral", "mistral", 4, 512, 8, 2, 1408, 32000, 512, rope_base=1000000.0,
                               window=48, types=_llama_types(matmul=T_Q8_0, token_embd=T_Q8_0, output=T_Q8_0)),
+    # Qwen2 (QKV biases) with Qwen2-7B's 7-way query-head group (28/4 there,
+    # 14/2 here); hidden 896 and FFN 2432 are not multiples of 256, so the
+    # K-quant rows straddle blocks (expanded headers)
+    "tiny-qwen2": ModelSpec("tiny-qwen2", "qwen2", 4, 896, 14, 2, 2432, 32000, 512, rope_base=1000000.0,
+                            types=_llama_types(matmul=T_Q4_K, attn_v=T_Q6_K, ffn_down=T_Q6_K, token_embd=T_Q6_K,
+                                               output=T_Q6_K)),
     # tensor-parallel parity: every split (heads, FFN rows, vocabulary, Wo/down
     # columns in whole 256-blocks) divides for 2, 4 and 8 ranks
     "small-tp": ModelSpec("small-tp", "llama", 2, 2048, 16, 8, 4096, 32000, 512, rope_base=500000.0,

@@ -1,7 +1,8 @@
 """End-to-end parity of the device token loop against the CPU restatement.
 
-For each model family (tiny Llama-3 = BASELINE config 0, and small Mistral /
-Gemma 2 variants whose sliding windows bind), a seeded GGUF is loaded twice:
+For each model family (tiny Llama-3 = BASELINE config 0, small Mistral /
+Gemma 2 variants whose sliding windows bind, and a small Qwen2 with QKV biases
+and a 7-way query-head group), a seeded GGUF is loaded twice:
 by the oracle (F32 weights, LlamaForwardPass & co.) and through
 fl_model_upload (raw blocks).  The greedy generation loop of
 LlamaLanguageModel.GenerateAsync runs on both; the criteria are those of the
@@ -57,7 +58,7 @@ def _teacher_forced_logits(fwd: runtime.CudaForwardPass, prompt, ref_tokens):
     return np.stack(out), np.array(am)
 
 
-@pytest.fixture(scope="module", params=["tiny", "tiny-mistral", "tiny-gemma2"])
+@pytest.fixture(scope="module", params=["tiny", "tiny-mistral", "tiny-gemma2", "tiny-qwen2"])
 def family(request):
     name = request.param
     prompt, toks, logs, eos = reference(name)
