@@ -658,15 +658,14 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
     int* tcnt = reinterpret_cast<int*>(smem + Ls.tcnt);
     float* best = reinterpret_cast<float*>(smem + Ls.best);
     float* misc = reinterpret_cast<float*>(smem + Ls.misc);
-    FeedState& f = reinterpret_cast<FeedState*>(smem + Ls.feed)[warp];
+    FeedState f; /* lane 0's cursor (registers) */
 
-    if (lane == 0) {
+    f.src = nullptr;
+    f.p = -1;
+    f.run = f.left = f.it = f.slot = 0;
+    f.bytes = 0;
+    if (lane == 0)
         for (int i = 0; i < R.S; i++) fl_mbar_init(&R.full[i], 1);
-        f.src = nullptr;
-        f.p = -1;
-        f.run = f.left = f.it = f.slot = 0;
-        f.bytes = 0;
-    }
     for (int i = tid; i < TCNT; i += NT) tcnt[i] = 0;
     for (int i = tid; i < FL_XENC_ZERO_BYTES; i += NT) zero[i] = 0;
     fl_fence_mbar_init();
