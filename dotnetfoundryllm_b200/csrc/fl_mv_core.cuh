@@ -196,6 +196,17 @@ __device__ __forceinline__ void process_unit(const uint8_t* __restrict__ u, int 
         }
     }
 
+    /* every B fragment (and Q6_K/Q4_0 limb sum) of the unit up front, so the
+     * 8 MMAs do not each wait on their own shared-memory load */
+    uint2 bf[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) bf[c] = *reinterpret_cast<const uint2*>(bp + c * FL_XENC_LIMB_BYTES);
+    short2 lsum[8];
+    if constexpr ((FMT == FL_FMT_Q6K || FMT == FL_FMT_Q4_0) && !EXP) {
+#pragma unroll
+        for (int c = 0; c < 8; c++) lsum[c] = xsk[c * 4];
+    }
+
     int ia0 = 0, ia1 = 0, ib0 = 0, ib1 = 0; /* int32 accumulators: rows g, g+8 x limb pair */
 #pragma unroll
     for (int s = 0; s < 4; s++) {
@@ -231,14 +242,13 @@ __device__ __forceinline__ void process_unit(const uint8_t* __restrict__ u, int 
                 a[1] = V.z;
                 a[3] = V.w;
             }
-            const uint2 b = *reinterpret_cast<const uint2*>(bp + c * FL_XENC_LIMB_BYTES);
             int d[4];
-            fl_mma_i8<SIGNED>(d, a, b.x, b.y);
+            fl_mma_i8<SIGNED>(d, a, bf[c].x, bf[c].y);
             if constexpr ((FMT == FL_FMT_Q6K || FMT == FL_FMT_Q4_0) && !EXP) {
                 /* (q - off) x = q x - off * sum(x): integer correction per limb
                  * (expanded headers carry the offset in `sub` instead) */
                 constexpr int off = FMT == FL_FMT_Q6K ? 32 : 8;
-                const short2 S = xsk[c * 4];
+                const short2 S = lsum[c];
                 d[0] -= off * S.x;
                 d[1] -= off * S.y;
                 d[2] -= off * S.x;
