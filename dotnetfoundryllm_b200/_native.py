@@ -87,6 +87,7 @@ PUBLIC_API = [
     ("fl_session_reset", C.c_int, [C.c_void_p, C.c_int32]),
     ("fl_forward", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     ("fl_decode_greedy", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]),
+    ("fl_prefill", C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32]),
     ("fl_topk", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("fl_topk_device", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("fl_session_tp_handle", C.c_int, [C.c_void_p, C.c_void_p]),

@@ -25,7 +25,7 @@ LIB = PKG / "_lib"
 OBJ = PKG / "_build"
 
 CUDA_SOURCES = ["fl_matvec.cu", "fl_misc.cu", "fl_token.cu", "fl_token_hd64.cu", "fl_token_hd128.cu",
-                "fl_token_hd256.cu", "fl_runtime.cu"]
+                "fl_token_hd256.cu", "fl_prefill.cu", "fl_runtime.cu"]
 HOST_SOURCES = ["fl_repack.cpp"]
 HEADERS = ["fl_layout.h", "fl_decode.h", "fl_device.cuh", "fl_kernels.h", "fl_repack.h", "fl_mv_core.cuh", "fl_dequant.cuh",
            "fl_token.cuh"]
@@ -93,7 +93,7 @@ def build_cuda(force: bool = False, verbose_ptxas: bool = False) -> Path:
     with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 4))) as ex:
         list(ex.map(_run, jobs))
     if force or jobs or _stale(out, objs):
-        _run([nvcc, *ARCH, "-shared", "-o", str(out), *map(str, objs), "-lcudart", "-lpthread"])
+        _run([nvcc, *ARCH, "-shared", "-o", str(out), *map(str, objs), "-lcublasLt", "-lcudart", "-lpthread"])
     return out
 
 

@@ -195,6 +195,23 @@ size_t fl_token_smem_bytes(int n_slots, int slot_bytes, size_t scratch_bytes);
 cudaError_t fl_token_configure(const void* kernel, int* max_dyn_smem);
 cudaError_t fl_launch_token(const void* kernel, const FlTokenArgs& ta, int grid, size_t smem, cudaStream_t st);
 
+/* ── the prompt path (fl_prefill.cu) ───────────────────────────────────── */
+#include <cuda_fp16.h>
+/* split-fp16 operands: [n x 3K] halves per matrix (see fl_prefill.cu) */
+#define FL_PF_WSCALE 256.0f
+cudaError_t fl_launch_dequant_split(int32_t type, const uint8_t* raw, int rows, int cols, __half* dst, cudaStream_t st);
+cudaError_t fl_launch_embed_rows(int32_t type, const uint8_t* raw, const int32_t* tokens, int n, int h, int vocab,
+                                 float* x, int* err, cudaStream_t st);
+cudaError_t fl_launch_rows_norm(float* x, const float* y, const float* post_w, const float* w, int n, int h, float eps,
+                                int gemma, __half* out, cudaStream_t st);
+cudaError_t fl_launch_rope_kv(const float* qkv, const float* bq, const float* bk, const float* bv, const float* rope_cs,
+                              int start_pos, int n, int qd, int kvd, int hd, float* q_out, float* k_cache,
+                              float* v_cache, cudaStream_t st);
+cudaError_t fl_launch_prefill_attn(const float* q, const float* k_cache, const float* v_cache, int start_pos, int n,
+                                   int nh, int nkv, int hd, int window, float scale, float softcap, __half* out,
+                                   cudaStream_t st);
+cudaError_t fl_launch_glu(const float* g, int n, int F, int gelu, __half* act, cudaStream_t st);
+
 /* Bit-exact block dequantization (fl_dequant). */
 cudaError_t fl_launch_dequant(int32_t ggml_type, const uint8_t* src, int64_t n_blocks, float* dst, cudaStream_t st);
 

@@ -1,0 +1,363 @@
+/*
+ * fl_prefill.cu — the prompt path: all prompt tokens of a chunk through one
+ * layer at a time (the reference feeds them one by one, LlamaLanguageModel.cs:
+ * 133-137; the values are those of LlamaForwardPass.Forward for each token).
+ *
+ * The projections are dense contractions of the chunk's [n x K] activations
+ * with the layer's weights, on the tensor cores through cuBLASLt in split
+ * fp16 ("fp16x3"): every operand value v is stored as hi = fp16(v) and
+ * lo = fp16(v - hi), and one GEMM over K' = 3K with rows [x_hi | x_lo | x_hi]
+ * and [w_hi | w_hi | w_lo] sums x_hi*w_hi + x_lo*w_hi + x_hi*w_lo in fp32 —
+ * close to fp32 products of the bit-exact dequantized weights (weights are
+ * scaled by FL_PF_WSCALE first so their lo parts stay normal fp16).  These
+ * kernels do the rest:
+ * embedding rows, the residual adds fused with the norms, bias + RoPE + K/V
+ * append, causal attention over the KV cache, and the gated FFN activation.
+ */
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "fl_dequant.cuh"
+#include "fl_device.cuh"
+#include "fl_kernels.h"
+
+namespace {
+
+/* silu / gelu with the reference's evaluation order (TensorOperations.cs:78-87,
+ * 110-117), as in the decode epilogue */
+__device__ __forceinline__ float pf_silu(float g)
+{
+    float sig = 1.0f / __fadd_rn(1.0f, expf(-g));
+    return __fmul_rn(g, sig);
+}
+
+__device__ __forceinline__ float pf_gelu(float v)
+{
+    float cube = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, v), v), v);
+    float inner = __fmul_rn(0.7978845608f, __fadd_rn(v, cube));
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+/* v into the split layout of its row: [hi | lo | hi] (activations) or
+ * [hi | hi | lo] (weights), K values per part */
+__device__ __forceinline__ void store_split(__half* row3, int K, int c, float v, bool weight)
+{
+    const __half hi = __float2half_rn(v);
+    const __half lo = __float2half_rn(v - __half2float(hi));
+    row3[c] = hi;
+    row3[K + c] = weight ? hi : lo;
+    row3[2 * K + c] = weight ? lo : hi;
+}
+
+__global__ void dequant_split_kernel(int type, const uint8_t* __restrict__ raw, int64_t n, int cols,
+                                     __half* __restrict__ dst)
+{
+    for (int64_t f = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; f < n; f += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = f / cols;
+        const int c = (int)(f - r * cols);
+        store_split(dst + r * 3 * cols, cols, c, fl_dequant_elem(type, raw, f) * FL_PF_WSCALE, true);
+    }
+}
+
+__global__ void embed_rows_kernel(int type, const uint8_t* __restrict__ raw, const int32_t* __restrict__ tokens,
+                                  int h, int vocab, float* __restrict__ x, int* err)
+{
+    const int r = blockIdx.x;
+    int tok = tokens[r];
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0) atomicExch(err, FL_DEV_ERR_TOKEN);
+        tok = 0;
+    }
+    for (int i = threadIdx.x; i < h; i += blockDim.x)
+        x[(size_t)r * h + i] = fl_dequant_elem(type, raw, (int64_t)tok * h + i);
+}
+
+__device__ float block_sum(float v, float* red)
+{
+    v = fl_warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) t += red[i];
+    return t;
+}
+
+/* One row per CTA: optionally x += y (Gemma: x += GemmaRmsNorm(y, post_w)),
+ * then out = norm(x) * w as fp16 (RmsNorm, or GemmaRmsNorm with w + 1). */
+__global__ void rows_norm_kernel(float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ post_w,
+                                 const float* __restrict__ w, int h, float eps, int gemma, __half* __restrict__ out)
+{
+    __shared__ float red[32];
+    const int r = blockIdx.x;
+    float* xr = x + (size_t)r * h;
+    if (y) {
+        const float* yr = y + (size_t)r * h;
+        float rp = 1.0f;
+        if (post_w) {
+            float sp = 0.0f;
+            for (int i = threadIdx.x; i < h; i += blockDim.x) sp = fmaf(yr[i], yr[i], sp);
+            sp = block_sum(sp, red);
+            rp = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(sp, (float)h), 1e-6f));
+        }
+        for (int i = threadIdx.x; i < h; i += blockDim.x) {
+            const float add = post_w ? __fmul_rn(__fmul_rn(yr[i], rp), __fadd_rn(post_w[i], 1.0f)) : yr[i];
+            xr[i] = __fadd_rn(xr[i], add);
+        }
+        __syncthreads();
+    }
+    if (!out) return;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < h; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+    ss = block_sum(ss, red);
+    const float rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)h), eps));
+    for (int i = threadIdx.x; i < h; i += blockDim.x) {
+        const float wi = gemma ? __fadd_rn(w[i], 1.0f) : w[i];
+        store_split(out + (size_t)r * 3 * h, h, i, __fmul_rn(__fmul_rn(xr[i], rms), wi), false);
+    }
+}
+
+/* q, k, v of token r (GEMM output row [q | k | v]): bias, RoPE on q and k
+ * (TensorOperations.ApplyRope, the decode epilogue's order), q to q_out,
+ * k and v into the cache at position start_pos + r. */
+__global__ void rope_kv_kernel(const float* __restrict__ qkv, const float* __restrict__ bq, const float* __restrict__ bk,
+                               const float* __restrict__ bv, const float* __restrict__ rope_cs, int start_pos, int qd,
+                               int kvd, int hd, float* __restrict__ q_out, float* __restrict__ k_cache,
+                               float* __restrict__ v_cache)
+{
+    const int r = blockIdx.x, pos = start_pos + r, half = hd >> 1;
+    const int width = qd + 2 * kvd;
+    const float* row = qkv + (size_t)r * width;
+    for (int j = threadIdx.x; j < width; j += blockDim.x) {
+        if (j < qd + kvd) {
+            const bool is_q = j < qd;
+            const int e = is_q ? j : j - qd;
+            const float* b = is_q ? bq : bk;
+            const int pe = e ^ 1;
+            float v = row[j], partner = row[is_q ? pe : qd + pe];
+            if (b) {
+                v = __fadd_rn(v, b[e]);
+                partner = __fadd_rn(partner, b[pe]);
+            }
+            const int d = e % hd, i = d >> 1;
+            const float2 cs = *reinterpret_cast<const float2*>(rope_cs + ((size_t)pos * half + i) * 2);
+            float o;
+            if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(partner, cs.y));
+            else o = __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(v, cs.x));
+            if (is_q) q_out[(size_t)r * qd + e] = o;
+            else k_cache[(size_t)pos * kvd + e] = o;
+        } else {
+            const int e = j - qd - kvd;
+            float v = row[j];
+            if (bv) v = __fadd_rn(v, bv[e]);
+            v_cache[(size_t)pos * kvd + e] = v;
+        }
+    }
+}
+
+/* Causal attention of a chunk, fp32: CTA = (64 query tokens, one query head),
+ * 256 threads; thread t owns query rows 4*(t/16) .. +4, score columns
+ * 4*(t%16) .. +4 of each 64-key tile and output dims (HD/16)*(t%16) .. of
+ * those rows, so each row's online-softmax state lives in the 16 threads of a
+ * half-warp.  Keys of query position p: [max(0, p+1-window), p+1). */
+template <int HD>
+__global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* __restrict__ q, const float* __restrict__ k_cache,
+                                                           const float* __restrict__ v_cache, int start_pos, int n,
+                                                           int nh, int nkv, int window, float scale, float softcap,
+                                                           __half* __restrict__ out)
+{
+    constexpr int BQ = 64, BK = 64, DT = HD / 16;
+    extern __shared__ __align__(16) float sm[];
+    float* sQ = sm;                   /* [HD][BQ] (d-major) */
+    float* sK = sQ + HD * BQ;         /* [HD][BK] */
+    float* sV = sK + HD * BK;         /* [BK][HD] */
+    float* sP = sV + BK * HD;         /* [BQ][BK + 4] */
+    const int t = threadIdx.x, rg = t >> 4, cg = t & 15;
+    const int head = blockIdx.y, kvh = head / (nh / nkv);
+    const int qd = nh * HD, kvd = nkv * HD;
+    const int q0 = blockIdx.x * BQ;
+    for (int i = t; i < BQ * HD; i += 256) {
+        const int r = i / HD, d = i % HD;
+        sQ[d * BQ + r] = q0 + r < n ? q[(size_t)(q0 + r) * qd + head * HD + d] : 0.0f;
+    }
+    float m[4], l[4], o[4][DT];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        m[i] = -INFINITY;
+        l[i] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < DT; j++) o[i][j] = 0.0f;
+    }
+    const int p_first = start_pos + q0, p_last = start_pos + min(n, q0 + BQ) - 1;
+    int k_begin = 0;
+    if (window < p_first + 1) k_begin = p_first + 1 - window;
+    k_begin = k_begin / BK * BK;
+    const float inv_cap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
+    for (int k0 = k_begin; k0 <= p_last; k0 += BK) {
+        __syncthreads();
+        for (int i = t; i < BK * HD; i += 256) {
+            const int r = i / HD, d = i % HD;
+            const bool ok = k0 + r <= p_last;
+            sK[d * BK + r] = ok ? k_cache[(size_t)(k0 + r) * kvd + kvh * HD + d] : 0.0f;
+            sV[r * HD + d] = ok ? v_cache[(size_t)(k0 + r) * kvd + kvh * HD + d] : 0.0f;
+        }
+        __syncthreads();
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) s[i][j] = 0.0f;
+#pragma unroll 8
+        for (int d = 0; d < HD; d++) {
+            const float4 qa = *reinterpret_cast<const float4*>(sQ + d * BQ + 4 * rg);
+            const float4 ka = *reinterpret_cast<const float4*>(sK + d * BK + 4 * cg);
+            const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {ka.x, ka.y, ka.z, ka.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) s[i][j] = fmaf(qv[i], kv[j], s[i][j]);
+        }
+        /* scale, softcap, masks; online softmax per row (16 threads share a row) */
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int p = start_pos + q0 + 4 * rg + i;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int kp = k0 + 4 * cg + j;
+                float v = __fmul_rn(s[i][j], scale);
+                if (softcap > 0.0f) v = __fmul_rn(tanhf(__fmul_rn(v, inv_cap)), softcap);
+                const bool ok = kp <= p && kp > p - window;
+                s[i][j] = ok ? v : -INFINITY;
+                mx = fmaxf(mx, s[i][j]);
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(m[i], mx);
+            const float alpha = mn == -INFINITY ? 1.0f : expf(m[i] - mn);
+            float ps = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float pv = mn == -INFINITY ? 0.0f : expf(s[i][j] - mn);
+                s[i][j] = pv;
+                ps += pv;
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            l[i] = fmaf(l[i], alpha, ps);
+            m[i] = mn;
+#pragma unroll
+            for (int j = 0; j < DT; j++) o[i][j] *= alpha;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            *reinterpret_cast<float4*>(sP + (4 * rg + i) * (BK + 4) + 4 * cg) = make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
+        __syncthreads();
+        for (int kk = 0; kk < BK; kk++) {
+            float pr[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) pr[i] = sP[(4 * rg + i) * (BK + 4) + kk];
+            const float* vr = sV + kk * HD + DT * cg;
+#pragma unroll
+            for (int j = 0; j < DT; j += 4) {
+                const float4 vv = *reinterpret_cast<const float4*>(vr + j);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    o[i][j] = fmaf(pr[i], vv.x, o[i][j]);
+                    o[i][j + 1] = fmaf(pr[i], vv.y, o[i][j + 1]);
+                    o[i][j + 2] = fmaf(pr[i], vv.z, o[i][j + 2]);
+                    o[i][j + 3] = fmaf(pr[i], vv.w, o[i][j + 3]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = q0 + 4 * rg + i;
+        if (r >= n) continue;
+        const float inv = l[i] > 0.0f ? 1.0f / l[i] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < DT; j++) store_split(out + (size_t)r * 3 * qd, qd, head * HD + DT * cg + j, o[i][j] * inv, false);
+    }
+}
+
+/* act = silu|gelu(gate) * up for the chunk: g is the [n x 2F] output of the
+ * stacked [gate; up] projection. */
+__global__ void glu_kernel(const float* __restrict__ g, int n, int F, int gelu, __half* __restrict__ act)
+{
+    const int64_t total = (int64_t)n * F;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / F, c = i % F;
+        const float gv = g[r * 2 * F + c], up = g[r * 2 * F + F + c];
+        store_split(act + r * 3 * F, F, (int)c, __fmul_rn(gelu ? pf_gelu(gv) : pf_silu(gv), up), false);
+    }
+}
+
+} // namespace
+
+cudaError_t fl_launch_dequant_split(int32_t type, const uint8_t* raw, int rows, int cols, __half* dst, cudaStream_t st)
+{
+    const int64_t n = (int64_t)rows * cols;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    if (blocks < 1) blocks = 1;
+    dequant_split_kernel<<<(unsigned)blocks, 256, 0, st>>>(type, raw, n, cols, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_embed_rows(int32_t type, const uint8_t* raw, const int32_t* tokens, int n, int h, int vocab,
+                                 float* x, int* err, cudaStream_t st)
+{
+    embed_rows_kernel<<<n, 256, 0, st>>>(type, raw, tokens, h, vocab, x, err);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_rows_norm(float* x, const float* y, const float* post_w, const float* w, int n, int h, float eps,
+                                int gemma, __half* out, cudaStream_t st)
+{
+    rows_norm_kernel<<<n, 256, 0, st>>>(x, y, post_w, w, h, eps, gemma, out);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_rope_kv(const float* qkv, const float* bq, const float* bk, const float* bv, const float* rope_cs,
+                              int start_pos, int n, int qd, int kvd, int hd, float* q_out, float* k_cache,
+                              float* v_cache, cudaStream_t st)
+{
+    rope_kv_kernel<<<n, 256, 0, st>>>(qkv, bq, bk, bv, rope_cs, start_pos, qd, kvd, hd, q_out, k_cache, v_cache);
+    return cudaGetLastError();
+}
+
+template <int HD>
+static cudaError_t attn_hd(const float* q, const float* kc, const float* vc, int start_pos, int n, int nh, int nkv,
+                           int window, float scale, float softcap, __half* out, cudaStream_t st)
+{
+    const size_t smem = (size_t)(3 * HD * 64 + 64 * 68) * 4;
+    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((unsigned)((n + 63) / 64), (unsigned)nh);
+    prefill_attn_kernel<HD><<<grid, 256, smem, st>>>(q, kc, vc, start_pos, n, nh, nkv, window, scale, softcap, out);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_prefill_attn(const float* q, const float* k_cache, const float* v_cache, int start_pos, int n,
+                                   int nh, int nkv, int hd, int window, float scale, float softcap, __half* out,
+                                   cudaStream_t st)
+{
+    switch (hd) {
+    case 64: return attn_hd<64>(q, k_cache, v_cache, start_pos, n, nh, nkv, window, scale, softcap, out, st);
+    case 128: return attn_hd<128>(q, k_cache, v_cache, start_pos, n, nh, nkv, window, scale, softcap, out, st);
+    case 256: return attn_hd<256>(q, k_cache, v_cache, start_pos, n, nh, nkv, window, scale, softcap, out, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t fl_launch_glu(const float* g, int n, int F, int gelu, __half* act, cudaStream_t st)
+{
+    const int64_t total = (int64_t)n * F;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    if (blocks < 1) blocks = 1;
+    glu_kernel<<<(unsigned)blocks, 256, 0, st>>>(g, n, F, gelu, act);
+    return cudaGetLastError();
+}

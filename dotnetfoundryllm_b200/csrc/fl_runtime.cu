@@ -19,6 +19,8 @@
 #include <string>
 #include <vector>
 
+#include <cublasLt.h>
+
 #include "../../include/foundry_cuda.h"
 #include "fl_kernels.h"
 #include "fl_repack.h"
@@ -57,12 +59,21 @@ struct DevMatrix {
     bool present = false;
 };
 
+/* A matrix's raw GGUF blocks on the device (the prompt path dequantizes them
+ * to fp16 for its GEMMs; rows x cols in GGUF row-major order). */
+struct RawMatrix {
+    uint8_t* d = nullptr;
+    int type = -1;
+    int rows = 0, cols = 0;
+};
+
 struct Layer {
     DevMatrix wq, wk, wv, wo, gate_up, down;
     float *attn_norm = nullptr, *ffn_norm = nullptr, *post_attn_norm = nullptr, *post_ffn_norm = nullptr;
     float *bq = nullptr, *bk = nullptr, *bv = nullptr;
     std::vector<uint8_t> stash;      /* raw bytes of gate or up until its partner arrives */
     int stash_type = -1, stash_is_gate = 0;
+    RawMatrix rq, rk, rv, ro, rgate, rup, rdown; /* raw blocks for the prompt path */
 };
 
 struct fl_model {
@@ -127,6 +138,14 @@ struct fl_session {
     int32_t* tp_epoch = nullptr;
     uint8_t* tp_peer[FL_TP_MAX] = {};
     void* tp_opened[FL_TP_MAX] = {};
+    /* the prompt path, allocated by the first fl_prefill */
+    int pf_cap = 0;
+    int32_t* pf_tokens = nullptr;
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_y = nullptr;
+    __half *pf_act = nullptr, *pf_w = nullptr;
+    cublasLtHandle_t lt = nullptr;
+    void* lt_ws = nullptr;
+    size_t lt_ws_bytes = 0;
     std::vector<void*> allocs;
 };
 
@@ -318,6 +337,17 @@ extern "C" int fl_tp_slice(int32_t type, int32_t rows, int32_t cols, int32_t dim
     return FL_OK;
 }
 
+static int keep_raw(fl_model* m, RawMatrix* rm, int type, int rows, int cols, const uint8_t* raw, uint64_t nbytes)
+{
+    int rc = dalloc(m->allocs, &rm->d, nbytes);
+    if (rc) return rc;
+    CK(cudaMemcpy(rm->d, raw, nbytes, cudaMemcpyHostToDevice));
+    rm->type = type;
+    rm->rows = rows;
+    rm->cols = cols;
+    return FL_OK;
+}
+
 static bool parse_layer(const char* name, int* layer, std::string* suffix)
 {
     if (strncmp(name, "blk.", 4) != 0) return false;
@@ -392,10 +422,17 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
         {"attn_output.weight", &L.wo, h, qd, 1, h, m->qd_l},
         {"ffn_down.weight", &L.down, h, f, 1, h, m->ffn_l},
     };
+    RawMatrix* raws[] = {&L.rq, &L.rk, &L.rv, &L.ro, &L.rdown};
+    int mi = 0;
     for (auto& e : mats) {
+        RawMatrix* rm = raws[mi++];
         if (sfx == e.s) {
             if (!mat_shape_ok(e.rows, e.cols)) return fail(FL_ERR_ARG, "%s shape mismatch", name);
-            if (T == 1) return upload_matrix(m, type, e.rows, e.cols, raw, nullptr, nullptr, e.dm, (double)nbytes);
+            if (T == 1) {
+                int rc = keep_raw(m, rm, type, e.rows, e.cols, raw, nbytes);
+                if (rc) return rc;
+                return upload_matrix(m, type, e.rows, e.cols, raw, nullptr, nullptr, e.dm, (double)nbytes);
+            }
             if (e.split_cols && e.lcols % block_elems(type))
                 return fail(FL_ERR_UNSUPPORTED, "%s: %d columns per rank are not whole blocks of type %d", name,
                             e.lcols, type);
@@ -413,6 +450,9 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
             part = slice_rows(raw, type, h, rk * m->ffn_l, m->ffn_l);
             raw = part.data();
             nbytes = part.size();
+        } else {
+            int rc = keep_raw(m, is_gate ? &L.rgate : &L.rup, type, f, h, raw, nbytes);
+            if (rc) return rc;
         }
         if (L.stash_type < 0) {
             L.stash.assign(raw, raw + nbytes);
@@ -960,6 +1000,7 @@ extern "C" void fl_session_destroy(fl_session* s)
     cudaSetDevice(s->m->d.device);
     if (s->st) cudaStreamSynchronize(s->st);
     if (s->graph) cudaGraphExecDestroy(s->graph);
+    if (s->lt) cublasLtDestroy(s->lt);
     for (void* p : s->tp_opened)
         if (p) cudaIpcCloseMemHandle(p);
     for (void* p : s->allocs) cudaFree(p);
@@ -1169,6 +1210,162 @@ extern "C" int fl_topk_device(const float* logits, int32_t n, int32_t k, int32_t
                     FL_TOPK_DEVICE_MAX_N);
     if (k < 1 || k > n) return fail(FL_ERR_ARG, "k must be in [1, %d]", n);
     CK(fl_launch_topk_static(logits, n, k, ids, vals, static_cast<cudaStream_t>(stream)));
+    return FL_OK;
+}
+
+/* ── the prompt path ────────────────────────────────────────────────────── */
+#define LTCK(call)                                                                                  \
+    do {                                                                                           \
+        cublasStatus_t st_ = (call);                                                               \
+        if (st_ != CUBLAS_STATUS_SUCCESS) return fail(FL_ERR_CUDA, "%s: cuBLASLt status %d", #call, (int)st_); \
+    } while (0)
+
+/* Y[n x N] (fp32, row-major) = X · W^T for split-fp16 operands: X is
+ * [n x 3K] ([hi | lo | hi]), W is [N x 3K] ([hi | hi | lo], scaled by
+ * FL_PF_WSCALE): the column-major "TN" product over K' = 3K on the tensor
+ * cores, fp32 accumulation, alpha undoing the weight scale. */
+static int pf_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K0, int n)
+{
+    const int K = 3 * K0;
+    cublasLtMatmulDesc_t op = nullptr;
+    cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+    int rc = FL_OK;
+    cublasStatus_t st = cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F);
+    const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
+    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof ta);
+    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof tb);
+    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&la, CUDA_R_16F, K, N, K);
+    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&lb, CUDA_R_16F, K, n, K);
+    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&lc, CUDA_R_32F, N, n, N);
+    cublasLtMatmulPreference_t pref = nullptr;
+    cublasLtMatmulHeuristicResult_t heur;
+    int found = 0;
+    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatmulPreferenceCreate(&pref);
+    if (st == CUBLAS_STATUS_SUCCESS)
+        st = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &s->lt_ws_bytes,
+                                                  sizeof s->lt_ws_bytes);
+    if (st == CUBLAS_STATUS_SUCCESS)
+        st = cublasLtMatmulAlgoGetHeuristic(s->lt, op, la, lb, lc, lc, pref, 1, &heur, &found);
+    if (st == CUBLAS_STATUS_SUCCESS && found < 1) st = CUBLAS_STATUS_NOT_SUPPORTED;
+    const float alpha = 1.0f / FL_PF_WSCALE, zero = 0.0f;
+    if (st == CUBLAS_STATUS_SUCCESS)
+        st = cublasLtMatmul(s->lt, op, &alpha, W, la, X, lb, &zero, Y, lc, Y, lc, &heur.algo, s->lt_ws, s->lt_ws_bytes,
+                            s->st);
+    if (st != CUBLAS_STATUS_SUCCESS) rc = fail(FL_ERR_CUDA, "cuBLASLt GEMM %dx%dx%d: status %d", N, n, K, (int)st);
+    if (pref) cublasLtMatmulPreferenceDestroy(pref);
+    if (lc) cublasLtMatrixLayoutDestroy(lc);
+    if (lb) cublasLtMatrixLayoutDestroy(lb);
+    if (la) cublasLtMatrixLayoutDestroy(la);
+    if (op) cublasLtMatmulDescDestroy(op);
+    return rc;
+}
+
+/* split-fp16 weights of a raw matrix into dst (rows x 3*cols) */
+static int pf_dequant(fl_session* s, const RawMatrix& r, __half* dst)
+{
+    CK(fl_launch_dequant_split(r.type, r.d, r.rows, r.cols, dst, s->st));
+    return FL_OK;
+}
+
+static int pf_alloc(fl_session* s)
+{
+    fl_model* m = s->m;
+    const fl_model_desc& d = m->d;
+    const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, F = m->ffn_l;
+    const int cap = std::min(s->max_ctx, 2048);
+    const size_t wmax = std::max({(size_t)(qd + 2 * kvd) * h, (size_t)h * qd, (size_t)2 * F * h, (size_t)h * F});
+    const size_t amax = std::max({(size_t)h, (size_t)qd, (size_t)F});
+    const size_t ymax = std::max((size_t)h, (size_t)2 * F);
+    int rc = FL_OK;
+#define AL(p, b) if (!rc) rc = dalloc(s->allocs, &(p), (b))
+    AL(s->pf_tokens, (size_t)cap * 4);
+    AL(s->pf_x, (size_t)cap * h * 4);
+    AL(s->pf_qkv, (size_t)cap * (qd + 2 * kvd) * 4);
+    AL(s->pf_q, (size_t)cap * qd * 4);
+    AL(s->pf_y, (size_t)cap * ymax * 4);
+    AL(s->pf_act, (size_t)cap * amax * 3 * 2);
+    AL(s->pf_w, wmax * 3 * 2);
+    s->lt_ws_bytes = (size_t)32 << 20;
+    AL(s->lt_ws, s->lt_ws_bytes);
+#undef AL
+    if (rc) return rc;
+    LTCK(cublasLtCreate(&s->lt));
+    s->pf_cap = cap;
+    return FL_OK;
+}
+
+/* One chunk of prompt tokens through every layer (the K/V of its positions
+ * land in the session's cache). */
+static int pf_chunk(fl_session* s, const int32_t* tokens, int n, int start)
+{
+    fl_model* m = s->m;
+    const fl_model_desc& d = m->d;
+    const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, F = m->ffn_l, hd = d.head_dim;
+    const bool gemma = d.arch == FL_ARCH_GEMMA2;
+    const float eps = gemma ? 1e-6f : d.rms_eps;
+    int rc = FL_OK;
+    CK(cudaMemcpyAsync(s->pf_tokens, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s->st));
+    CK(fl_launch_embed_rows(m->emb_type, m->emb_raw, s->pf_tokens, n, h, d.vocab, s->pf_x, s->state + ST_ERR, s->st));
+    for (int l = 0; l < d.n_layers; l++) {
+        Layer& L = m->layers[(size_t)l];
+        /* residual of the previous FFN (Gemma: its post-norm first), then the attention norm */
+        const float* prev = l > 0 ? s->pf_y : nullptr;
+        const float* prev_post = l > 0 && gemma ? m->layers[(size_t)l - 1].post_ffn_norm : nullptr;
+        CK(fl_launch_rows_norm(s->pf_x, prev, prev_post, L.attn_norm, n, h, eps, gemma, s->pf_act, s->st));
+        /* q, k, v */
+        if ((rc = pf_dequant(s, L.rq, s->pf_w))) return rc;
+        if ((rc = pf_dequant(s, L.rk, s->pf_w + (size_t)qd * 3 * h))) return rc;
+        if ((rc = pf_dequant(s, L.rv, s->pf_w + (size_t)(qd + kvd) * 3 * h))) return rc;
+        if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_qkv, qd + 2 * kvd, h, n))) return rc;
+        float* kc = s->kc + (size_t)l * s->max_ctx * kvd;
+        float* vc = s->vc + (size_t)l * s->max_ctx * kvd;
+        CK(fl_launch_rope_kv(s->pf_qkv, L.bq, L.bk, L.bv, m->rope_cs, start, n, qd, kvd, hd, s->pf_q, kc, vc, s->st));
+        int window = INT_MAX;
+        if (d.arch == FL_ARCH_MISTRAL) window = d.sliding_window;
+        if (gemma && (l % 2) == 0) window = d.sliding_window; /* Gemma2ForwardPass.cs:87 */
+        if (window <= 0) window = INT_MAX;
+        CK(fl_launch_prefill_attn(s->pf_q, kc, vc, start, n, m->nh_l, m->nkv_l, hd, window, d.attn_scale,
+                                  gemma ? d.attn_softcap : 0.0f, s->pf_act, s->st));
+        /* output projection, residual (Gemma: post-attention norm), FFN norm */
+        if ((rc = pf_dequant(s, L.ro, s->pf_w))) return rc;
+        if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_y, h, qd, n))) return rc;
+        CK(fl_launch_rows_norm(s->pf_x, s->pf_y, gemma ? L.post_attn_norm : nullptr, L.ffn_norm, n, h, eps, gemma,
+                               s->pf_act, s->st));
+        /* gate and up stacked: columns [0, F) gate, [F, 2F) up */
+        if ((rc = pf_dequant(s, L.rgate, s->pf_w))) return rc;
+        if ((rc = pf_dequant(s, L.rup, s->pf_w + (size_t)F * 3 * h))) return rc;
+        if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_y, 2 * F, h, n))) return rc;
+        CK(fl_launch_glu(s->pf_y, n, F, gemma ? 1 : 0, s->pf_act, s->st));
+        if ((rc = pf_dequant(s, L.rdown, s->pf_w))) return rc;
+        if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_y, h, F, n))) return rc;
+    }
+    return FL_OK;
+}
+
+extern "C" int fl_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos)
+{
+    if (!s || (!tokens && n)) return fail(FL_ERR_ARG, "null argument");
+    if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
+    fl_model* m = s->m;
+    const fl_model_desc& d = m->d;
+    if (m->T > 1) return fail(FL_ERR_UNSUPPORTED, "the batched prompt path runs on one GPU (tp_size 1)");
+    if (n < 0 || start_pos < 0 || start_pos > s->cur_len || start_pos + n > s->max_ctx)
+        return fail(FL_ERR_ARG, "prompt positions [%d, %d) do not fit the KV cache (holds %d of %d)", start_pos,
+                    start_pos + n, s->cur_len, s->max_ctx);
+    for (int i = 0; i < n; i++)
+        if ((uint32_t)tokens[i] >= (uint32_t)d.vocab)
+            return fail(FL_ERR_ARG, "Token id %d is outside the valid vocabulary range [0, %d].", tokens[i], d.vocab - 1);
+    if (n == 0) return FL_OK;
+    if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    int rc = FL_OK;
+    if (!s->pf_cap && (rc = pf_alloc(s))) return rc;
+    for (int c = 0; c < n; c += s->pf_cap) {
+        const int len = std::min(s->pf_cap, n - c);
+        if ((rc = pf_chunk(s, tokens + c, len, start_pos + c))) return rc;
+    }
+    CK(cudaStreamSynchronize(s->st));
+    if ((rc = check_device_err(s))) return rc;
+    s->cur_len = start_pos + n;
     return FL_OK;
 }
 

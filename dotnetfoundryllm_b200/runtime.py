@@ -147,6 +147,16 @@ class CudaForwardPass:
             raise ObjectDisposedError("CudaForwardPass")
         return self._h
 
+    def prefill(self, tokens, start_pos: int = 0, kv_cache=None) -> None:
+        """The prompt path (fl_prefill): K/V of tokens at positions start_pos..
+        in one batched pass per layer; follow with forward() for the last
+        prompt token."""
+        if kv_cache is not self._kv_key or start_pos == 0:
+            check(self.lib.fl_session_reset(self.handle, 0))
+            self._kv_key = kv_cache
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(self.lib.fl_prefill(self.handle, _ptr(t), int(t.size), int(start_pos)), "fl_prefill")
+
     # ── tensor parallelism ──
     def tp_handle(self) -> bytes:
         """This rank's exchange-region handle (FL_TP_HANDLE_BYTES)."""

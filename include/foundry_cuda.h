@@ -134,6 +134,17 @@ int fl_session_reset(fl_session* s, int32_t seq_slot);
  * maximum) are copied to host memory when the pointers are non-NULL. */
 int fl_forward(fl_session* s, int32_t token, int32_t position, float* logits, int32_t* argmax);
 
+/* The prompt path: feeds tokens[0..n) at positions start_pos.. into the KV
+ * cache, all tokens of a chunk (up to 2048) through one layer at a time.
+ * Replaces the prefill loop of LlamaLanguageModel.GenerateAsync
+ * (LlamaLanguageModel.cs:133-137: Forward for every prompt token but the
+ * last, logits ignored); the last prompt token then goes through fl_forward.
+ * The projections run as fp16 tensor-core GEMMs (weights dequantized
+ * bit-exactly, then rounded to fp16; fp32 accumulation); norms, RoPE,
+ * attention and the FFN activation in fp32.  start_pos must not skip cached
+ * positions.  One GPU (tp_size 1). */
+int fl_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos);
+
 /* Greedy decode of n_steps tokens entirely on the device: step i feeds the
  * argmax of step i-1 (step 0 feeds `token`) at position start_pos + i.  The
  * generated ids are copied to out_tokens (n_steps ints) at the end.  This is
