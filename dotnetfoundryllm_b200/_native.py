@@ -97,6 +97,7 @@ PUBLIC_API = [
     ("fl_matvec", C.c_int, [C.c_int32, C.c_void_p, C.c_uint64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     ("fl_profile_step", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("fl_time_decode", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_float)]),
+    ("fl_time_prefill", C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.POINTER(C.c_float)]),
     ("fl_model_weight_bytes", C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
     ("fl_session_launches_per_step", C.c_int, [C.c_void_p, C.POINTER(C.c_int32)]),
 ]

@@ -122,6 +122,9 @@ struct FlAttnArgs {
 
 /* ── the persistent token kernel (fl_token.cu) ─────────────────────────── */
 #define FL_TK_WARPS 16
+#ifndef FL_TK_MAX_SLOTS
+#define FL_TK_MAX_SLOTS 2        /* ring slots per warp (fewer if shared memory is short) */
+#endif
 #define FL_TK_MAX_TILES 256      /* 16-row tiles of one matvec phase per CTA */
 
 /* FL_PH_ATTN writes per-split partials; FL_PH_ATTN_COMBINE merges them (same args). */
@@ -190,7 +193,7 @@ struct FlTokenArgs {
 /* The instance for (head_dim, query heads per kv head), or NULL when none is
  * built (head_dim 64/128/256, group <= 8; <= 4 for head_dim 256). */
 const void* fl_token_kernel_ptr(int head_dim, int group);
-size_t fl_token_smem_bytes(int n_slots, int slot_bytes, size_t scratch_bytes);
+size_t fl_token_smem_bytes(int n_slots, int slot_bytes, size_t scratch_bytes, int n_feed);
 /* Opts the instance into the largest dynamic shared memory (before capture). */
 cudaError_t fl_token_configure(const void* kernel, int* max_dyn_smem);
 cudaError_t fl_launch_token(const void* kernel, const FlTokenArgs& ta, int grid, size_t smem, cudaStream_t st);

@@ -936,10 +936,13 @@ static int session_build(fl_session* s)
     const size_t attn =
         (size_t)(grp * d.head_dim + FL_TK_WARPS * grp * d.head_dim + FL_TK_WARPS * 8 + per_max * grp) * 4;
     const size_t scratch = std::max(xenc, attn);
-    int n_slots = 2;
-    while (fl_token_smem_bytes(n_slots + 1, slot, scratch) <= (size_t)max_dyn) n_slots++;
-    if (fl_token_smem_bytes(n_slots, slot, scratch) > (size_t)max_dyn)
-        return fail(FL_ERR_UNSUPPORTED, "shared memory budget exceeded (x encoding %zu B)", xenc);
+    const int n_feed = (int)feed.size();
+    int n_slots = 1;
+    while (n_slots < FL_TK_MAX_SLOTS && fl_token_smem_bytes(n_slots + 1, slot, scratch, n_feed) <= (size_t)max_dyn)
+        n_slots++;
+    if (fl_token_smem_bytes(n_slots, slot, scratch, n_feed) > (size_t)max_dyn)
+        return fail(FL_ERR_UNSUPPORTED, "shared memory budget exceeded (x encoding %zu B, %d stream descriptors)", xenc,
+                    n_feed);
     FlTokenArgs& ta = s->ta;
     memset(&ta, 0, sizeof ta);
     ta.phases = s->d_phases;
@@ -967,7 +970,7 @@ static int session_build(fl_session* s)
         ta.tp_epoch = s->tp_epoch;
         for (int q = 0; q < m->T; q++) ta.tp_peer[q] = s->tp_peer[q];
     }
-    s->tk_smem = fl_token_smem_bytes(n_slots, slot, scratch);
+    s->tk_smem = fl_token_smem_bytes(n_slots, slot, scratch, n_feed);
     s->tk_grid = G;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, s->tk_kernel, 32 * FL_TK_WARPS, s->tk_smem) !=
@@ -1324,6 +1327,7 @@ static int pf_chunk(fl_session* s, const int32_t* tokens, int n, int start)
         if (d.arch == FL_ARCH_MISTRAL) window = d.sliding_window;
         if (gemma && (l % 2) == 0) window = d.sliding_window; /* Gemma2ForwardPass.cs:87 */
         if (window <= 0) window = INT_MAX;
+        if (l == d.n_layers - 1) break; /* the prompt's last-layer outputs feed nothing: only its K/V are kept */
         CK(fl_launch_prefill_attn(s->pf_q, kc, vc, start, n, m->nh_l, m->nkv_l, hd, window, d.attn_scale,
                                   gemma ? d.attn_softcap : 0.0f, s->pf_act, s->st));
         /* output projection, residual (Gemma: post-attention norm), FFN norm */
@@ -1342,7 +1346,9 @@ static int pf_chunk(fl_session* s, const int32_t* tokens, int n, int start)
     return FL_OK;
 }
 
-extern "C" int fl_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos)
+/* fl_prefill; with ms != null the chunk loop is bracketed by CUDA events on
+ * the session stream and their elapsed time is returned (benchmark hook). */
+static int prefill_impl(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos, float* ms)
 {
     if (!s || (!tokens && n)) return fail(FL_ERR_ARG, "null argument");
     if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
@@ -1359,14 +1365,36 @@ extern "C" int fl_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
     int rc = FL_OK;
     if (!s->pf_cap && (rc = pf_alloc(s))) return rc;
-    for (int c = 0; c < n; c += s->pf_cap) {
-        const int len = std::min(s->pf_cap, n - c);
-        if ((rc = pf_chunk(s, tokens + c, len, start_pos + c))) return rc;
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    if (ms) {
+        CK(cudaEventCreate(&ev[0]));
+        CK(cudaEventCreate(&ev[1]));
+        CK(cudaEventRecord(ev[0], s->st));
     }
-    CK(cudaStreamSynchronize(s->st));
-    if ((rc = check_device_err(s))) return rc;
+    for (int c = 0; c < n && !rc; c += s->pf_cap) {
+        const int len = std::min(s->pf_cap, n - c);
+        rc = pf_chunk(s, tokens + c, len, start_pos + c);
+    }
+    if (ms && !rc && cudaEventRecord(ev[1], s->st) != cudaSuccess) rc = fail(FL_ERR_CUDA, "cudaEventRecord failed");
+    if (!rc && cudaStreamSynchronize(s->st) != cudaSuccess) rc = fail(FL_ERR_CUDA, "prefill: stream failed");
+    if (!rc) rc = check_device_err(s);
+    if (ms && !rc && cudaEventElapsedTime(ms, ev[0], ev[1]) != cudaSuccess) rc = fail(FL_ERR_CUDA, "cudaEventElapsedTime failed");
+    for (cudaEvent_t e : ev)
+        if (e) cudaEventDestroy(e);
+    if (rc) return rc;
     s->cur_len = start_pos + n;
     return FL_OK;
+}
+
+extern "C" int fl_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos)
+{
+    return prefill_impl(s, tokens, n, start_pos, nullptr);
+}
+
+extern "C" int fl_time_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos, float* ms)
+{
+    if (!ms) return fail(FL_ERR_ARG, "null argument");
+    return prefill_impl(s, tokens, n, start_pos, ms);
 }
 
 /* ── stateless helpers ──────────────────────────────────────────────────── */

@@ -22,9 +22,9 @@ const void* fl_token_kernel_ptr(int head_dim, int group)
     }
 }
 
-size_t fl_token_smem_bytes(int n_slots, int slot_bytes, size_t scratch_bytes)
+size_t fl_token_smem_bytes(int n_slots, int slot_bytes, size_t scratch_bytes, int n_feed)
 {
-    return fltk::tk_layout(n_slots, slot_bytes, scratch_bytes).total;
+    return fltk::tk_layout(n_slots, slot_bytes, scratch_bytes, n_feed).total;
 }
 
 cudaError_t fl_token_configure(const void* kernel, int* max_dyn_smem)

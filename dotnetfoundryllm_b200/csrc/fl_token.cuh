@@ -55,11 +55,11 @@ struct FeedState {
 };
 
 struct TkLayout {
-    size_t ring, full, scratch, zero, outbox, tcnt, best, misc, feed, args, args_stride, total;
+    size_t ring, full, scratch, zero, outbox, tcnt, best, misc, feed, args, args_stride, fdesc, total;
 };
 
-/* n_slots is per warp. */
-__host__ __device__ inline TkLayout tk_layout(int n_slots, int slot_bytes, size_t scratch_bytes)
+/* n_slots is per warp; n_feed matvec phases have a weight-stream descriptor. */
+__host__ __device__ inline TkLayout tk_layout(int n_slots, int slot_bytes, size_t scratch_bytes, int n_feed)
 {
     TkLayout L;
     L.ring = 0;
@@ -74,7 +74,8 @@ __host__ __device__ inline TkLayout tk_layout(int n_slots, int slot_bytes, size_
     L.args = L.feed + ((NW * sizeof(FeedState) + 15) & ~(size_t)15); /* staged phase arguments */
     const size_t args = sizeof(FlMvArgs) > sizeof(FlAttnArgs) ? sizeof(FlMvArgs) : sizeof(FlAttnArgs);
     L.args_stride = (args + 15) / 16 * 16;           /* two buffers: phases alternate */
-    L.total = L.args + 2 * L.args_stride;
+    L.fdesc = (L.args + 2 * L.args_stride + 127) & ~(size_t)127; /* [n_feed] FlFeedPhase */
+    L.total = L.fdesc + (size_t)n_feed * sizeof(FlFeedPhase);
     return L;
 }
 
@@ -532,6 +533,7 @@ struct WarpRing {
     uint8_t* base;
     uint64_t* full;
     int S, slot_bytes;
+    const FlFeedPhase* fd; /* the weight-stream descriptors, in shared memory */
 };
 
 __device__ __forceinline__ int my_tiles_of(const FlMvArgs& a)
@@ -544,10 +546,10 @@ __device__ __forceinline__ int my_tiles_of(const FlMvArgs& a)
  * range in the current matvec phase, or the start of its range in the next
  * one (F.p indexes ta.feed, the matvec phases in order).  False once every
  * unit has been issued. */
-__device__ __forceinline__ bool feed_advance(const FlTokenArgs& ta, FeedState& F, int warp)
+__device__ __forceinline__ bool feed_advance(const FlTokenArgs& ta, const FlFeedPhase* fd, FeedState& F, int warp)
 {
     int kb = 0;
-    const FlFeedPhase* fp = ta.feed + (F.p < 0 ? 0 : F.p);
+    const FlFeedPhase* fp = fd + (F.p < 0 ? 0 : F.p);
     if (F.left > 0) {
         F.it++;
     } else {
@@ -557,7 +559,7 @@ __device__ __forceinline__ bool feed_advance(const FlTokenArgs& ta, FeedState& F
                 return false;
             }
             F.p++;
-            fp = ta.feed + F.p;
+            fp = fd + F.p;
             const int G = gridDim.x;
             const int tiles = fp->n_tiles > (int)blockIdx.x ? (fp->n_tiles - (int)blockIdx.x + G - 1) / G : 0;
             const int U = tiles * fp->n_kb;
@@ -594,7 +596,7 @@ __device__ __forceinline__ bool feed_advance(const FlTokenArgs& ta, FeedState& F
 /* Lane 0: issues the copy of the warp's next unit into the next ring slot. */
 __device__ __forceinline__ void feed(const FlTokenArgs& ta, const WarpRing& R, FeedState& F, int warp)
 {
-    if (F.run == 0 && !feed_advance(ta, F, warp)) return;
+    if (F.run == 0 && !feed_advance(ta, R.fd, F, warp)) return;
     const int slot = F.slot;
     const uint32_t bytes = F.bytes;
     const uint8_t* src = F.src;
@@ -647,11 +649,12 @@ template <int HD, int GMAX>
 __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__ FlTokenArgs ta)
 {
     extern __shared__ __align__(128) uint8_t smem[];
-    const TkLayout Ls = tk_layout(ta.n_slots, ta.slot_bytes, ta.scratch_bytes);
+    const TkLayout Ls = tk_layout(ta.n_slots, ta.slot_bytes, ta.scratch_bytes, ta.n_feed);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     const int G = gridDim.x;
     const WarpRing R{smem + Ls.ring + (size_t)warp * ta.n_slots * ta.slot_bytes,
-                     reinterpret_cast<uint64_t*>(smem + Ls.full) + warp * ta.n_slots, ta.n_slots, ta.slot_bytes};
+                     reinterpret_cast<uint64_t*>(smem + Ls.full) + warp * ta.n_slots, ta.n_slots, ta.slot_bytes,
+                     reinterpret_cast<const FlFeedPhase*>(smem + Ls.fdesc)};
     uint8_t* scratch = smem + Ls.scratch;
     uint8_t* zero = smem + Ls.zero;
     float* outbox = reinterpret_cast<float*>(smem + Ls.outbox);
@@ -668,6 +671,8 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         for (int i = 0; i < R.S; i++) fl_mbar_init(&R.full[i], 1);
     for (int i = tid; i < TCNT; i += NT) tcnt[i] = 0;
     for (int i = tid; i < FL_XENC_ZERO_BYTES; i += NT) zero[i] = 0;
+    /* the lane-0 cursors walk the descriptors at every run boundary: keep them on chip */
+    copy_words(smem + Ls.fdesc, ta.feed, (size_t)ta.n_feed * sizeof(FlFeedPhase));
     fl_fence_mbar_init();
     __syncthreads();
 

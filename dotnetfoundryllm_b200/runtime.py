@@ -157,6 +157,17 @@ class CudaForwardPass:
         t = np.ascontiguousarray(tokens, dtype=np.int32)
         check(self.lib.fl_prefill(self.handle, _ptr(t), int(t.size), int(start_pos)), "fl_prefill")
 
+    def time_prefill(self, tokens, start_pos: int = 0, kv_cache=None) -> float:
+        """prefill() timed on the device (CUDA events); returns milliseconds."""
+        if kv_cache is not self._kv_key or start_pos == 0:
+            check(self.lib.fl_session_reset(self.handle, 0))
+            self._kv_key = kv_cache
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        ms = C.c_float()
+        check(self.lib.fl_time_prefill(self.handle, _ptr(t), int(t.size), int(start_pos), C.byref(ms)),
+              "fl_time_prefill")
+        return ms.value
+
     # ── tensor parallelism ──
     def tp_handle(self) -> bytes:
         """This rank's exchange-region handle (FL_TP_HANDLE_BYTES)."""

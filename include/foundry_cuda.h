@@ -139,8 +139,9 @@ int fl_forward(fl_session* s, int32_t token, int32_t position, float* logits, in
  * Replaces the prefill loop of LlamaLanguageModel.GenerateAsync
  * (LlamaLanguageModel.cs:133-137: Forward for every prompt token but the
  * last, logits ignored); the last prompt token then goes through fl_forward.
- * The projections run as fp16 tensor-core GEMMs (weights dequantized
- * bit-exactly, then rounded to fp16; fp32 accumulation); norms, RoPE,
+ * The projections run as split-fp16 tensor-core GEMMs (every weight,
+ * dequantized bit-exactly, and every activation as an fp16 hi + lo pair;
+ * the three significant cross products accumulated in fp32); norms, RoPE,
  * attention and the FFN activation in fp32.  start_pos must not skip cached
  * positions.  One GPU (tp_size 1). */
 int fl_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos);
@@ -208,6 +209,10 @@ int fl_profile_step(fl_session* s, int32_t token, int32_t position, double* ms, 
  * in fl_decode_greedy and returns the elapsed device milliseconds (CUDA events
  * on the session stream). */
 int fl_time_decode(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, float* ms);
+
+/* fl_prefill with its device time: the chunk loop bracketed by CUDA events on
+ * the session stream (token upload included), elapsed milliseconds in *ms. */
+int fl_time_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos, float* ms);
 
 /* Bytes of weights one decode step reads (the GGUF payload of every matrix,
  * norm and one embedding row): the roofline numerator without the KV term. */
