@@ -74,6 +74,16 @@ class FlMatrixLayout(C.Structure):
     ]
 
 
+class FlSamplerDesc(C.Structure):
+    _fields_ = [
+        ("struct_size", C.c_int32),
+        ("temperature", C.c_float),
+        ("top_k", C.c_int32),
+        ("top_p", C.c_float),
+        ("repetition_penalty", C.c_float),
+    ]
+
+
 # Every entry point declared in include/foundry_cuda.h: (name, restype, argtypes)
 PUBLIC_API = [
     ("fl_last_error", C.c_char_p, []),
@@ -90,6 +100,8 @@ PUBLIC_API = [
     ("fl_prefill", C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32]),
     ("fl_topk", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("fl_topk_device", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("fl_sample", C.c_int, [C.c_void_p, C.POINTER(FlSamplerDesc), C.c_void_p, C.c_int32, C.c_float,
+                            C.POINTER(C.c_int32)]),
     ("fl_session_tp_handle", C.c_int, [C.c_void_p, C.c_void_p]),
     ("fl_session_tp_connect", C.c_int, [C.c_void_p, C.c_void_p]),
     ("fl_session_destroy", None, [C.c_void_p]),

@@ -222,6 +222,11 @@ cudaError_t fl_launch_dequant(int32_t ggml_type, const uint8_t* src, int64_t n_b
 cudaError_t fl_launch_topk(const float* logits, int32_t n, int32_t k, int32_t* ids, float* vals, uint8_t* scratch,
                            size_t scratch_bytes, cudaStream_t st);
 size_t fl_topk_scratch_bytes(int32_t n, int32_t k);
+/* sampling (fl_sample.cu) on a working copy w of the logits */
+cudaError_t fl_launch_sample_penalty(float* w, const int2* pairs, int n_pairs, float penalty, cudaStream_t st);
+cudaError_t fl_launch_sample_scale(float* w, int n, float inv, cudaStream_t st);
+cudaError_t fl_launch_sample_topk_mask(float* w, int n, const float* vals, int k, cudaStream_t st);
+cudaError_t fl_launch_sample_finish(float* w, int n, int greedy, float top_p, float u, int* token, cudaStream_t st);
 /* fl_launch_topk on the file-scope scratch of fl_topk_device (n <= FL_TOPK_DEVICE_MAX_N). */
 #define FL_MAX_DEVICES 64
 cudaError_t fl_launch_topk_static(const float* logits, int32_t n, int32_t k, int32_t* ids, float* vals,

@@ -105,6 +105,11 @@ struct fl_session {
     int32_t* state = nullptr; /* token, pos, argmax, step, err, head_counter */
     int32_t* attn_counter = nullptr;
     float* attn_part = nullptr;
+    /* fl_sample: working copy of the logits (+ the token), (id, count) pairs */
+    float* samp_w = nullptr;
+    int32_t* samp_tok = nullptr;
+    int2* samp_pairs = nullptr;
+    size_t samp_pairs_cap = 0;
     float* cta_best = nullptr;
     int32_t* out_tokens = nullptr;
     int32_t* topk_ids = nullptr;
@@ -1202,6 +1207,65 @@ extern "C" int fl_topk(fl_session* s, int32_t k, int32_t* ids, float* vals, floa
     CK(cudaMemcpyAsync(vals, s->topk_vals, (size_t)k * 4, cudaMemcpyDeviceToHost, s->st));
     CK(cudaStreamSynchronize(s->st));
     if (threshold) *threshold = vals[k - 1];
+    return FL_OK;
+}
+
+extern "C" int fl_sample(fl_session* s, const fl_sampler_desc* sd, const int32_t* generated, int32_t n_generated,
+                         float u, int32_t* token)
+{
+    if (!s || !sd || !token || (!generated && n_generated > 0)) return fail(FL_ERR_ARG, "null argument");
+    if (sd->struct_size != (int32_t)sizeof(fl_sampler_desc)) return fail(FL_ERR_ARG, "fl_sampler_desc size mismatch");
+    if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
+    /* SamplerPipeline's constructor checks (SamplerPipeline.cs:47-48) */
+    if (!(sd->temperature >= 0.0f)) return fail(FL_ERR_ARG, "Temperature must be >= 0.");
+    if (!(sd->top_p > 0.0f && sd->top_p <= 1.0f)) return fail(FL_ERR_ARG, "topP must be in (0, 1].");
+    if (!(sd->repetition_penalty > 0.0f)) return fail(FL_ERR_ARG, "repetition penalty must be > 0");
+    if (n_generated < 0) return fail(FL_ERR_ARG, "n_generated must be >= 0");
+    const int V = s->m->d.vocab;
+    if (cudaSetDevice(s->m->d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    /* (id, occurrences) of the in-range generated ids */
+    std::vector<int2> pairs;
+    if (sd->repetition_penalty != 1.0f && n_generated > 0) {
+        std::vector<int32_t> ids;
+        ids.reserve((size_t)n_generated);
+        for (int i = 0; i < n_generated; i++)
+            if ((uint32_t)generated[i] < (uint32_t)V) ids.push_back(generated[i]);
+        std::sort(ids.begin(), ids.end());
+        for (size_t i = 0; i < ids.size();) {
+            size_t j = i;
+            while (j < ids.size() && ids[j] == ids[i]) j++;
+            pairs.push_back(make_int2(ids[i], (int)(j - i)));
+            i = j;
+        }
+    }
+    if (!s->samp_w) {
+        int rc = dalloc(s->allocs, &s->samp_w, (size_t)V * 4 + 256);
+        if (rc) return rc;
+        s->samp_tok = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(s->samp_w) + (size_t)V * 4);
+    }
+    if (pairs.size() > s->samp_pairs_cap) {
+        const size_t cap = std::max(pairs.size(), std::max<size_t>(256, 2 * s->samp_pairs_cap));
+        int rc = dalloc(s->allocs, &s->samp_pairs, cap * sizeof(int2));
+        if (rc) return rc;
+        s->samp_pairs_cap = cap;
+    }
+    CK(cudaMemcpyAsync(s->samp_w, s->logits, (size_t)V * 4, cudaMemcpyDeviceToDevice, s->st));
+    if (!pairs.empty()) {
+        CK(cudaMemcpyAsync(s->samp_pairs, pairs.data(), pairs.size() * sizeof(int2), cudaMemcpyHostToDevice, s->st));
+        CK(fl_launch_sample_penalty(s->samp_w, s->samp_pairs, (int)pairs.size(), sd->repetition_penalty, s->st));
+    }
+    const bool greedy = sd->temperature == 0.0f;
+    if (!greedy) {
+        if (sd->temperature != 1.0f) CK(fl_launch_sample_scale(s->samp_w, V, 1.0f / sd->temperature, s->st));
+        if (sd->top_k > 0 && sd->top_k < V) {
+            CK(fl_launch_topk(s->samp_w, V, sd->top_k, s->topk_ids, s->topk_vals, s->topk_scratch,
+                              s->topk_scratch_bytes, s->st));
+            CK(fl_launch_sample_topk_mask(s->samp_w, V, s->topk_vals, sd->top_k, s->st));
+        }
+    }
+    CK(fl_launch_sample_finish(s->samp_w, V, greedy ? 1 : 0, sd->top_p, u, s->samp_tok, s->st));
+    CK(cudaMemcpyAsync(token, s->samp_tok, 4, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaStreamSynchronize(s->st));
     return FL_OK;
 }
 

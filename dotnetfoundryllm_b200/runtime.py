@@ -211,6 +211,18 @@ class CudaForwardPass:
         check(self.lib.fl_topk(self.handle, k, _ptr(ids), _ptr(vals), C.byref(thr)), "fl_topk")
         return ids, vals, thr.value
 
+    def sample(self, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0, repetition_penalty: float = 1.0,
+               generated=(), u: float = 0.0) -> int:
+        """fl_sample: the GenerateAsync sampling step on the device, on the
+        logits of the last forward(); u is the request generator's draw."""
+        d = N.FlSamplerDesc(C.sizeof(N.FlSamplerDesc), float(temperature), int(top_k), float(top_p),
+                            float(repetition_penalty))
+        g = np.ascontiguousarray(generated, dtype=np.int32)
+        tok = C.c_int32()
+        check(self.lib.fl_sample(self.handle, C.byref(d), _ptr(g) if g.size else None, int(g.size), float(u),
+                                 C.byref(tok)), "fl_sample")
+        return int(tok.value)
+
     def time_decode(self, token_id: int, start_pos: int, n_steps: int) -> float:
         ms = C.c_float()
         check(self.lib.fl_time_decode(self.handle, int(token_id), int(start_pos), int(n_steps), C.byref(ms)),
@@ -271,6 +283,71 @@ def generate_greedy(fwd: CudaForwardPass, prompt: np.ndarray, max_tokens: int, e
         if eos is not None and nxt == eos:
             break
     return np.array(toks, dtype=np.int32), (np.stack(logs) if collect_logits else None)
+
+
+class XoshiroRandom:
+    """Core/XoshiroRandom.cs: xoshiro256** seeded by four SplitMix64 outputs
+    (XoshiroRandom.cs:9-25); NextFloat rounds the top 53 bits, as a double in
+    [0, 1), to float (:44)."""
+
+    M = (1 << 64) - 1
+
+    def __init__(self, seed: int):
+        x = seed & self.M
+        self.s = []
+        for _ in range(4):
+            x = (x + 0x9E3779B97F4A7C15) & self.M
+            z = x
+            z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & self.M
+            z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & self.M
+            self.s.append(z ^ (z >> 31))
+
+    @staticmethod
+    def _rotl(x: int, k: int) -> int:
+        return ((x << k) | (x >> (64 - k))) & XoshiroRandom.M
+
+    def next_uint64(self) -> int:
+        s0, s1, s2, s3 = self.s
+        result = (self._rotl((s1 * 5) & self.M, 7) * 9) & self.M
+        t = (s1 << 17) & self.M
+        s2 ^= s0
+        s3 ^= s1
+        s1 ^= s2
+        s0 ^= s3
+        s2 ^= t
+        s3 = self._rotl(s3, 45)
+        self.s = [s0, s1, s2, s3]
+        return result
+
+    def next_float(self) -> float:
+        return float(np.float32((self.next_uint64() >> 11) * (1.0 / (1 << 53))))
+
+
+def generate(fwd: CudaForwardPass, prompt: np.ndarray, max_tokens: int, temperature: float = 1.0, top_k: int = 0,
+             top_p: float = 1.0, seed: int = 0, repetition_penalty: float = 1.0, eos: int | None = None) -> np.ndarray:
+    """LlamaLanguageModel.GenerateAsync with a SamplerPipeline
+    (LlamaLanguageModel.cs:126-293, 343-373): the prompt as in
+    generate_greedy, then every step forward → repetition penalty over the
+    tokens generated so far → SamplerPipeline.Sample, all on the device; the
+    only per-step host work is the generator draw."""
+    import time
+    rng = XoshiroRandom(seed if seed else time.monotonic_ns())
+    kv = object()
+    pos = 0
+    for i in range(len(prompt) - 1):
+        fwd.forward(int(prompt[i]), pos, kv, want_logits=False)
+        pos += 1
+    nxt = int(prompt[-1]) if len(prompt) else fwd.model.desc.bos
+    toks: list[int] = []
+    for _ in range(max_tokens):
+        fwd.forward(nxt, pos, kv, want_logits=False)
+        pos += 1
+        u = rng.next_float() if temperature != 0.0 else 0.0
+        nxt = fwd.sample(temperature, top_k, top_p, repetition_penalty, toks, u)
+        toks.append(nxt)
+        if eos is not None and nxt == eos:
+            break
+    return np.array(toks, dtype=np.int32)
 
 
 def dequantize(ggml_type: int, raw: np.ndarray, dst_len: int | None = None) -> np.ndarray:

@@ -159,6 +159,27 @@ int fl_decode_greedy(fl_session* s, int32_t token, int32_t start_pos, int32_t n_
  * keeps; ids/vals receive exactly k entries. */
 int fl_topk(fl_session* s, int32_t k, int32_t* ids, float* vals, float* threshold);
 
+/* The sampling step of LlamaLanguageModel.GenerateAsync on the device, on the
+ * logits of the session's last fl_forward (which may pass NULL logits):
+ * ApplyRepetitionPenalty over `generated` (LlamaLanguageModel.cs:183-186,
+ * 357-373), then SamplerPipeline.Sample (SamplerPipeline.cs:58-89):
+ * temperature 0 → ArgMax; else scale by 1/T, TopKSampler.ApplyTopK (top_k > 0),
+ * Softmax, TopPSampler.ApplyTopP (top_p < 1), SampleFromProbabilities with the
+ * draw `u`.  The caller draws u from the request's generator (XoshiroRandom.
+ * NextFloat, one draw per call with temperature > 0, none at temperature 0), so
+ * a seeded request sees the reference's draws.  The device logits are left
+ * unchanged.  Errors as SamplerPipeline's constructor: temperature < 0 or top_p
+ * outside (0, 1] → FL_ERR_ARG; also repetition_penalty <= 0. */
+typedef struct fl_sampler_desc {
+    int32_t struct_size;      /* sizeof(fl_sampler_desc) */
+    float temperature;        /* GenerationOptions.Temperature */
+    int32_t top_k;            /* GenerationOptions.TopK, <= 0 = off */
+    float top_p;              /* GenerationOptions.TopP, 1 = off */
+    float repetition_penalty; /* GenerationOptions.RepetitionPenalty, 1 = off */
+} fl_sampler_desc;
+int fl_sample(fl_session* s, const fl_sampler_desc* d, const int32_t* generated, int32_t n_generated, float u,
+              int32_t* token);
+
 void fl_session_destroy(fl_session* s);
 
 /* Allocation-free top-k.  No counterpart in the reference: its sampler works

@@ -395,6 +395,128 @@ void or_apply_topk(float* logits, int n, int k)
         if (logits[i] < thr) logits[i] = -INFINITY;
 }
 
+/* ── sampling ───────────────────────────────────────────────────────────── */
+
+/* XoshiroRandom (Core/XoshiroRandom.cs:9-25): the 256-bit state from four
+ * SplitMix64 outputs of the seed. */
+static uint64_t splitmix64(uint64_t* x)
+{
+    *x += 0x9e3779b97f4a7c15ULL;
+    uint64_t z = *x;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+    return z ^ (z >> 31);
+}
+
+void or_xoshiro_seed(uint64_t seed, uint64_t* st)
+{
+    for (int i = 0; i < 4; i++) st[i] = splitmix64(&seed);
+}
+
+static inline uint64_t rotl64(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+
+/* XoshiroRandom.NextUInt64 (:28-39), xoshiro256**. */
+uint64_t or_xoshiro_next(uint64_t* st)
+{
+    const uint64_t result = rotl64(st[1] * 5, 7) * 9;
+    const uint64_t t = st[1] << 17;
+    st[2] ^= st[0];
+    st[3] ^= st[1];
+    st[1] ^= st[2];
+    st[0] ^= st[3];
+    st[2] ^= t;
+    st[3] = rotl64(st[3], 45);
+    return result;
+}
+
+/* XoshiroRandom.NextFloat (:44): the top 53 bits as a double in [0, 1), then
+ * rounded to float (which can round up to 1.0f). */
+float or_xoshiro_next_float(uint64_t* st)
+{
+    return (float)((double)(or_xoshiro_next(st) >> 11) * (1.0 / 9007199254740992.0));
+}
+
+/* LlamaLanguageModel.ApplyRepetitionPenalty (LlamaLanguageModel.cs:357-373):
+ * every occurrence in the generated list, in order: positive logits divided,
+ * the others multiplied. */
+void or_apply_repetition_penalty(float* logits, int n, const int* generated, int n_generated, float penalty)
+{
+    for (int i = 0; i < n_generated; i++) {
+        const int id = generated[i];
+        if ((unsigned)id < (unsigned)n) {
+            if (logits[id] > 0.0f) logits[id] = logits[id] / penalty;
+            else logits[id] = logits[id] * penalty;
+        }
+    }
+}
+
+static const float* g_topp_probs;
+static int cmp_prob_desc(const void* a, const void* b)
+{
+    const int ia = *(const int*)a, ib = *(const int*)b;
+    const float pa = g_topp_probs[ia], pb = g_topp_probs[ib];
+    if (pa != pb) return pa < pb ? 1 : -1;
+    return (ia > ib) - (ia < ib);
+}
+
+/* TopPSampler.ApplyTopP (TopPSampler.cs:60-110): walk the tokens by
+ * descending probability, keep them until the running sum reaches p, zero the
+ * rest, renormalize.  Ties are ordered by index (Array.Sort's introsort leaves
+ * their order unspecified). */
+void or_apply_topp(float* probs, int n, float p)
+{
+    if (p >= 1.0f) return;
+    int* idx = (int*)malloc(sizeof(int) * (size_t)n);
+    float* copy = (float*)malloc(sizeof(float) * (size_t)n);
+    for (int i = 0; i < n; i++) idx[i] = i;
+    memcpy(copy, probs, sizeof(float) * (size_t)n);
+    g_topp_probs = copy;
+    qsort(idx, (size_t)n, sizeof(int), cmp_prob_desc);
+    float cum = 0.0f;
+    int reached = 0;
+    for (int r = 0; r < n; r++) {
+        if (reached) {
+            probs[idx[r]] = 0.0f;
+        } else {
+            cum = cum + probs[idx[r]];
+            if (cum >= p) reached = 1;
+        }
+    }
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) sum = sum + probs[i];
+    if (sum > 0.0f)
+        for (int i = 0; i < n; i++) probs[i] = probs[i] / sum;
+    free(idx);
+    free(copy);
+}
+
+/* TemperatureSampler.SampleFromProbabilities (TemperatureSampler.cs:53-70). */
+int or_sample_from_probs(const float* probs, int n, float u)
+{
+    float cum = 0.0f;
+    for (int i = 0; i < n; i++) {
+        cum = cum + probs[i];
+        if (u < cum) return i;
+    }
+    for (int i = n - 1; i >= 0; i--)
+        if (probs[i] > 0.0f) return i;
+    return n - 1;
+}
+
+/* SamplerPipeline.Sample (SamplerPipeline.cs:58-89). */
+int or_sampler_pipeline(float* logits, int n, float temperature, int top_k, float top_p, float u)
+{
+    if (temperature == 0.0f) return or_argmax(logits, n);
+    if (temperature != 1.0f) {
+        const float inv = 1.0f / temperature;
+        for (int i = 0; i < n; i++) logits[i] = logits[i] * inv;
+    }
+    if (top_k > 0) or_apply_topk(logits, n, top_k);
+    or_softmax(logits, n);
+    if (top_p < 1.0f) or_apply_topp(logits, n, top_p);
+    return or_sample_from_probs(logits, n, u);
+}
+
 /* TensorOperations.ApplyRope(Span<float>, float, ReadOnlySpan<float>)
  * (TensorOperations.cs:250-260): adjacent pairs rotated by pos*invFreq[i]. */
 void or_rope(float* x, float position, const float* inv, int half)

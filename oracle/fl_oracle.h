@@ -52,6 +52,17 @@ int or_argmax(const float* x, int n);
 void or_apply_topk(float* logits, int n, int k);
 void or_rope(float* x, float position, const float* inv_freqs, int half);
 
+/* ── Sampling (the Sampling project, Core/XoshiroRandom.cs, Inference) ───── */
+void or_xoshiro_seed(uint64_t seed, uint64_t* state4);
+uint64_t or_xoshiro_next(uint64_t* state4);
+float or_xoshiro_next_float(uint64_t* state4);
+void or_apply_repetition_penalty(float* logits, int n, const int* generated, int n_generated, float penalty);
+void or_apply_topp(float* probs, int n, float p);
+int or_sample_from_probs(const float* probs, int n, float u);
+/* SamplerPipeline.Sample on logits (modified in place); u is the pipeline's
+ * NextFloat draw (unused when temperature is 0). */
+int or_sampler_pipeline(float* logits, int n, float temperature, int top_k, float top_p, float u);
+
 /* ── ModelFormats.Gguf ─────────────────────────────────────────────────── */
 typedef struct or_gguf or_gguf;
 /* Parses a whole GGUF image held in memory (GgufReader.Parse).  The image

@@ -49,6 +49,13 @@ def lib() -> C.CDLL:
             "or_argmax": (i32, [vp, i32]),
             "or_apply_topk": (None, [vp, i32, i32]),
             "or_rope": (None, [vp, f32, vp, i32]),
+            "or_xoshiro_seed": (None, [C.c_uint64, vp]),
+            "or_xoshiro_next": (C.c_uint64, [vp]),
+            "or_xoshiro_next_float": (f32, [vp]),
+            "or_apply_repetition_penalty": (None, [vp, i32, vp, i32, f32]),
+            "or_apply_topp": (None, [vp, i32, f32]),
+            "or_sample_from_probs": (i32, [vp, i32, f32]),
+            "or_sampler_pipeline": (i32, [vp, i32, f32, i32, f32, f32]),
             "or_gguf_parse": (vp, [vp, i64, C.c_char_p, i32]),
             "or_gguf_free": (None, [vp]),
             "or_gguf_version": (C.c_uint32, [vp]),
@@ -176,3 +183,38 @@ class Session:
 
 def set_threads(n: int) -> None:
     lib().or_set_threads(n)
+
+
+class Xoshiro:
+    """XoshiroRandom (Core/XoshiroRandom.cs) through the C restatement."""
+
+    def __init__(self, seed: int):
+        self.state = np.zeros(4, dtype=np.uint64)
+        lib().or_xoshiro_seed(C.c_uint64(seed), _p(self.state))
+
+    def next_uint64(self) -> int:
+        return int(lib().or_xoshiro_next(_p(self.state)))
+
+    def next_float(self) -> float:
+        return float(lib().or_xoshiro_next_float(_p(self.state)))
+
+
+def apply_repetition_penalty(logits: np.ndarray, generated, penalty: float) -> np.ndarray:
+    out = np.ascontiguousarray(logits, dtype=np.float32).copy()
+    g = np.ascontiguousarray(generated, dtype=np.int32)
+    lib().or_apply_repetition_penalty(_p(out), out.size, _p(g), g.size, penalty)
+    return out
+
+
+def apply_topp(probs: np.ndarray, p: float) -> np.ndarray:
+    out = np.ascontiguousarray(probs, dtype=np.float32).copy()
+    lib().or_apply_topp(_p(out), out.size, p)
+    return out
+
+
+def sampler_pipeline(logits: np.ndarray, temperature: float, top_k: int, top_p: float, u: float) -> tuple[int, np.ndarray]:
+    """SamplerPipeline.Sample; returns the token and the final distribution
+    (the transformed logits array)."""
+    out = np.ascontiguousarray(logits, dtype=np.float32).copy()
+    tok = lib().or_sampler_pipeline(_p(out), out.size, temperature, top_k, top_p, u)
+    return int(tok), out
