@@ -59,6 +59,84 @@ __global__ void dequant_split_kernel(int type, const uint8_t* __restrict__ raw, 
     }
 }
 
+/* The 8 consecutive values f0..f0+7 (f0 a multiple of 8) of a quantized
+ * matrix: the formulas of fl_dequant_elem, with the block header decoded once
+ * and the packed quants read as whole bytes. */
+template <int TYPE>
+__device__ __forceinline__ void dequant8(const uint8_t* __restrict__ raw, int64_t f0, float (&v)[8])
+{
+    if constexpr (TYPE == FL_T_Q4_K || TYPE == FL_T_Q5_K) {
+        constexpr int bb = TYPE == FL_T_Q4_K ? 144 : 176;
+        const uint8_t* b = raw + (f0 / 256) * bb;
+        const int e0 = (int)(f0 % 256);
+        int sc, mn;
+        fl_kscale_min(b + 4, e0 / 32, &sc, &mn);
+        const float dg = __fmul_rn(fl_dq_half(b), (float)sc);
+        const float mg = __fmul_rn(fl_dq_half(b + 2), (float)mn);
+        const uint8_t* qs = b + (TYPE == FL_T_Q4_K ? 16 : 48) + (e0 >> 1);
+        const int hb = TYPE == FL_T_Q5_K ? b[16 + (e0 >> 3)] : 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            int q = (qs[i >> 1] >> ((i & 1) * 4)) & 0xF;
+            if constexpr (TYPE == FL_T_Q5_K) q |= ((hb >> i) & 1) << 4;
+            v[i] = __fsub_rn(__fmul_rn(dg, (float)q), mg);
+        }
+    } else if constexpr (TYPE == FL_T_Q6_K) {
+        const uint8_t* b = raw + (f0 / 256) * 210;
+        const int i0 = (int)(f0 % 256);
+        const float ds = __fmul_rn(fl_dq_half(b + 208), (float)(int8_t)b[192 + (i0 >> 4)]);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int e = i0 + i;
+            const int lo = (b[e >> 1] >> ((e & 1) * 4)) & 0xF;
+            const int hi = (b[128 + (e >> 2)] >> ((e & 3) * 2)) & 3;
+            v[i] = __fmul_rn(ds, (float)(((hi << 4) | lo) - 32));
+        }
+    } else if constexpr (TYPE == FL_T_Q8_0) {
+        const uint8_t* b = raw + (f0 / 32) * 34;
+        const int j0 = (int)(f0 % 32);
+        const float d = fl_dq_half(b);
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = __fmul_rn((float)(int8_t)b[2 + j0 + i], d);
+    } else { /* Q4_0 */
+        const uint8_t* b = raw + (f0 / 32) * 18;
+        const int j0 = (int)(f0 % 32);
+        const float d = fl_dq_half(b);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int j = j0 + i;
+            const int q = j < 16 ? (b[2 + j] & 0x0F) : (b[2 + j - 16] >> 4);
+            v[i] = __fmul_rn((float)(q - 8), d);
+        }
+    }
+}
+
+/* Weights in the split layout [hi | hi | lo] (scaled by FL_PF_WSCALE), 8
+ * values per thread, each part written as one 16-byte store. */
+template <int TYPE>
+__global__ void dequant_split8_kernel(const uint8_t* __restrict__ raw, int64_t n8, int cols, __half* __restrict__ dst)
+{
+    for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < n8; g += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t f0 = g * 8;
+        float v[8];
+        dequant8<TYPE>(raw, f0, v);
+        const int64_t r = f0 / cols;
+        const int c = (int)(f0 - r * cols);
+        __align__(16) __half hi[8], lo[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float x = v[i] * FL_PF_WSCALE;
+            hi[i] = __float2half_rn(x);
+            lo[i] = __float2half_rn(x - __half2float(hi[i]));
+        }
+        __half* row3 = dst + r * 3 * (int64_t)cols;
+        const uint4 h4 = *reinterpret_cast<const uint4*>(hi), l4 = *reinterpret_cast<const uint4*>(lo);
+        *reinterpret_cast<uint4*>(row3 + c) = h4;
+        *reinterpret_cast<uint4*>(row3 + cols + c) = h4;
+        *reinterpret_cast<uint4*>(row3 + 2 * cols + c) = l4;
+    }
+}
+
 __global__ void embed_rows_kernel(int type, const uint8_t* __restrict__ raw, const int32_t* __restrict__ tokens,
                                   int h, int vocab, float* __restrict__ x, int* err)
 {
@@ -299,6 +377,20 @@ __global__ void glu_kernel(const float* __restrict__ g, int n, int F, int gelu, 
 cudaError_t fl_launch_dequant_split(int32_t type, const uint8_t* raw, int rows, int cols, __half* dst, cudaStream_t st)
 {
     const int64_t n = (int64_t)rows * cols;
+    if (cols % 8 == 0) {
+        const int64_t n8 = n / 8;
+        int64_t b8 = (n8 + 255) / 256;
+        if (b8 > 148 * 16) b8 = 148 * 16;
+        if (b8 < 1) b8 = 1;
+        switch (type) {
+        case FL_T_Q4_K: dequant_split8_kernel<FL_T_Q4_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
+        case FL_T_Q5_K: dequant_split8_kernel<FL_T_Q5_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
+        case FL_T_Q6_K: dequant_split8_kernel<FL_T_Q6_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
+        case FL_T_Q8_0: dequant_split8_kernel<FL_T_Q8_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
+        case FL_T_Q4_0: dequant_split8_kernel<FL_T_Q4_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
+        default: break;
+        }
+    }
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 32) blocks = 148 * 32;
     if (blocks < 1) blocks = 1;

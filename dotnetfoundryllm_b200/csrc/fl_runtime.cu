@@ -1489,6 +1489,29 @@ extern "C" int fl_dequant(int32_t type, const void* src, uint64_t nbytes, float*
     return FL_OK;
 }
 
+/* Test hook (internal): the prefill's split-fp16 weight layout of a raw
+ * matrix, rows x 3*cols halves ([hi | hi | lo] of value * FL_PF_WSCALE). */
+extern "C" int fl_dequant_split_test(int32_t type, const void* src, uint64_t nbytes, int32_t rows, int32_t cols,
+                                     uint16_t* dst)
+{
+    if (!src || !dst || rows <= 0 || cols <= 0) return fail(FL_ERR_ARG, "bad argument");
+    const int be = block_elems(type), bb = block_bytes(type);
+    if (!be || cols % be) return fail(FL_ERR_ARG, "cols must be whole blocks");
+    if ((uint64_t)rows * cols / be * bb != nbytes) return fail(FL_ERR_ARG, "byte size mismatch");
+    uint8_t* d_src = nullptr;
+    __half* d_dst = nullptr;
+    const size_t out_bytes = (size_t)rows * cols * 3 * 2;
+    CK(cudaMalloc(&d_src, nbytes));
+    cudaError_t e = cudaMalloc(&d_dst, out_bytes);
+    if (e == cudaSuccess) e = cudaMemcpy(d_src, src, nbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = fl_launch_dequant_split(type, d_src, rows, cols, d_dst, 0);
+    if (e == cudaSuccess) e = cudaMemcpy(dst, d_dst, out_bytes, cudaMemcpyDeviceToHost);
+    cudaFree(d_src);
+    if (d_dst) cudaFree(d_dst);
+    if (e != cudaSuccess) return fail(FL_ERR_CUDA, "fl_dequant_split_test: %s", cudaGetErrorString(e));
+    return FL_OK;
+}
+
 extern "C" int fl_matvec(int32_t type, const void* w, uint64_t nbytes, int32_t rows, int32_t cols, const float* x,
                          float* y)
 {

@@ -100,3 +100,30 @@ def test_prefill_argument_errors(family):
     fwd.prefill([1, 2, 3], 0, kv)
     with pytest.raises(runtime.ArgumentError):
         fwd.prefill([4], 5, kv)  # skips cached positions
+
+
+@pytest.mark.parametrize("t", [12, 13, 14, 8, 2])  # Q4_K, Q5_K, Q6_K, Q8_0, Q4_0
+def test_split_weights_are_the_exact_values(t):
+    """The prefill's weight layout: every value bit-exactly dequantized, times
+    FL_PF_WSCALE, as fp16 hi and lo = fp16(v - hi), in [hi | hi | lo]."""
+    import ctypes as C
+    from dotnetfoundryllm_b200 import _native as N
+    from oracle import oracle as O
+    rows, cols = 48, 768
+    raw = ggufgen.random_blocks(t, rows * cols, 5, t)
+    # random bytes as well: every bit pattern of the scales and quants
+    raw2 = np.random.default_rng(t).integers(0, 256, raw.size, dtype=np.uint8)
+    for blob in (raw, raw2):
+        out = np.zeros(rows * cols * 3, dtype=np.uint16)
+        runtime.check(N.cuda().fl_dequant_split_test(t, blob.ctypes.data_as(C.c_void_p), blob.size, rows, cols,
+                                                     out.ctypes.data_as(C.c_void_p)), "fl_dequant_split_test")
+        rc, v = O.dequantize(t, blob, rows * cols)
+        assert rc == O.OK
+        x = (v.astype(np.float32) * np.float32(256.0)).reshape(rows, cols)
+        hi = x.astype(np.float16)
+        lo = (x - hi.astype(np.float32)).astype(np.float16)
+        got = out.view(np.float16).reshape(rows, 3 * cols)
+        finite = np.isfinite(x)
+        for part, want in ((0, hi), (1, hi), (2, lo)):
+            g = got[:, part * cols:(part + 1) * cols]
+            np.testing.assert_array_equal(g.view(np.uint16)[finite], want.view(np.uint16)[finite])
