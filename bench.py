@@ -274,7 +274,8 @@ def prefill_record(p: dict, d, peaks: dict, ws: int, cpu: dict) -> dict:
     fl = prefill_flops(d, p["tokens"])
     tflops = fl / (p["ms"] / 1e3) / 1e12
     return {
-        "path": "fl_prefill: split-fp16 tensor-core GEMMs (cuBLASLt) + own dequant/norm/RoPE/attention kernels",
+        "path": "fl_prefill: split-fp16 tensor-core GEMMs (cuBLASLt) for the projections and for attention's "
+                "QK^T and PV; own dequant, norm, RoPE/KV-append, masked-softmax and GLU kernels",
         "tokens": p["tokens"], "ms": p["ms"], "tok_s": ws * p["tokens"] / (p["ms"] / 1e3),
         "e2e_tok_s": ws * p["tokens"] / p["e2e_s"],
         "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
@@ -285,6 +286,25 @@ def prefill_record(p: dict, d, peaks: dict, ws: int, cpu: dict) -> dict:
                          "sample": "the reference prefills with one Forward per prompt token: the decode "
                                    "cpu_baseline sample stands for its prompt rate"},
     }
+
+
+def run_prefill_only(args):
+    """The prompt path of the benchmark model alone (for profiler launch lists)."""
+    from dotnetfoundryllm_b200 import ggufgen, loader, runtime
+    img = ggufgen.build_model(spec(args))
+    max_ctx = args.prompt + 64
+    model = loader.load(img, device=0, max_ctx=max_ctx)
+    fwd = runtime.CudaForwardPass(model, max_ctx=max_ctx)
+    pre = ggufgen.prompt_ids(args.prompt, model.desc.vocab, 0)[:-1]
+    kv = object()
+    ms = [fwd.time_prefill(pre, 0, kv) for _ in range(args.warmup + args.steps)][args.warmup:]
+    fl = prefill_flops(model.desc, len(pre))
+    peaks = load_peaks()
+    print(json.dumps({"metric": "prefill tok/s", "value": len(pre) / (max(ms) / 1e3), "unit": "tok/s",
+                      "ms": max(ms), "tokens": len(pre), "tflops": fl / (max(ms) / 1e3) / 1e12,
+                      "frac": fl / (max(ms) / 1e3) / 1e12 / peaks["bf16_tflops"]}), flush=True)
+    fwd.close()
+    model.close()
 
 
 def run_ours(args, ws, rank, local):
@@ -404,6 +424,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt length (default: the BASELINE 2048)")
     ap.add_argument("--layers", type=int, default=0, help="profiling only: fewer blocks, same matrix shapes")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="profiling only: skip the CPU sample")
+    ap.add_argument("--prefill-only", action="store_true",
+                    help="profiling only: the prompt path alone (one GPU), W + K device-timed passes")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
                     help="N > 1: tensor parallelism (default) or independent replicas")
     args = ap.parse_args()
@@ -414,6 +436,9 @@ def main():
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
         return
     ws, rank, local = dist_setup()
+    if args.prefill_only:
+        run_prefill_only(args)
+        return
     res = run_ours(args, ws, rank, local)
     if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)

@@ -210,9 +210,12 @@ cudaError_t fl_launch_rows_norm(float* x, const float* y, const float* post_w, c
 cudaError_t fl_launch_rope_kv(const float* qkv, const float* bq, const float* bk, const float* bv, const float* rope_cs,
                               int start_pos, int n, int qd, int kvd, int hd, float* q_out, float* k_cache,
                               float* v_cache, cudaStream_t st);
-cudaError_t fl_launch_prefill_attn(const float* q, const float* k_cache, const float* v_cache, int start_pos, int n,
-                                   int nh, int nkv, int hd, int window, float scale, float softcap, __half* out,
-                                   cudaStream_t st);
+cudaError_t fl_launch_attn_q_split(const float* q, int n, int nh, int nkv, int hd, __half* qs, cudaStream_t st);
+cudaError_t fl_launch_attn_kv_split(const float* kc, const float* vc, int nk, int nkp, int kvd, int hd, __half* ks,
+                                    __half* vt, cudaStream_t st);
+cudaError_t fl_launch_attn_softmax(const float* S, int rows, int n, int grp, int nkp, int start, int window, float scale,
+                                   float softcap, __half* P, cudaStream_t st);
+cudaError_t fl_launch_attn_out(const float* O, int n, int nh, int nkv, int hd, __half* act, cudaStream_t st);
 cudaError_t fl_launch_glu(const float* g, int n, int F, int gelu, __half* act, cudaStream_t st);
 
 /* Bit-exact block dequantization (fl_dequant). */

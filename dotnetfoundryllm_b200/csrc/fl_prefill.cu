@@ -234,134 +234,110 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, const float* __res
     }
 }
 
-/* Causal attention of a chunk, fp32: CTA = (64 query tokens, one query head),
- * 256 threads; thread t owns query rows 4*(t/16) .. +4, score columns
- * 4*(t%16) .. +4 of each 64-key tile and output dims (HD/16)*(t%16) .. of
- * those rows, so each row's online-softmax state lives in the 16 threads of a
- * half-warp.  Keys of query position p: [max(0, p+1-window), p+1). */
-template <int HD>
-__global__ void __launch_bounds__(256, 1) prefill_attn_kernel(const float* __restrict__ q, const float* __restrict__ k_cache,
-                                                           const float* __restrict__ v_cache, int start_pos, int n,
-                                                           int nh, int nkv, int window, float scale, float softcap,
-                                                           __half* __restrict__ out)
+/* ── causal attention of a chunk on the tensor cores ────────────────────────
+ * Per kv head g (a GEMM batch), the chunk's queries of all grp query heads of
+ * the group are the rows (t, h) = t*grp + h of one matrix, so one split-fp16
+ * GEMM forms every score against the keys 0..nk of the cache (earlier chunks
+ * included); a row kernel applies the scale, softcap, causal and window masks
+ * and the softmax; a second split-fp16 GEMM multiplies the probabilities
+ * (times 2^10, so their lo parts stay normal) by the values. */
+
+/* Q rows into [hi | lo | hi] per head, grouped by kv head. */
+__global__ void attn_q_split_kernel(const float* __restrict__ q, int n, int nh, int nkv, int hd, __half* __restrict__ qs)
 {
-    constexpr int BQ = 64, BK = 64, DT = HD / 16;
-    extern __shared__ __align__(16) float sm[];
-    float* sQ = sm;                   /* [HD][BQ] (d-major) */
-    float* sK = sQ + HD * BQ;         /* [HD][BK] */
-    float* sV = sK + HD * BK;         /* [BK][HD] */
-    float* sP = sV + BK * HD;         /* [BQ][BK + 4] */
-    const int t = threadIdx.x, rg = t >> 4, cg = t & 15;
-    const int head = blockIdx.y, kvh = head / (nh / nkv);
-    const int qd = nh * HD, kvd = nkv * HD;
-    const int q0 = blockIdx.x * BQ;
-    for (int i = t; i < BQ * HD; i += 256) {
-        const int r = i / HD, d = i % HD;
-        sQ[d * BQ + r] = q0 + r < n ? q[(size_t)(q0 + r) * qd + head * HD + d] : 0.0f;
-    }
-    float m[4], l[4], o[4][DT];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        m[i] = -INFINITY;
-        l[i] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < DT; j++) o[i][j] = 0.0f;
-    }
-    const int p_first = start_pos + q0, p_last = start_pos + min(n, q0 + BQ) - 1;
-    int k_begin = 0;
-    if (window < p_first + 1) k_begin = p_first + 1 - window;
-    k_begin = k_begin / BK * BK;
-    const float inv_cap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
-    for (int k0 = k_begin; k0 <= p_last; k0 += BK) {
-        __syncthreads();
-        for (int i = t; i < BK * HD; i += 256) {
-            const int r = i / HD, d = i % HD;
-            const bool ok = k0 + r <= p_last;
-            sK[d * BK + r] = ok ? k_cache[(size_t)(k0 + r) * kvd + kvh * HD + d] : 0.0f;
-            sV[r * HD + d] = ok ? v_cache[(size_t)(k0 + r) * kvd + kvh * HD + d] : 0.0f;
-        }
-        __syncthreads();
-        float s[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) s[i][j] = 0.0f;
-#pragma unroll 8
-        for (int d = 0; d < HD; d++) {
-            const float4 qa = *reinterpret_cast<const float4*>(sQ + d * BQ + 4 * rg);
-            const float4 ka = *reinterpret_cast<const float4*>(sK + d * BK + 4 * cg);
-            const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {ka.x, ka.y, ka.z, ka.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) s[i][j] = fmaf(qv[i], kv[j], s[i][j]);
-        }
-        /* scale, softcap, masks; online softmax per row (16 threads share a row) */
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int p = start_pos + q0 + 4 * rg + i;
-            float mx = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int kp = k0 + 4 * cg + j;
-                float v = __fmul_rn(s[i][j], scale);
-                if (softcap > 0.0f) v = __fmul_rn(tanhf(__fmul_rn(v, inv_cap)), softcap);
-                const bool ok = kp <= p && kp > p - window;
-                s[i][j] = ok ? v : -INFINITY;
-                mx = fmaxf(mx, s[i][j]);
-            }
-#pragma unroll
-            for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-            const float mn = fmaxf(m[i], mx);
-            const float alpha = mn == -INFINITY ? 1.0f : expf(m[i] - mn);
-            float ps = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float pv = mn == -INFINITY ? 0.0f : expf(s[i][j] - mn);
-                s[i][j] = pv;
-                ps += pv;
-            }
-#pragma unroll
-            for (int off = 1; off < 16; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-            l[i] = fmaf(l[i], alpha, ps);
-            m[i] = mn;
-#pragma unroll
-            for (int j = 0; j < DT; j++) o[i][j] *= alpha;
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-            *reinterpret_cast<float4*>(sP + (4 * rg + i) * (BK + 4) + 4 * cg) = make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
-        __syncthreads();
-        for (int kk = 0; kk < BK; kk++) {
-            float pr[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) pr[i] = sP[(4 * rg + i) * (BK + 4) + kk];
-            const float* vr = sV + kk * HD + DT * cg;
-#pragma unroll
-            for (int j = 0; j < DT; j += 4) {
-                const float4 vv = *reinterpret_cast<const float4*>(vr + j);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    o[i][j] = fmaf(pr[i], vv.x, o[i][j]);
-                    o[i][j + 1] = fmaf(pr[i], vv.y, o[i][j + 1]);
-                    o[i][j + 2] = fmaf(pr[i], vv.z, o[i][j + 2]);
-                    o[i][j + 3] = fmaf(pr[i], vv.w, o[i][j + 3]);
-                }
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int r = q0 + 4 * rg + i;
-        if (r >= n) continue;
-        const float inv = l[i] > 0.0f ? 1.0f / l[i] : 0.0f;
-#pragma unroll
-        for (int j = 0; j < DT; j++) store_split(out + (size_t)r * 3 * qd, qd, head * HD + DT * cg + j, o[i][j] * inv, false);
+    const int t = blockIdx.x, qd = nh * hd, grp = nh / nkv;
+    for (int i = threadIdx.x; i < qd; i += blockDim.x) {
+        const int head = i / hd, d = i - head * hd, g = head / grp, h = head - g * grp;
+        __half* row = qs + ((size_t)g * n * grp + (size_t)t * grp + h) * 3 * hd;
+        store_split(row, hd, d, q[(size_t)t * qd + i], false);
     }
 }
 
-/* act = silu|gelu(gate) * up for the chunk: g is the [n x 2F] output of the
- * stacked [gate; up] projection. */
+/* Keys 0..nkp of every kv head into [hi | hi | lo] rows; values transposed,
+ * one [hi | hi | lo] row of nkp keys per (kv head, dim); zero past nk.  A
+ * 32-key x 32-dim tile per block, staged so both sides are coalesced. */
+__global__ void attn_kv_split_kernel(const float* __restrict__ kc, const float* __restrict__ vc, int nk, int nkp,
+                                     int kvd, int hd, __half* __restrict__ ks, __half* __restrict__ vt)
+{
+    __shared__ float tile[32][33];
+    const int k0 = blockIdx.x * 32, c0 = blockIdx.y * 32, tx = threadIdx.x, ty = threadIdx.y;
+    for (int r = ty; r < 32; r += 8) {
+        const int key = k0 + r, c = c0 + tx;
+        const bool ok = key < nk && c < kvd;
+        const float kv = ok ? kc[(size_t)key * kvd + c] : 0.0f;
+        const float vv = ok ? vc[(size_t)key * kvd + c] : 0.0f;
+        if (key < nkp && c < kvd) {
+            const int g = c / hd, d = c - g * hd;
+            store_split(ks + ((size_t)g * nkp + key) * 3 * hd, hd, d, kv, true);
+        }
+        tile[r][tx] = vv;
+    }
+    __syncthreads();
+    for (int r = ty; r < 32; r += 8) {
+        const int c = c0 + r, key = k0 + tx;
+        if (c < kvd && key < nkp) {
+            const int g = c / hd, d = c - g * hd;
+            store_split(vt + ((size_t)g * hd + d) * 3 * nkp, nkp, key, tile[tx][r], true);
+        }
+    }
+}
+
+__device__ float attn_block_reduce(float v, bool is_max, float* red)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = is_max ? fl_warp_max(v) : fl_warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        float t = lane < (int)(blockDim.x >> 5) ? red[lane] : (is_max ? -INFINITY : 0.0f);
+        t = is_max ? fl_warp_max(t) : fl_warp_sum(t);
+        if (lane == 0) red[32] = t;
+    }
+    __syncthreads();
+    return red[32];
+}
+
+/* Row (g, t, h): ComputeAttention's score (dot * scale [→ softcap]) over the
+ * keys [max(0, p+1-window), p+1) of position p = start + t, then Softmax
+ * (max, exp(s - max), sum, divide); written as 2^10 * p in [hi | lo | hi]. */
+__global__ void attn_softmax_kernel(const float* __restrict__ S, int n, int grp, int nkp, int start, int window,
+                                    float scale, float softcap, __half* __restrict__ P)
+{
+    __shared__ float red[33];
+    const size_t row = blockIdx.x;
+    const int t = (int)((row % ((size_t)n * grp)) / grp), pos = start + t;
+    const int k_lo = window < pos + 1 ? pos + 1 - window : 0, k_hi = pos;
+    const float* srow = S + row * nkp;
+    __half* prow = P + row * 3 * (size_t)nkp;
+    const float inv_cap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
+    auto score = [&](int k) {
+        float v = __fmul_rn(srow[k], scale);
+        if (softcap > 0.0f) v = __fmul_rn(tanhf(__fmul_rn(v, inv_cap)), softcap);
+        return v;
+    };
+    float mx = -INFINITY;
+    for (int k = k_lo + threadIdx.x; k <= k_hi; k += blockDim.x) mx = fmaxf(mx, score(k));
+    mx = attn_block_reduce(mx, true, red);
+    float sum = 0.0f;
+    for (int k = k_lo + threadIdx.x; k <= k_hi; k += blockDim.x) sum += expf(__fsub_rn(score(k), mx));
+    sum = attn_block_reduce(sum, false, red);
+    for (int k = threadIdx.x; k < nkp; k += blockDim.x) {
+        const float p = k >= k_lo && k <= k_hi ? __fdiv_rn(expf(__fsub_rn(score(k), mx)), sum) : 0.0f;
+        store_split(prow, nkp, k, p * 1024.0f, false);
+    }
+}
+
+/* The attention output rows (g, t, h) into the Wo input layout [t][qd]. */
+__global__ void attn_out_kernel(const float* __restrict__ O, int n, int nh, int nkv, int hd, __half* __restrict__ act)
+{
+    const int t = blockIdx.x, qd = nh * hd, grp = nh / nkv;
+    for (int i = threadIdx.x; i < qd; i += blockDim.x) {
+        const int head = i / hd, d = i - head * hd, g = head / grp, h = head - g * grp;
+        store_split(act + (size_t)t * 3 * qd, qd, i, O[((size_t)g * n * grp + (size_t)t * grp + h) * hd + d], false);
+    }
+}
+
 __global__ void glu_kernel(const float* __restrict__ g, int n, int F, int gelu, __half* __restrict__ act)
 {
     const int64_t total = (int64_t)n * F;
@@ -420,28 +396,31 @@ cudaError_t fl_launch_rope_kv(const float* qkv, const float* bq, const float* bk
     return cudaGetLastError();
 }
 
-template <int HD>
-static cudaError_t attn_hd(const float* q, const float* kc, const float* vc, int start_pos, int n, int nh, int nkv,
-                           int window, float scale, float softcap, __half* out, cudaStream_t st)
+cudaError_t fl_launch_attn_q_split(const float* q, int n, int nh, int nkv, int hd, __half* qs, cudaStream_t st)
 {
-    const size_t smem = (size_t)(3 * HD * 64 + 64 * 68) * 4;
-    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)((n + 63) / 64), (unsigned)nh);
-    prefill_attn_kernel<HD><<<grid, 256, smem, st>>>(q, kc, vc, start_pos, n, nh, nkv, window, scale, softcap, out);
+    attn_q_split_kernel<<<n, 256, 0, st>>>(q, n, nh, nkv, hd, qs);
     return cudaGetLastError();
 }
 
-cudaError_t fl_launch_prefill_attn(const float* q, const float* k_cache, const float* v_cache, int start_pos, int n,
-                                   int nh, int nkv, int hd, int window, float scale, float softcap, __half* out,
-                                   cudaStream_t st)
+cudaError_t fl_launch_attn_kv_split(const float* kc, const float* vc, int nk, int nkp, int kvd, int hd, __half* ks,
+                                    __half* vt, cudaStream_t st)
 {
-    switch (hd) {
-    case 64: return attn_hd<64>(q, k_cache, v_cache, start_pos, n, nh, nkv, window, scale, softcap, out, st);
-    case 128: return attn_hd<128>(q, k_cache, v_cache, start_pos, n, nh, nkv, window, scale, softcap, out, st);
-    case 256: return attn_hd<256>(q, k_cache, v_cache, start_pos, n, nh, nkv, window, scale, softcap, out, st);
-    default: return cudaErrorInvalidValue;
-    }
+    dim3 grid((unsigned)((nkp + 31) / 32), (unsigned)((kvd + 31) / 32));
+    attn_kv_split_kernel<<<grid, dim3(32, 8), 0, st>>>(kc, vc, nk, nkp, kvd, hd, ks, vt);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_attn_softmax(const float* S, int rows, int n, int grp, int nkp, int start, int window, float scale,
+                                   float softcap, __half* P, cudaStream_t st)
+{
+    attn_softmax_kernel<<<rows, 256, 0, st>>>(S, n, grp, nkp, start, window, scale, softcap, P);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_attn_out(const float* O, int n, int nh, int nkv, int hd, __half* act, cudaStream_t st)
+{
+    attn_out_kernel<<<n, 256, 0, st>>>(O, n, nh, nkv, hd, act);
+    return cudaGetLastError();
 }
 
 cudaError_t fl_launch_glu(const float* g, int n, int F, int gelu, __half* act, cudaStream_t st)

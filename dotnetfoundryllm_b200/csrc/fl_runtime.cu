@@ -148,6 +148,10 @@ struct fl_session {
     int32_t* pf_tokens = nullptr;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_y = nullptr;
     __half *pf_act = nullptr, *pf_w = nullptr;
+    /* attention of a chunk: split Q/K/V^T, scores, split probabilities, output */
+    int pf_nkmax = 0;
+    __half *pf_qs = nullptr, *pf_ks = nullptr, *pf_vt = nullptr, *pf_p = nullptr;
+    float *pf_s = nullptr, *pf_o = nullptr;
     cublasLtHandle_t lt = nullptr;
     void* lt_ws = nullptr;
     size_t lt_ws_bytes = 0;
@@ -1287,13 +1291,12 @@ extern "C" int fl_topk_device(const float* logits, int32_t n, int32_t k, int32_t
         if (st_ != CUBLAS_STATUS_SUCCESS) return fail(FL_ERR_CUDA, "%s: cuBLASLt status %d", #call, (int)st_); \
     } while (0)
 
-/* Y[n x N] (fp32, row-major) = X · W^T for split-fp16 operands: X is
- * [n x 3K] ([hi | lo | hi]), W is [N x 3K] ([hi | hi | lo], scaled by
- * FL_PF_WSCALE): the column-major "TN" product over K' = 3K on the tensor
- * cores, fp32 accumulation, alpha undoing the weight scale. */
-static int pf_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K0, int n)
+/* Y[n x N] (fp32, row-major, ld N) = alpha * X[n x K] · W[N x K]^T (fp16,
+ * row-major, ld K): the column-major "TN" product Y^T = W · X^T on the tensor
+ * cores with fp32 accumulation, `batch` times with the given element strides. */
+static int lt_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K, int n, float alpha,
+                   int batch = 1, int64_t sW = 0, int64_t sX = 0, int64_t sY = 0)
 {
-    const int K = 3 * K0;
     cublasLtMatmulDesc_t op = nullptr;
     cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
     int rc = FL_OK;
@@ -1304,6 +1307,16 @@ static int pf_gemm(fl_session* s, const __half* W, const __half* X, float* Y, in
     if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&la, CUDA_R_16F, K, N, K);
     if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&lb, CUDA_R_16F, K, n, K);
     if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&lc, CUDA_R_32F, N, n, N);
+    if (batch > 1) {
+        const cublasLtMatrixLayout_t ls[3] = {la, lb, lc};
+        const int64_t strides[3] = {sW, sX, sY};
+        for (int i = 0; i < 3 && st == CUBLAS_STATUS_SUCCESS; i++) {
+            st = cublasLtMatrixLayoutSetAttribute(ls[i], CUBLASLT_MATRIX_LAYOUT_BATCH_COUNT, &batch, sizeof batch);
+            if (st == CUBLAS_STATUS_SUCCESS)
+                st = cublasLtMatrixLayoutSetAttribute(ls[i], CUBLASLT_MATRIX_LAYOUT_STRIDED_BATCH_OFFSET, &strides[i],
+                                                      sizeof strides[i]);
+        }
+    }
     cublasLtMatmulPreference_t pref = nullptr;
     cublasLtMatmulHeuristicResult_t heur;
     int found = 0;
@@ -1314,17 +1327,25 @@ static int pf_gemm(fl_session* s, const __half* W, const __half* X, float* Y, in
     if (st == CUBLAS_STATUS_SUCCESS)
         st = cublasLtMatmulAlgoGetHeuristic(s->lt, op, la, lb, lc, lc, pref, 1, &heur, &found);
     if (st == CUBLAS_STATUS_SUCCESS && found < 1) st = CUBLAS_STATUS_NOT_SUPPORTED;
-    const float alpha = 1.0f / FL_PF_WSCALE, zero = 0.0f;
+    const float zero = 0.0f;
     if (st == CUBLAS_STATUS_SUCCESS)
         st = cublasLtMatmul(s->lt, op, &alpha, W, la, X, lb, &zero, Y, lc, Y, lc, &heur.algo, s->lt_ws, s->lt_ws_bytes,
                             s->st);
-    if (st != CUBLAS_STATUS_SUCCESS) rc = fail(FL_ERR_CUDA, "cuBLASLt GEMM %dx%dx%d: status %d", N, n, K, (int)st);
+    if (st != CUBLAS_STATUS_SUCCESS)
+        rc = fail(FL_ERR_CUDA, "cuBLASLt GEMM %dx%dx%d (batch %d): status %d", N, n, K, batch, (int)st);
     if (pref) cublasLtMatmulPreferenceDestroy(pref);
     if (lc) cublasLtMatrixLayoutDestroy(lc);
     if (lb) cublasLtMatrixLayoutDestroy(lb);
     if (la) cublasLtMatrixLayoutDestroy(la);
     if (op) cublasLtMatmulDescDestroy(op);
     return rc;
+}
+
+/* A projection in split fp16: X is [n x 3K0] ([hi | lo | hi]), W is
+ * [N x 3K0] ([hi | hi | lo], scaled by FL_PF_WSCALE, which alpha undoes). */
+static int pf_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K0, int n)
+{
+    return lt_gemm(s, W, X, Y, N, 3 * K0, n, 1.0f / FL_PF_WSCALE);
 }
 
 /* split-fp16 weights of a raw matrix into dst (rows x 3*cols) */
@@ -1339,7 +1360,12 @@ static int pf_alloc(fl_session* s)
     fl_model* m = s->m;
     const fl_model_desc& d = m->d;
     const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, F = m->ffn_l;
-    const int cap = std::min(s->max_ctx, 2048);
+    /* scores and split probabilities take 10 bytes per (query head, key) of
+     * a chunk row: the chunk shrinks so they stay within 4 GiB */
+    const int nkmax = (s->max_ctx + 7) & ~7;
+    const size_t per_tok = (size_t)m->nh_l * nkmax * 10;
+    int cap = std::min(s->max_ctx, 2048);
+    if ((size_t)cap * per_tok > ((size_t)4 << 30)) cap = std::max(16, (int)((((size_t)4 << 30) / per_tok) & ~(size_t)15));
     const size_t wmax = std::max({(size_t)(qd + 2 * kvd) * h, (size_t)h * qd, (size_t)2 * F * h, (size_t)h * F});
     const size_t amax = std::max({(size_t)h, (size_t)qd, (size_t)F});
     const size_t ymax = std::max((size_t)h, (size_t)2 * F);
@@ -1352,6 +1378,13 @@ static int pf_alloc(fl_session* s)
     AL(s->pf_y, (size_t)cap * ymax * 4);
     AL(s->pf_act, (size_t)cap * amax * 3 * 2);
     AL(s->pf_w, wmax * 3 * 2);
+    AL(s->pf_qs, (size_t)cap * qd * 3 * 2);
+    AL(s->pf_ks, (size_t)nkmax * kvd * 3 * 2);
+    AL(s->pf_vt, (size_t)nkmax * kvd * 3 * 2);
+    AL(s->pf_s, (size_t)cap * m->nh_l * nkmax * 4);
+    AL(s->pf_p, (size_t)cap * m->nh_l * nkmax * 3 * 2);
+    AL(s->pf_o, (size_t)cap * qd * 4);
+    s->pf_nkmax = nkmax;
     s->lt_ws_bytes = (size_t)32 << 20;
     AL(s->lt_ws, s->lt_ws_bytes);
 #undef AL
@@ -1392,8 +1425,20 @@ static int pf_chunk(fl_session* s, const int32_t* tokens, int n, int start)
         if (gemma && (l % 2) == 0) window = d.sliding_window; /* Gemma2ForwardPass.cs:87 */
         if (window <= 0) window = INT_MAX;
         if (l == d.n_layers - 1) break; /* the prompt's last-layer outputs feed nothing: only its K/V are kept */
-        CK(fl_launch_prefill_attn(s->pf_q, kc, vc, start, n, m->nh_l, m->nkv_l, hd, window, d.attn_scale,
-                                  gemma ? d.attn_softcap : 0.0f, s->pf_act, s->st));
+        {
+            const int nkv = m->nkv_l, grp = m->nh_l / nkv, nk = start + n, nkp = (nk + 7) & ~7, rows = n * grp;
+            CK(fl_launch_attn_q_split(s->pf_q, n, m->nh_l, nkv, hd, s->pf_qs, s->st));
+            CK(fl_launch_attn_kv_split(kc, vc, nk, nkp, kvd, hd, s->pf_ks, s->pf_vt, s->st));
+            if ((rc = lt_gemm(s, s->pf_ks, s->pf_qs, s->pf_s, nkp, 3 * hd, rows, 1.0f, nkv, (int64_t)nkp * 3 * hd,
+                              (int64_t)rows * 3 * hd, (int64_t)rows * nkp)))
+                return rc;
+            CK(fl_launch_attn_softmax(s->pf_s, nkv * rows, n, grp, nkp, start, window, d.attn_scale,
+                                      gemma ? d.attn_softcap : 0.0f, s->pf_p, s->st));
+            if ((rc = lt_gemm(s, s->pf_vt, s->pf_p, s->pf_o, hd, 3 * nkp, rows, 1.0f / 1024.0f, nkv,
+                              (int64_t)hd * 3 * nkp, (int64_t)rows * 3 * nkp, (int64_t)rows * hd)))
+                return rc;
+            CK(fl_launch_attn_out(s->pf_o, n, m->nh_l, nkv, hd, s->pf_act, s->st));
+        }
         /* output projection, residual (Gemma: post-attention norm), FFN norm */
         if ((rc = pf_dequant(s, L.ro, s->pf_w))) return rc;
         if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_y, h, qd, n))) return rc;
