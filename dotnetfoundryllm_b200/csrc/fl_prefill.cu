@@ -301,10 +301,12 @@ __device__ float attn_block_reduce(float v, bool is_max, float* red)
 /* Row (g, t, h): ComputeAttention's score (dot * scale [→ softcap]) over the
  * keys [max(0, p+1-window), p+1) of position p = start + t, then Softmax
  * (max, exp(s - max), sum, divide); written as 2^10 * p in [hi | lo | hi]. */
+template <bool STAGED>
 __global__ void attn_softmax_kernel(const float* __restrict__ S, int n, int grp, int nkp, int start, int window,
                                     float scale, float softcap, __half* __restrict__ P)
 {
     __shared__ float red[33];
+    extern __shared__ float srow_s[]; /* STAGED: the row's scores, then exp(score - max) */
     const size_t row = blockIdx.x;
     const int t = (int)((row % ((size_t)n * grp)) / grp), pos = start + t;
     const int k_lo = window < pos + 1 ? pos + 1 - window : 0, k_hi = pos;
@@ -317,13 +319,22 @@ __global__ void attn_softmax_kernel(const float* __restrict__ S, int n, int grp,
         return v;
     };
     float mx = -INFINITY;
-    for (int k = k_lo + threadIdx.x; k <= k_hi; k += blockDim.x) mx = fmaxf(mx, score(k));
+    for (int k = k_lo + threadIdx.x; k <= k_hi; k += blockDim.x) {
+        const float v = score(k);
+        if constexpr (STAGED) srow_s[k] = v;
+        mx = fmaxf(mx, v);
+    }
     mx = attn_block_reduce(mx, true, red);
     float sum = 0.0f;
-    for (int k = k_lo + threadIdx.x; k <= k_hi; k += blockDim.x) sum += expf(__fsub_rn(score(k), mx));
+    for (int k = k_lo + threadIdx.x; k <= k_hi; k += blockDim.x) {
+        const float e = expf(__fsub_rn(STAGED ? srow_s[k] : score(k), mx));
+        if constexpr (STAGED) srow_s[k] = e;
+        sum += e;
+    }
     sum = attn_block_reduce(sum, false, red);
     for (int k = threadIdx.x; k < nkp; k += blockDim.x) {
-        const float p = k >= k_lo && k <= k_hi ? __fdiv_rn(expf(__fsub_rn(score(k), mx)), sum) : 0.0f;
+        float p = 0.0f;
+        if (k >= k_lo && k <= k_hi) p = __fdiv_rn(STAGED ? srow_s[k] : expf(__fsub_rn(score(k), mx)), sum);
         store_split(prow, nkp, k, p * 1024.0f, false);
     }
 }
@@ -413,7 +424,17 @@ cudaError_t fl_launch_attn_kv_split(const float* kc, const float* vc, int nk, in
 cudaError_t fl_launch_attn_softmax(const float* S, int rows, int n, int grp, int nkp, int start, int window, float scale,
                                    float softcap, __half* P, cudaStream_t st)
 {
-    attn_softmax_kernel<<<rows, 256, 0, st>>>(S, n, grp, nkp, start, window, scale, softcap, P);
+    const size_t smem = (size_t)nkp * 4;
+    if (smem <= (size_t)200 * 1024) {
+        if (smem > 48 * 1024) {
+            const cudaError_t e = cudaFuncSetAttribute(attn_softmax_kernel<true>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+        attn_softmax_kernel<true><<<rows, 256, smem, st>>>(S, n, grp, nkp, start, window, scale, softcap, P);
+    } else {
+        attn_softmax_kernel<false><<<rows, 256, 0, st>>>(S, n, grp, nkp, start, window, scale, softcap, P);
+    }
     return cudaGetLastError();
 }
 
