@@ -98,6 +98,9 @@ PUBLIC_API = [
     ("fl_forward", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     ("fl_decode_greedy", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p]),
     ("fl_prefill", C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32]),
+    ("fl_prefill_seq", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_int32, C.c_int32]),
+    ("fl_forward_batch", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_void_p]),
     ("fl_topk", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("fl_topk_device", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("fl_sample", C.c_int, [C.c_void_p, C.POINTER(FlSamplerDesc), C.c_void_p, C.c_int32, C.c_float,

@@ -210,6 +210,16 @@ cudaError_t fl_launch_rows_norm(float* x, const float* y, const float* post_w, c
 cudaError_t fl_launch_rope_kv(const float* qkv, const float* bq, const float* bk, const float* bv, const float* rope_cs,
                               int start_pos, int n, int qd, int kvd, int hd, float* q_out, float* k_cache,
                               float* v_cache, cudaStream_t st);
+/* batched decode (fl_forward_batch): row b at position row_pos[b] of cache slot row_slot[b] */
+cudaError_t fl_launch_rope_kv_rows(const float* qkv, const float* bq, const float* bk, const float* bv,
+                                   const float* rope_cs, const int* row_pos, const int* row_slot, size_t slot_stride,
+                                   int n, int qd, int kvd, int hd, float* q_out, float* k_cache, float* v_cache,
+                                   cudaStream_t st);
+cudaError_t fl_launch_batch_attn(const float* q, const float* k_cache, const float* v_cache, const int* row_pos,
+                                 const int* row_slot, size_t slot_stride, int B, int nh, int nkv, int hd, int window,
+                                 float scale, float softcap, __half* out, cudaStream_t st);
+cudaError_t fl_launch_softcap_rows(float* x, size_t n, float cap, cudaStream_t st);
+cudaError_t fl_launch_argmax_rows(const float* x, int rows, int n, int* out, cudaStream_t st);
 cudaError_t fl_launch_attn_q_split(const float* q, int n, int nh, int nkv, int hd, __half* qs, cudaStream_t st);
 cudaError_t fl_launch_attn_kv_split(const float* kc, const float* vc, int nk, int nkp, int kvd, int hd, __half* ks,
                                     __half* vt, cudaStream_t st);

@@ -202,9 +202,16 @@ __global__ void rows_norm_kernel(float* __restrict__ x, const float* __restrict_
 __global__ void rope_kv_kernel(const float* __restrict__ qkv, const float* __restrict__ bq, const float* __restrict__ bk,
                                const float* __restrict__ bv, const float* __restrict__ rope_cs, int start_pos, int qd,
                                int kvd, int hd, float* __restrict__ q_out, float* __restrict__ k_cache,
-                               float* __restrict__ v_cache)
+                               float* __restrict__ v_cache, const int* __restrict__ row_pos,
+                               const int* __restrict__ row_slot, size_t slot_stride)
 {
-    const int r = blockIdx.x, pos = start_pos + r, half = hd >> 1;
+    /* row r is position start_pos + r of one sequence, or (batched decode)
+     * position row_pos[r] of the sequence in cache slot row_slot[r] */
+    const int r = blockIdx.x, pos = row_pos ? row_pos[r] : start_pos + r, half = hd >> 1;
+    if (row_slot) {
+        k_cache += (size_t)row_slot[r] * slot_stride;
+        v_cache += (size_t)row_slot[r] * slot_stride;
+    }
     const int width = qd + 2 * kvd;
     const float* row = qkv + (size_t)r * width;
     for (int j = threadIdx.x; j < width; j += blockDim.x) {
@@ -231,6 +238,143 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, const float* __res
             if (bv) v = __fadd_rn(v, bv[e]);
             v_cache[(size_t)pos * kvd + e] = v;
         }
+    }
+}
+
+/* ── batched decode: one query per row, each row its own sequence ──────────
+ * ComputeAttention (LlamaForwardPass.cs:158-211, windows and softcap as in the
+ * Mistral/Gemma passes) for row b, kv head g: the grp query heads of the
+ * group against keys [max(0, p+1-window), p+1) of the row's cache slot.  Each
+ * of the 8 warps takes every 8th key; lanes own head_dim/32 dims; a warp keeps
+ * a running (max, sum, output) per head; the warps are merged in warp order. */
+template <int HD>
+__global__ void __launch_bounds__(256) batch_attn_kernel(const float* __restrict__ q, const float* __restrict__ k_cache,
+                                                        const float* __restrict__ v_cache,
+                                                        const int* __restrict__ row_pos,
+                                                        const int* __restrict__ row_slot, size_t slot_stride, int nh,
+                                                        int nkv, int window, float scale, float softcap,
+                                                        __half* __restrict__ out)
+{
+    constexpr int PER = HD / 32, GM = HD == 256 ? 4 : 8, NWB = 8; /* GM: largest query-head group */
+    __shared__ float s_o[NWB][GM][HD];
+    __shared__ float s_ml[NWB][GM][2];
+    const int b = blockIdx.x, g = blockIdx.y, grp = nh / nkv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qd = nh * HD, kvd = nkv * HD;
+    const int pos = row_pos[b];
+    const int k_lo = window < pos + 1 ? pos + 1 - window : 0;
+    const float* kc = k_cache + (size_t)row_slot[b] * slot_stride + (size_t)g * HD + lane * PER;
+    const float* vc = v_cache + (size_t)row_slot[b] * slot_stride + (size_t)g * HD + lane * PER;
+    const float inv_cap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
+    float qv[GM][PER], o[GM][PER], m[GM], l[GM];
+#pragma unroll
+    for (int h = 0; h < GM; h++) {
+        m[h] = -INFINITY;
+        l[h] = 0.0f;
+#pragma unroll
+        for (int p = 0; p < PER; p++) {
+            qv[h][p] = h < grp ? q[(size_t)b * qd + (size_t)(g * grp + h) * HD + lane * PER + p] : 0.0f;
+            o[h][p] = 0.0f;
+        }
+    }
+    for (int k = k_lo + warp; k <= pos; k += NWB) {
+        float kk[PER], vv[PER];
+#pragma unroll
+        for (int p = 0; p < PER; p++) {
+            kk[p] = kc[(size_t)k * kvd + p];
+            vv[p] = vc[(size_t)k * kvd + p];
+        }
+#pragma unroll
+        for (int h = 0; h < GM; h++) {
+            if (h >= grp) break;
+            float acc = 0.0f;
+#pragma unroll
+            for (int p = 0; p < PER; p++) acc = fmaf(qv[h][p], kk[p], acc);
+            acc = fl_warp_sum(acc);
+            float sc = __fmul_rn(acc, scale);
+            if (softcap > 0.0f) sc = __fmul_rn(tanhf(__fmul_rn(sc, inv_cap)), softcap);
+            const float mn = fmaxf(m[h], sc);
+            const float corr = expf(m[h] - mn), pw = expf(sc - mn);
+            m[h] = mn;
+            l[h] = fmaf(l[h], corr, pw);
+#pragma unroll
+            for (int p = 0; p < PER; p++) o[h][p] = fmaf(pw, vv[p], o[h][p] * corr);
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < GM; h++) {
+        if (h >= grp) break;
+#pragma unroll
+        for (int p = 0; p < PER; p++) s_o[warp][h][lane * PER + p] = o[h][p];
+        if (lane == 0) {
+            s_ml[warp][h][0] = m[h];
+            s_ml[warp][h][1] = l[h];
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < grp * HD; i += blockDim.x) {
+        const int h = i / HD, d = i - h * HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NWB; w++) M = fmaxf(M, s_ml[w][h][0]);
+        float O = 0.0f, L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NWB; w++) {
+            const float mw = s_ml[w][h][0];
+            const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+            O = fmaf(s_o[w][h][d], f, O);
+            L = fmaf(s_ml[w][h][1], f, L);
+        }
+        store_split(out + (size_t)b * 3 * qd, qd, (g * grp + h) * HD + d, L > 0.0f ? O / L : 0.0f, false);
+    }
+}
+
+/* TensorOperations.SoftCap (TensorOperations.cs:120-126) on logits rows */
+__global__ void softcap_kernel(float* __restrict__ x, size_t n, float cap)
+{
+    const float inv = 1.0f / cap;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        x[i] = __fmul_rn(tanhf(__fmul_rn(x[i], inv)), cap);
+}
+
+/* TensorOperations.ArgMax per row (the first maximum). */
+__global__ void argmax_rows_kernel(const float* __restrict__ x, int n, int* __restrict__ out)
+{
+    __shared__ float sv[16];
+    __shared__ int si[16];
+    const float* row = x + (size_t)blockIdx.x * n;
+    float bv = 0.0f;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = row[i];
+        if (bi == 0x7fffffff || fl_argmax_better(v, i, bv, bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (oi != 0x7fffffff && (bi == 0x7fffffff || fl_argmax_better(ov, oi, bv, bi))) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = bv;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float v = sv[0];
+        int i0 = si[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+            if (si[w] != 0x7fffffff && (i0 == 0x7fffffff || fl_argmax_better(sv[w], si[w], v, i0))) {
+                v = sv[w];
+                i0 = si[w];
+            }
+        out[blockIdx.x] = i0;
     }
 }
 
@@ -403,7 +547,44 @@ cudaError_t fl_launch_rope_kv(const float* qkv, const float* bq, const float* bk
                               int start_pos, int n, int qd, int kvd, int hd, float* q_out, float* k_cache,
                               float* v_cache, cudaStream_t st)
 {
-    rope_kv_kernel<<<n, 256, 0, st>>>(qkv, bq, bk, bv, rope_cs, start_pos, qd, kvd, hd, q_out, k_cache, v_cache);
+    rope_kv_kernel<<<n, 256, 0, st>>>(qkv, bq, bk, bv, rope_cs, start_pos, qd, kvd, hd, q_out, k_cache, v_cache,
+                                      nullptr, nullptr, 0);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_rope_kv_rows(const float* qkv, const float* bq, const float* bk, const float* bv,
+                                   const float* rope_cs, const int* row_pos, const int* row_slot, size_t slot_stride,
+                                   int n, int qd, int kvd, int hd, float* q_out, float* k_cache, float* v_cache,
+                                   cudaStream_t st)
+{
+    rope_kv_kernel<<<n, 256, 0, st>>>(qkv, bq, bk, bv, rope_cs, 0, qd, kvd, hd, q_out, k_cache, v_cache, row_pos,
+                                      row_slot, slot_stride);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_batch_attn(const float* q, const float* k_cache, const float* v_cache, const int* row_pos,
+                                 const int* row_slot, size_t slot_stride, int B, int nh, int nkv, int hd, int window,
+                                 float scale, float softcap, __half* out, cudaStream_t st)
+{
+    dim3 grid((unsigned)B, (unsigned)nkv);
+    switch (hd) {
+    case 64: batch_attn_kernel<64><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out); break;
+    case 128: batch_attn_kernel<128><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out); break;
+    case 256: batch_attn_kernel<256><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_softcap_rows(float* x, size_t n, float cap, cudaStream_t st)
+{
+    softcap_kernel<<<148 * 4, 256, 0, st>>>(x, n, cap);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_argmax_rows(const float* x, int rows, int n, int* out, cudaStream_t st)
+{
+    argmax_rows_kernel<<<rows, 512, 0, st>>>(x, n, out);
     return cudaGetLastError();
 }
 

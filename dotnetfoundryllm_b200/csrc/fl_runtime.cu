@@ -73,7 +73,7 @@ struct Layer {
     float *bq = nullptr, *bk = nullptr, *bv = nullptr;
     std::vector<uint8_t> stash;      /* raw bytes of gate or up until its partner arrives */
     int stash_type = -1, stash_is_gate = 0;
-    RawMatrix rq, rk, rv, ro, rgate, rup, rdown; /* raw blocks for the prompt path */
+    RawMatrix rq, rk, rv, ro, rgate, rup, rdown; /* raw blocks for the prompt path and batched decode */
 };
 
 struct fl_model {
@@ -87,6 +87,7 @@ struct fl_model {
     int emb_type = -1;
     int64_t emb_bytes = 0;
     DevMatrix output;
+    RawMatrix rout; /* the LM head's raw blocks (one GPU): output.weight, or token_embd when tied */
     float* out_norm = nullptr;
     float* rope_cs = nullptr;
     bool finalized = false;
@@ -96,7 +97,11 @@ struct fl_model {
 
 struct fl_session {
     fl_model* m = nullptr;
-    int max_ctx = 0, cur_len = 0;
+    int max_ctx = 0, cur_len = 0; /* cur_len: the length of slot 0, the token loop's sequence */
+    /* sequence slots (max_batch): slot i's K (and V) cache starts slot_stride floats after slot i-1's */
+    int n_slots = 1;
+    size_t slot_stride = 0;
+    std::vector<int> slot_len; /* lengths of slots 1.. */
     cudaStream_t st = nullptr;
     float *xa = nullptr, *xb = nullptr, *q = nullptr, *att = nullptr, *act = nullptr, *o = nullptr, *logits = nullptr;
     float *kc = nullptr, *vc = nullptr;
@@ -148,6 +153,13 @@ struct fl_session {
     int32_t* pf_tokens = nullptr;
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_y = nullptr;
     __half *pf_act = nullptr, *pf_w = nullptr;
+    /* batched decode (fl_forward_batch): row positions, slots, logits, argmax;
+     * the split-fp16 weights cached on the first call when memory allows
+     * (per layer qkv, wo, gate/up, down; then the LM head) */
+    int32_t *bt_pos = nullptr, *bt_slot = nullptr, *bt_argmax = nullptr;
+    float* bt_logits = nullptr;
+    bool bt_cache_tried = false;
+    std::vector<__half*> bt_w;
     /* attention of a chunk: split Q/K/V^T, scores, split probabilities, output */
     int pf_nkmax = 0;
     __half *pf_qs = nullptr, *pf_ks = nullptr, *pf_vt = nullptr, *pf_p = nullptr;
@@ -400,7 +412,11 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
     const int T = m->T, rk = m->rank;
     if (n == "output.weight") {
         if (!mat_shape_ok(d.vocab, h)) return fail(FL_ERR_ARG, "output.weight shape mismatch");
-        if (T == 1) return upload_matrix(m, type, d.vocab, h, raw, nullptr, nullptr, &m->output, (double)nbytes);
+        if (T == 1) {
+            int rc = keep_raw(m, &m->rout, type, d.vocab, h, raw, nbytes);
+            if (rc) return rc;
+            return upload_matrix(m, type, d.vocab, h, raw, nullptr, nullptr, &m->output, (double)nbytes);
+        }
         std::vector<uint8_t> part = slice_rows(raw, type, h, rk * m->vocab_l, m->vocab_l);
         return upload_matrix(m, type, m->vocab_l, h, part.data(), nullptr, nullptr, &m->output, (double)part.size());
     }
@@ -515,6 +531,7 @@ extern "C" int fl_model_finalize(fl_model* m)
     }
     if (!m->output.present) {
         /* LoadTensorOptional("output.weight") ?? tokenEmbed (GgufModelLoader.cs:368-369) */
+        if (m->T == 1) m->rout = RawMatrix{m->emb_raw, m->emb_type, d.vocab, d.hidden};
         std::vector<uint8_t> host((size_t)m->emb_bytes);
         CK(cudaMemcpy(host.data(), m->emb_raw, (size_t)m->emb_bytes, cudaMemcpyDeviceToHost));
         if (m->T > 1) host = slice_rows(host.data(), m->emb_type, d.hidden, m->rank * m->vocab_l, m->vocab_l);
@@ -800,7 +817,8 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
         if (rc) return rc;
     }
     if (kv_dtype != FL_KV_F32) return fail(FL_ERR_UNSUPPORTED, "kv dtype %d", kv_dtype);
-    if (max_batch > 1) return fail(FL_ERR_UNSUPPORTED, "batched sessions are not built into this library yet");
+    if (max_batch < 1) max_batch = 1;
+    if (max_batch > 1 && m->T > 1) return fail(FL_ERR_UNSUPPORTED, "batched sessions run on one GPU (tp_size 1)");
     const fl_model_desc& d = m->d;
     if (max_ctx <= 0 || max_ctx > d.max_ctx) max_ctx = d.max_ctx;
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
@@ -825,7 +843,10 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     s->attn_split = split;
     s->n_absmax = 2 * d.n_layers;
     int rc = FL_OK;
-    size_t kv_bytes = (size_t)d.n_layers * max_ctx * kvd * 4;
+    s->n_slots = max_batch;
+    s->slot_stride = (size_t)d.n_layers * max_ctx * kvd;
+    s->slot_len.assign((size_t)max_batch, 0);
+    size_t kv_bytes = (size_t)max_batch * d.n_layers * max_ctx * kvd * 4;
 #define AL(p, b) if (!rc) rc = dalloc(s->allocs, &(p), (b))
     AL(s->xa, (size_t)h * 4);
     AL(s->xb, (size_t)h * 4);
@@ -1060,8 +1081,10 @@ extern "C" int fl_session_tp_connect(fl_session* s, const void* handles)
 extern "C" int fl_session_reset(fl_session* s, int32_t seq_slot)
 {
     if (!s) return fail(FL_ERR_ARG, "null session");
-    if (seq_slot != 0) return fail(FL_ERR_ARG, "sequence slot %d (single-sequence session)", seq_slot);
-    s->cur_len = 0;
+    if (seq_slot < 0 || seq_slot >= s->n_slots)
+        return fail(FL_ERR_ARG, "sequence slot %d outside [0, %d)", seq_slot, s->n_slots);
+    if (seq_slot == 0) s->cur_len = 0;
+    else s->slot_len[(size_t)seq_slot] = 0;
     return FL_OK;
 }
 
@@ -1366,7 +1389,8 @@ static int pf_alloc(fl_session* s)
     const size_t per_tok = (size_t)m->nh_l * nkmax * 10;
     int cap = std::min(s->max_ctx, 2048);
     if ((size_t)cap * per_tok > ((size_t)4 << 30)) cap = std::max(16, (int)((((size_t)4 << 30) / per_tok) & ~(size_t)15));
-    const size_t wmax = std::max({(size_t)(qd + 2 * kvd) * h, (size_t)h * qd, (size_t)2 * F * h, (size_t)h * F});
+    size_t wmax = std::max({(size_t)(qd + 2 * kvd) * h, (size_t)h * qd, (size_t)2 * F * h, (size_t)h * F});
+    if (s->n_slots > 1) wmax = std::max(wmax, (size_t)d.vocab * h); /* the LM head of batched steps */
     const size_t amax = std::max({(size_t)h, (size_t)qd, (size_t)F});
     const size_t ymax = std::max((size_t)h, (size_t)2 * F);
     int rc = FL_OK;
@@ -1396,7 +1420,7 @@ static int pf_alloc(fl_session* s)
 
 /* One chunk of prompt tokens through every layer (the K/V of its positions
  * land in the session's cache). */
-static int pf_chunk(fl_session* s, const int32_t* tokens, int n, int start)
+static int pf_chunk(fl_session* s, int slot, const int32_t* tokens, int n, int start)
 {
     fl_model* m = s->m;
     const fl_model_desc& d = m->d;
@@ -1417,8 +1441,8 @@ static int pf_chunk(fl_session* s, const int32_t* tokens, int n, int start)
         if ((rc = pf_dequant(s, L.rk, s->pf_w + (size_t)qd * 3 * h))) return rc;
         if ((rc = pf_dequant(s, L.rv, s->pf_w + (size_t)(qd + kvd) * 3 * h))) return rc;
         if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_qkv, qd + 2 * kvd, h, n))) return rc;
-        float* kc = s->kc + (size_t)l * s->max_ctx * kvd;
-        float* vc = s->vc + (size_t)l * s->max_ctx * kvd;
+        float* kc = s->kc + (size_t)slot * s->slot_stride + (size_t)l * s->max_ctx * kvd;
+        float* vc = s->vc + (size_t)slot * s->slot_stride + (size_t)l * s->max_ctx * kvd;
         CK(fl_launch_rope_kv(s->pf_qkv, L.bq, L.bk, L.bv, m->rope_cs, start, n, qd, kvd, hd, s->pf_q, kc, vc, s->st));
         int window = INT_MAX;
         if (d.arch == FL_ARCH_MISTRAL) window = d.sliding_window;
@@ -1457,16 +1481,20 @@ static int pf_chunk(fl_session* s, const int32_t* tokens, int n, int start)
 
 /* fl_prefill; with ms != null the chunk loop is bracketed by CUDA events on
  * the session stream and their elapsed time is returned (benchmark hook). */
-static int prefill_impl(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos, float* ms)
+static int& slot_length(fl_session* s, int slot) { return slot == 0 ? s->cur_len : s->slot_len[(size_t)slot]; }
+
+static int prefill_impl(fl_session* s, int slot, const int32_t* tokens, int32_t n, int32_t start_pos, float* ms)
 {
     if (!s || (!tokens && n)) return fail(FL_ERR_ARG, "null argument");
     if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     fl_model* m = s->m;
     const fl_model_desc& d = m->d;
     if (m->T > 1) return fail(FL_ERR_UNSUPPORTED, "the batched prompt path runs on one GPU (tp_size 1)");
-    if (n < 0 || start_pos < 0 || start_pos > s->cur_len || start_pos + n > s->max_ctx)
+    if (slot < 0 || slot >= s->n_slots) return fail(FL_ERR_ARG, "sequence slot %d outside [0, %d)", slot, s->n_slots);
+    const int have = slot_length(s, slot);
+    if (n < 0 || start_pos < 0 || start_pos > have || start_pos + n > s->max_ctx)
         return fail(FL_ERR_ARG, "prompt positions [%d, %d) do not fit the KV cache (holds %d of %d)", start_pos,
-                    start_pos + n, s->cur_len, s->max_ctx);
+                    start_pos + n, have, s->max_ctx);
     for (int i = 0; i < n; i++)
         if ((uint32_t)tokens[i] >= (uint32_t)d.vocab)
             return fail(FL_ERR_ARG, "Token id %d is outside the valid vocabulary range [0, %d].", tokens[i], d.vocab - 1);
@@ -1482,7 +1510,7 @@ static int prefill_impl(fl_session* s, const int32_t* tokens, int32_t n, int32_t
     }
     for (int c = 0; c < n && !rc; c += s->pf_cap) {
         const int len = std::min(s->pf_cap, n - c);
-        rc = pf_chunk(s, tokens + c, len, start_pos + c);
+        rc = pf_chunk(s, slot, tokens + c, len, start_pos + c);
     }
     if (ms && !rc && cudaEventRecord(ev[1], s->st) != cudaSuccess) rc = fail(FL_ERR_CUDA, "cudaEventRecord failed");
     if (!rc && cudaStreamSynchronize(s->st) != cudaSuccess) rc = fail(FL_ERR_CUDA, "prefill: stream failed");
@@ -1491,19 +1519,164 @@ static int prefill_impl(fl_session* s, const int32_t* tokens, int32_t n, int32_t
     for (cudaEvent_t e : ev)
         if (e) cudaEventDestroy(e);
     if (rc) return rc;
-    s->cur_len = start_pos + n;
+    slot_length(s, slot) = start_pos + n;
     return FL_OK;
 }
 
 extern "C" int fl_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos)
 {
-    return prefill_impl(s, tokens, n, start_pos, nullptr);
+    return prefill_impl(s, 0, tokens, n, start_pos, nullptr);
+}
+
+extern "C" int fl_prefill_seq(fl_session* s, int32_t seq_slot, const int32_t* tokens, int32_t n, int32_t start_pos)
+{
+    return prefill_impl(s, seq_slot, tokens, n, start_pos, nullptr);
 }
 
 extern "C" int fl_time_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos, float* ms)
 {
     if (!ms) return fail(FL_ERR_ARG, "null argument");
-    return prefill_impl(s, tokens, n, start_pos, ms);
+    return prefill_impl(s, 0, tokens, n, start_pos, ms);
+}
+
+/* ── batched decode ─────────────────────────────────────────────────────── */
+
+/* The split-fp16 weights of every projection and of the LM head, kept for
+ * the session's batched steps: 6 bytes per weight (8B: ~45 GB), tried once;
+ * without them each step dequantizes into the prompt path's buffer. */
+static void bt_cache_weights(fl_session* s)
+{
+    s->bt_cache_tried = true;
+    fl_model* m = s->m;
+    const fl_model_desc& d = m->d;
+    const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, F = m->ffn_l;
+    std::vector<size_t> sizes;
+    for (int l = 0; l < d.n_layers; l++) {
+        sizes.push_back((size_t)(qd + 2 * kvd) * h);
+        sizes.push_back((size_t)h * qd);
+        sizes.push_back((size_t)2 * F * h);
+        sizes.push_back((size_t)h * F);
+    }
+    sizes.push_back((size_t)d.vocab * h);
+    size_t total = 0;
+    for (size_t e : sizes) total += (e * 3 * 2 + 255) & ~(size_t)255;
+    size_t free_b = 0, tot_b = 0;
+    if (cudaMemGetInfo(&free_b, &tot_b) != cudaSuccess || total + ((size_t)4 << 30) > free_b) return;
+    uint8_t* base = nullptr;
+    if (cudaMalloc(&base, total) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    s->allocs.push_back(base);
+    size_t off = 0;
+    for (size_t e : sizes) {
+        s->bt_w.push_back(reinterpret_cast<__half*>(base + off));
+        off += (e * 3 * 2 + 255) & ~(size_t)255;
+    }
+    for (int l = 0; l < d.n_layers; l++) {
+        const Layer& L = m->layers[(size_t)l];
+        __half** w = &s->bt_w[(size_t)l * 4];
+        if (pf_dequant(s, L.rq, w[0]) || pf_dequant(s, L.rk, w[0] + (size_t)qd * 3 * h) ||
+            pf_dequant(s, L.rv, w[0] + (size_t)(qd + kvd) * 3 * h) || pf_dequant(s, L.ro, w[1]) ||
+            pf_dequant(s, L.rgate, w[2]) || pf_dequant(s, L.rup, w[2] + (size_t)F * 3 * h) ||
+            pf_dequant(s, L.rdown, w[3])) {
+            s->bt_w.clear();
+            return;
+        }
+    }
+    if (pf_dequant(s, m->rout, s->bt_w.back())) s->bt_w.clear();
+}
+
+extern "C" int fl_forward_batch(fl_session* s, int32_t B, const int32_t* tokens, const int32_t* positions,
+                                const int32_t* slots, float* logits, int32_t* argmax)
+{
+    if (!s || !tokens || !positions || !slots) return fail(FL_ERR_ARG, "null argument");
+    if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
+    fl_model* m = s->m;
+    const fl_model_desc& d = m->d;
+    if (m->T > 1) return fail(FL_ERR_UNSUPPORTED, "batched decode runs on one GPU (tp_size 1)");
+    if (B < 1 || B > s->n_slots) return fail(FL_ERR_ARG, "batch %d outside [1, %d] (the session's sequence slots)", B,
+                                             s->n_slots);
+    std::vector<char> seen((size_t)s->n_slots, 0);
+    for (int b = 0; b < B; b++) {
+        if (slots[b] < 0 || slots[b] >= s->n_slots)
+            return fail(FL_ERR_ARG, "sequence slot %d outside [0, %d)", slots[b], s->n_slots);
+        if (seen[(size_t)slots[b]]++) return fail(FL_ERR_ARG, "sequence slot %d appears twice in one batch", slots[b]);
+        if ((uint32_t)tokens[b] >= (uint32_t)d.vocab)
+            return fail(FL_ERR_ARG, "Token id %d is outside the valid vocabulary range [0, %d].", tokens[b], d.vocab - 1);
+        if (positions[b] < 0 || positions[b] >= s->max_ctx || positions[b] > slot_length(s, slots[b]))
+            return fail(FL_ERR_ARG, "position %d of slot %d skips cached positions or exceeds the context", positions[b],
+                        slots[b]);
+    }
+    if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+    int rc = FL_OK;
+    if (!s->pf_cap && (rc = pf_alloc(s))) return rc;
+    if (B > s->pf_cap) return fail(FL_ERR_UNSUPPORTED, "batch %d above the prompt path's %d rows", B, s->pf_cap);
+    if (!s->bt_pos) {
+        const int S = s->n_slots;
+        if ((rc = dalloc(s->allocs, &s->bt_pos, (size_t)S * 4)) || (rc = dalloc(s->allocs, &s->bt_slot, (size_t)S * 4)) ||
+            (rc = dalloc(s->allocs, &s->bt_argmax, (size_t)S * 4)) ||
+            (rc = dalloc(s->allocs, &s->bt_logits, (size_t)S * d.vocab * 4)))
+            return rc;
+    }
+    if (!s->bt_cache_tried) bt_cache_weights(s);
+    const bool cached = !s->bt_w.empty();
+    const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, F = m->ffn_l, hd = d.head_dim;
+    const bool gemma = d.arch == FL_ARCH_GEMMA2;
+    const float eps = gemma ? 1e-6f : d.rms_eps;
+    CK(cudaMemcpyAsync(s->pf_tokens, tokens, (size_t)B * 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaMemcpyAsync(s->bt_pos, positions, (size_t)B * 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaMemcpyAsync(s->bt_slot, slots, (size_t)B * 4, cudaMemcpyHostToDevice, s->st));
+    CK(fl_launch_embed_rows(m->emb_type, m->emb_raw, s->pf_tokens, B, h, d.vocab, s->pf_x, s->state + ST_ERR, s->st));
+    for (int l = 0; l < d.n_layers; l++) {
+        Layer& L = m->layers[(size_t)l];
+        __half* const* cw = cached ? &s->bt_w[(size_t)l * 4] : nullptr;
+        const float* prev = l > 0 ? s->pf_y : nullptr;
+        const float* prev_post = l > 0 && gemma ? m->layers[(size_t)l - 1].post_ffn_norm : nullptr;
+        CK(fl_launch_rows_norm(s->pf_x, prev, prev_post, L.attn_norm, B, h, eps, gemma, s->pf_act, s->st));
+        const __half* w = cached ? cw[0] : s->pf_w;
+        if (!cached && ((rc = pf_dequant(s, L.rq, s->pf_w)) || (rc = pf_dequant(s, L.rk, s->pf_w + (size_t)qd * 3 * h)) ||
+                        (rc = pf_dequant(s, L.rv, s->pf_w + (size_t)(qd + kvd) * 3 * h))))
+            return rc;
+        if ((rc = pf_gemm(s, w, s->pf_act, s->pf_qkv, qd + 2 * kvd, h, B))) return rc;
+        float* kc = s->kc + (size_t)l * s->max_ctx * kvd;
+        float* vc = s->vc + (size_t)l * s->max_ctx * kvd;
+        CK(fl_launch_rope_kv_rows(s->pf_qkv, L.bq, L.bk, L.bv, m->rope_cs, s->bt_pos, s->bt_slot, s->slot_stride, B, qd,
+                                  kvd, hd, s->pf_q, kc, vc, s->st));
+        int window = INT_MAX;
+        if (d.arch == FL_ARCH_MISTRAL) window = d.sliding_window;
+        if (gemma && (l % 2) == 0) window = d.sliding_window; /* Gemma2ForwardPass.cs:87 */
+        if (window <= 0) window = INT_MAX;
+        CK(fl_launch_batch_attn(s->pf_q, kc, vc, s->bt_pos, s->bt_slot, s->slot_stride, B, m->nh_l, m->nkv_l, hd, window,
+                                d.attn_scale, gemma ? d.attn_softcap : 0.0f, s->pf_act, s->st));
+        w = cached ? cw[1] : s->pf_w;
+        if (!cached && (rc = pf_dequant(s, L.ro, s->pf_w))) return rc;
+        if ((rc = pf_gemm(s, w, s->pf_act, s->pf_y, h, qd, B))) return rc;
+        CK(fl_launch_rows_norm(s->pf_x, s->pf_y, gemma ? L.post_attn_norm : nullptr, L.ffn_norm, B, h, eps, gemma,
+                               s->pf_act, s->st));
+        w = cached ? cw[2] : s->pf_w;
+        if (!cached && ((rc = pf_dequant(s, L.rgate, s->pf_w)) || (rc = pf_dequant(s, L.rup, s->pf_w + (size_t)F * 3 * h))))
+            return rc;
+        if ((rc = pf_gemm(s, w, s->pf_act, s->pf_y, 2 * F, h, B))) return rc;
+        CK(fl_launch_glu(s->pf_y, B, F, gemma ? 1 : 0, s->pf_act, s->st));
+        w = cached ? cw[3] : s->pf_w;
+        if (!cached && (rc = pf_dequant(s, L.rdown, s->pf_w))) return rc;
+        if ((rc = pf_gemm(s, w, s->pf_act, s->pf_y, h, F, B))) return rc;
+    }
+    /* final norm (after the last residual) and the LM head */
+    CK(fl_launch_rows_norm(s->pf_x, s->pf_y, gemma ? m->layers.back().post_ffn_norm : nullptr, m->out_norm, B, h, eps,
+                           gemma, s->pf_act, s->st));
+    const __half* wh = cached ? s->bt_w.back() : s->pf_w;
+    if (!cached && (rc = pf_dequant(s, m->rout, s->pf_w))) return rc;
+    if ((rc = pf_gemm(s, wh, s->pf_act, s->bt_logits, d.vocab, h, B))) return rc;
+    if (gemma && d.final_softcap > 0.0f) CK(fl_launch_softcap_rows(s->bt_logits, (size_t)B * d.vocab, d.final_softcap, s->st));
+    CK(fl_launch_argmax_rows(s->bt_logits, B, d.vocab, s->bt_argmax, s->st));
+    if (argmax) CK(cudaMemcpyAsync(argmax, s->bt_argmax, (size_t)B * 4, cudaMemcpyDeviceToHost, s->st));
+    if (logits) CK(cudaMemcpyAsync(logits, s->bt_logits, (size_t)B * d.vocab * 4, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaStreamSynchronize(s->st));
+    if ((rc = check_device_err(s))) return rc;
+    for (int b = 0; b < B; b++) slot_length(s, slots[b]) = positions[b] + 1;
+    return FL_OK;
 }
 
 /* ── stateless helpers ──────────────────────────────────────────────────── */

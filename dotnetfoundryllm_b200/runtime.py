@@ -130,11 +130,12 @@ class CudaModel:
 class CudaForwardPass:
     """IForwardPass over a device session (one KV cache in HBM)."""
 
-    def __init__(self, model: CudaModel, max_ctx: int = 0):
+    def __init__(self, model: CudaModel, max_ctx: int = 0, max_batch: int = 1):
         self.model = model
         self.lib = model.lib
+        self.max_batch = max_batch
         h = C.c_void_p()
-        check(self.lib.fl_session_create(model.handle, max_ctx, 1, 0, C.byref(h)), "fl_session_create")
+        check(self.lib.fl_session_create(model.handle, max_ctx, max_batch, 0, C.byref(h)), "fl_session_create")
         self._h = h
         self.vocab = model.desc.vocab
         self._logits = np.zeros(self.vocab, dtype=np.float32)
@@ -222,6 +223,28 @@ class CudaForwardPass:
         check(self.lib.fl_sample(self.handle, C.byref(d), _ptr(g) if g.size else None, int(g.size), float(u),
                                  C.byref(tok)), "fl_sample")
         return int(tok.value)
+
+    # ── batched decode (sequence slots) ──
+    def reset_slot(self, slot: int) -> None:
+        check(self.lib.fl_session_reset(self.handle, int(slot)), "fl_session_reset")
+
+    def prefill_seq(self, slot: int, tokens, start_pos: int = 0) -> None:
+        """fl_prefill_seq: the prompt path into sequence slot `slot`."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(self.lib.fl_prefill_seq(self.handle, int(slot), _ptr(t), int(t.size), int(start_pos)),
+              "fl_prefill_seq")
+
+    def forward_batch(self, tokens, positions, slots, want_logits: bool = False):
+        """fl_forward_batch: one step of len(tokens) sequences; returns the
+        argmax per row and, if asked, the [rows x vocab] logits."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = np.ascontiguousarray(positions, dtype=np.int32)
+        sl = np.ascontiguousarray(slots, dtype=np.int32)
+        am = np.zeros(t.size, dtype=np.int32)
+        lg = np.zeros((t.size, self.vocab), dtype=np.float32) if want_logits else None
+        check(self.lib.fl_forward_batch(self.handle, int(t.size), _ptr(t), _ptr(p), _ptr(sl),
+                                        _ptr(lg) if want_logits else None, _ptr(am)), "fl_forward_batch")
+        return (am, lg) if want_logits else am
 
     def time_decode(self, token_id: int, start_pos: int, n_steps: int) -> float:
         ms = C.c_float()
@@ -348,6 +371,30 @@ def generate(fwd: CudaForwardPass, prompt: np.ndarray, max_tokens: int, temperat
         if eos is not None and nxt == eos:
             break
     return np.array(toks, dtype=np.int32)
+
+
+def generate_batch_greedy(fwd: CudaForwardPass, prompts, max_tokens: int) -> list[np.ndarray]:
+    """Greedy completion of several prompts at once, one sequence slot each:
+    every prompt but its last token through the prompt path, then batched
+    decode steps (each row the loop of LlamaLanguageModel.GenerateAsync with
+    Temperature = 0)."""
+    B = len(prompts)
+    if B > fwd.max_batch:
+        raise ArgumentError(f"{B} prompts for {fwd.max_batch} sequence slots")
+    pos = np.zeros(B, dtype=np.int32)
+    nxt = np.zeros(B, dtype=np.int32)
+    for b, pr in enumerate(prompts):
+        fwd.reset_slot(b)
+        fwd.prefill_seq(b, pr[:-1], 0)
+        pos[b] = len(pr) - 1
+        nxt[b] = int(pr[-1])
+    out = np.zeros((B, max_tokens), dtype=np.int32)
+    slots = np.arange(B, dtype=np.int32)
+    for step in range(max_tokens):
+        nxt = fwd.forward_batch(nxt, pos, slots)
+        out[:, step] = nxt
+        pos += 1
+    return [out[b] for b in range(B)]
 
 
 def dequantize(ggml_type: int, raw: np.ndarray, dst_len: int | None = None) -> np.ndarray:

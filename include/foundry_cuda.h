@@ -100,7 +100,11 @@ void fl_model_destroy(fl_model* m);
 /* Per-request forward-pass state: replaces `new KvCache(layers, maxContext,
  * kvDim)` (LlamaLanguageModel.cs:129) and the scratch arrays each forward
  * pass allocates (LlamaForwardPass.cs:54-62).  The KV cache lives in HBM.
- * max_ctx <= 0 uses the model's MaxContextLength. */
+ * max_ctx <= 0 uses the model's MaxContextLength.  max_batch (>= 1) is the
+ * number of sequence slots, each with its own KV cache of max_ctx positions;
+ * slot 0 is the sequence of fl_forward / fl_decode_greedy / fl_prefill, and
+ * fl_prefill_seq / fl_forward_batch address any slot (max_batch > 1 needs
+ * tp_size 1). */
 int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch, int32_t kv_dtype, fl_session** out);
 
 /* Tensor parallelism (fl_model_desc.tp_size = 2, 4 or 8; one process or
@@ -121,8 +125,24 @@ int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch, int32_t k
 int fl_session_tp_handle(fl_session* s, void* handle);
 int fl_session_tp_connect(fl_session* s, const void* handles);
 
-/* KvCache.Clear (KvCache.cs:138-144). */
+/* KvCache.Clear (KvCache.cs:138-144) of one sequence slot. */
 int fl_session_reset(fl_session* s, int32_t seq_slot);
+
+/* Batched decode.  No counterpart in the reference, which runs one
+ * LlamaLanguageModel.GenerateAsync per request (its BatchCompletion sample is
+ * a stub, samples/BatchCompletion/Program.cs:1): one step of `batch`
+ * sequences at once, row b being token tokens[b] at position positions[b] of
+ * the sequence in slot seq_slots[b] (distinct slots; a position may not skip
+ * cached positions; a smaller one rewinds that slot, as IKvCache does).  The
+ * values are those of `batch` separate Forward calls.  logits (batch x vocab)
+ * and argmax (batch) are host pointers, either may be NULL.  The projections
+ * and the LM head run as split-fp16 tensor-core GEMMs over all rows (the
+ * prompt path's arithmetic); the weights are dequantized once per session into
+ * a cached split layout (6 bytes per weight) when device memory allows, else
+ * at every step.  fl_prefill_seq is fl_prefill into a given slot. */
+int fl_prefill_seq(fl_session* s, int32_t seq_slot, const int32_t* tokens, int32_t n, int32_t start_pos);
+int fl_forward_batch(fl_session* s, int32_t batch, const int32_t* tokens, const int32_t* positions,
+                     const int32_t* seq_slots, float* logits, int32_t* argmax);
 
 /* IForwardPass.Forward(tokenId, position, kvCache) (IForwardPass.cs:8-15,
  * LlamaForwardPass.cs:82-130 and the Mistral/Gemma2/Qwen2 copies), plus the
