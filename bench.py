@@ -268,18 +268,16 @@ def prefill_flops(d, n: int) -> float:
 
 
 def prefill_record(p: dict, d, peaks: dict, ws: int, cpu: dict) -> dict:
-    if "ms" not in p:
-        return {"path": "token by token through fl_forward (tensor-parallel prompt path not built)",
-                "tokens": p["tokens"], "tok_s": ws * p["tokens"] / p["reference_style_s"]}
-    fl = prefill_flops(d, p["tokens"])
+    streams = p["streams"]  # prompts processed at once: 1 with tensor parallelism, N replicas otherwise
+    fl = streams * prefill_flops(d, p["tokens"])
     tflops = fl / (p["ms"] / 1e3) / 1e12
     return {
         "path": "fl_prefill: split-fp16 tensor-core GEMMs (cuBLASLt) for the projections and for attention's "
                 "QK^T and PV; own dequant, norm, RoPE/KV-append, masked-softmax and GLU kernels",
-        "tokens": p["tokens"], "ms": p["ms"], "tok_s": ws * p["tokens"] / (p["ms"] / 1e3),
-        "e2e_tok_s": ws * p["tokens"] / p["e2e_s"],
-        "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": tflops / peaks["bf16_tflops"], "algorithmic_flops": fl,
+        "tokens": p["tokens"], "ms": p["ms"], "tok_s": streams * p["tokens"] / (p["ms"] / 1e3),
+        "e2e_tok_s": streams * p["tokens"] / p["e2e_s"],
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": ws * peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / (ws * peaks["bf16_tflops"]), "algorithmic_flops": fl,
                      "executed_tensor_flops_note": "the split-fp16 GEMMs run 3x the projection FLOPs",
                      "peak_source": peaks["source"]},
         "cpu_baseline": {"value": cpu["tok_s"], "unit": "tok/s", "cores": cpu["threads"], "kind": "port",
@@ -382,23 +380,19 @@ def run_ours(args, ws, rank, local):
     prompt = ggufgen.prompt_ids(args.prompt, model.desc.vocab, 0)
     kv = object()
     pre = prompt[:-1]
-    prefill = None
-    if not tp:
-        # the prompt path (fl_prefill): PREFILL_WARMUP + PREFILL_TIMED device-timed passes
-        # over the same 2047 tokens (each starts from an empty KV cache), then one through
-        # the public call with the token ids in host memory; the last one leaves the
-        # prompt's K/V in the cache for the decode steps
-        pf_ms = [fwd.time_prefill(pre, 0, kv) for _ in range(PREFILL_WARMUP + PREFILL_TIMED)][PREFILL_WARMUP:]
-        t0 = time.perf_counter()
-        fwd.prefill(pre, 0, kv)
-        pf_e2e_s = time.perf_counter() - t0
-        prefill = {"ms": max(pf_ms), "e2e_s": pf_e2e_s, "tokens": len(pre)}
-    else:
-        # prefill the way LlamaLanguageModel does: one Forward per prompt token but the last
-        t0 = time.perf_counter()
-        for i in range(args.prompt - 1):
-            fwd.forward(int(prompt[i]), i, kv, want_logits=False)
-        prefill = {"reference_style_s": time.perf_counter() - t0, "tokens": len(pre)}
+    # the prompt path (fl_prefill; tensor-parallel across the ranks with TP):
+    # PREFILL_WARMUP + PREFILL_TIMED device-timed passes over the same 2047 tokens
+    # (each starts from an empty KV cache), then one through the public call with
+    # the token ids in host memory; the last one leaves the prompt's K/V in the
+    # cache for the decode steps.  Max over ranks.
+    barrier(ws)
+    pf_ms = [fwd.time_prefill(pre, 0, kv) for _ in range(PREFILL_WARMUP + PREFILL_TIMED)][PREFILL_WARMUP:]
+    barrier(ws)
+    t0 = time.perf_counter()
+    fwd.prefill(pre, 0, kv)
+    pf_e2e_s = time.perf_counter() - t0
+    prefill = {"ms": allreduce_max(max(pf_ms), ws), "e2e_s": allreduce_max(pf_e2e_s, ws), "tokens": len(pre),
+               "streams": streams}
     pos = args.prompt - 1
     tok = int(prompt[-1])
     # warm-up (device-resident greedy loop)

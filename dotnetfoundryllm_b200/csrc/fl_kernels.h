@@ -220,6 +220,11 @@ cudaError_t fl_launch_batch_attn(const float* q, const float* k_cache, const flo
                                  float scale, float softcap, __half* out, cudaStream_t st);
 cudaError_t fl_launch_softcap_rows(float* x, size_t n, float cap, cudaStream_t st);
 cudaError_t fl_launch_argmax_rows(const float* x, int rows, int n, int* out, cudaStream_t st);
+/* tensor-parallel prefill: every rank's partial slot and flag array (device
+ * addresses, own and peers'), summed in rank order into y once all ranks
+ * have raised their flag to epoch */
+cudaError_t fl_launch_tp_prefill_reduce(const float* const* slots, int* const* flags, int T, int rank, int epoch,
+                                        size_t count, float* y, int* err, cudaStream_t st);
 cudaError_t fl_launch_attn_q_split(const float* q, int n, int nh, int nkv, int hd, __half* qs, cudaStream_t st);
 cudaError_t fl_launch_attn_kv_split(const float* kc, const float* vc, int nk, int nkp, int kvd, int hd, __half* ks,
                                     __half* vt, cudaStream_t st);

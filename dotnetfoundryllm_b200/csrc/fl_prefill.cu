@@ -378,6 +378,52 @@ __global__ void argmax_rows_kernel(const float* __restrict__ x, int n, int* __re
     }
 }
 
+/* ── tensor parallelism: the allreduce of a chunk's row-parallel partials ── */
+
+/* This rank's partial slot is complete (the GEMM before this launch wrote it):
+ * publish it to every rank by raising this rank's flag there to `epoch`. */
+struct TpFlags {
+    int* f[FL_TP_MAX]; /* every rank's flag array (passed by value) */
+};
+
+__global__ void tp_pf_signal_kernel(TpFlags flags, int T, int rank, int epoch)
+{
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    __threadfence_system();
+    for (int q = 0; q < T; q++) fl_st_release_sys(flags.f[q] + rank, epoch);
+}
+
+struct TpSlots {
+    const float* slot[FL_TP_MAX];
+    const int* my_flags; /* this rank's flag array, which the peers write */
+};
+
+/* Waits (bounded, ~2 s) for every rank's flag to reach `epoch`, then sums the
+ * T partial slots in rank order (peers over NVLink) into y. */
+__global__ void tp_pf_reduce_kernel(TpSlots sl, int T, int epoch, size_t count, float* __restrict__ y, int* err)
+{
+    __shared__ int s_ok;
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        const uint64_t t0 = fl_globaltimer();
+        for (int q = 0; q < T && ok; q++)
+            for (uint32_t it = 0; fl_ld_acquire_sys(sl.my_flags + q) < epoch; it++)
+                if ((it & 255u) == 0 && fl_globaltimer() - t0 > 2000000000ull) {
+                    atomicExch(err, FL_DEV_ERR_TIMEOUT);
+                    ok = 0;
+                    break;
+                }
+        s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x) {
+        float sum = 0.0f;
+        for (int q = 0; q < T; q++) sum += fl_ld_relaxed_sys(sl.slot[q] + i);
+        y[i] = sum;
+    }
+}
+
 /* ── causal attention of a chunk on the tensor cores ────────────────────────
  * Per kv head g (a GEMM batch), the chunk's queries of all grp query heads of
  * the group are the rows (t, h) = t*grp + h of one matrix, so one split-fp16
@@ -585,6 +631,26 @@ cudaError_t fl_launch_softcap_rows(float* x, size_t n, float cap, cudaStream_t s
 cudaError_t fl_launch_argmax_rows(const float* x, int rows, int n, int* out, cudaStream_t st)
 {
     argmax_rows_kernel<<<rows, 512, 0, st>>>(x, n, out);
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_tp_prefill_reduce(const float* const* slots, int* const* flags, int T, int rank, int epoch,
+                                        size_t count, float* y, int* err, cudaStream_t st)
+{
+    if (T < 2 || T > FL_TP_MAX || rank < 0 || rank >= T) return cudaErrorInvalidValue;
+    TpFlags fl = {};
+    TpSlots sl = {};
+    for (int q = 0; q < T; q++) {
+        fl.f[q] = flags[q];
+        sl.slot[q] = slots[q];
+    }
+    sl.my_flags = flags[rank];
+    tp_pf_signal_kernel<<<1, 32, 0, st>>>(fl, T, rank, epoch);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    unsigned blocks = (unsigned)((count + 255) / 256);
+    if (blocks > 148) blocks = 148; /* every CTA co-resident: each one waits */
+    tp_pf_reduce_kernel<<<blocks, 256, 0, st>>>(sl, T, epoch, count, y, err);
     return cudaGetLastError();
 }
 

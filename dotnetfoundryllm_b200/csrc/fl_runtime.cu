@@ -143,7 +143,9 @@ struct fl_session {
     bool built = false;
     /* tensor parallelism: this rank's exchange region and every rank's, mapped */
     uint8_t* xchg = nullptr;
-    size_t xchg_bytes = 0, xchg_logits_off = 0;
+    size_t xchg_bytes = 0, xchg_logits_off = 0, xchg_pf_off = 0;
+    int pf_tp_rows = 0; /* rows of a prompt chunk's partial-sum slot in the exchange region */
+    int32_t pf_epoch = 0; /* the prompt path's flag epoch (host copy while it runs) */
     int xchg_recv_n = 0;
     int32_t* tp_epoch = nullptr;
     uint8_t* tp_peer[FL_TP_MAX] = {};
@@ -463,6 +465,8 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
                             e.lcols, type);
             std::vector<uint8_t> part = e.split_cols ? slice_cols(raw, type, e.rows, e.cols, rk * e.lcols, e.lcols)
                                                      : slice_rows(raw, type, e.cols, rk * e.lrows, e.lrows);
+            int rc = keep_raw(m, rm, type, e.lrows, e.lcols, part.data(), part.size()); /* this rank's slice */
+            if (rc) return rc;
             return upload_matrix(m, type, e.lrows, e.lcols, part.data(), nullptr, nullptr, e.dm, (double)part.size());
         }
     }
@@ -475,8 +479,9 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
             part = slice_rows(raw, type, h, rk * m->ffn_l, m->ffn_l);
             raw = part.data();
             nbytes = part.size();
-        } else {
-            int rc = keep_raw(m, is_gate ? &L.rgate : &L.rup, type, f, h, raw, nbytes);
+        }
+        {
+            int rc = keep_raw(m, is_gate ? &L.rgate : &L.rup, type, m->ffn_l, h, raw, nbytes);
             if (rc) return rc;
         }
         if (L.stash_type < 0) {
@@ -860,7 +865,10 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
         /* the exchange region peers write into; the full logits live at its end */
         s->xchg_recv_n = (h + 63) & ~63;
         s->xchg_logits_off = FL_TP_RECV_OFF + (size_t)2 * FL_TP_MAX * s->xchg_recv_n * 4;
-        s->xchg_bytes = s->xchg_logits_off + (size_t)d.vocab * 4;
+        /* then the prompt path's partial sums: two slots of pf_tp_rows x hidden floats */
+        s->pf_tp_rows = std::min(max_ctx, 2048);
+        s->xchg_pf_off = (s->xchg_logits_off + (size_t)d.vocab * 4 + 255) & ~(size_t)255;
+        s->xchg_bytes = s->xchg_pf_off + (size_t)2 * s->pf_tp_rows * h * 4;
         AL(s->xchg, s->xchg_bytes);
         AL(s->tp_epoch, 16);
         if (!rc) s->logits = reinterpret_cast<float*>(s->xchg + s->xchg_logits_off);
@@ -1389,6 +1397,7 @@ static int pf_alloc(fl_session* s)
     const size_t per_tok = (size_t)m->nh_l * nkmax * 10;
     int cap = std::min(s->max_ctx, 2048);
     if ((size_t)cap * per_tok > ((size_t)4 << 30)) cap = std::max(16, (int)((((size_t)4 << 30) / per_tok) & ~(size_t)15));
+    if (m->T > 1) cap = std::min(cap, s->pf_tp_rows);
     size_t wmax = std::max({(size_t)(qd + 2 * kvd) * h, (size_t)h * qd, (size_t)2 * F * h, (size_t)h * F});
     if (s->n_slots > 1) wmax = std::max(wmax, (size_t)d.vocab * h); /* the LM head of batched steps */
     const size_t amax = std::max({(size_t)h, (size_t)qd, (size_t)F});
@@ -1415,6 +1424,37 @@ static int pf_alloc(fl_session* s)
     if (rc) return rc;
     LTCK(cublasLtCreate(&s->lt));
     s->pf_cap = cap;
+    return FL_OK;
+}
+
+/* Where a row-parallel projection writes: pf_y on one GPU; with tensor
+ * parallelism this rank's slot of the next exchange (its own memory, which
+ * the peers read). */
+static float* pf_partial(fl_session* s)
+{
+    if (s->m->T == 1) return s->pf_y;
+    const int parity = (s->pf_epoch + 1) & 1;
+    return reinterpret_cast<float*>(s->xchg + s->xchg_pf_off) + (size_t)parity * s->pf_tp_rows * s->m->d.hidden;
+}
+
+/* The allreduce of a row-parallel projection's [n x hidden] partial sums
+ * (the decode path's TP_REDUCE, for a chunk): raise this rank's flag on every
+ * peer with the next epoch, then wait (bounded) for every rank's flag and sum
+ * the ranks' slots in rank order into pf_y, identically on every rank. */
+static int pf_allreduce(fl_session* s, int n)
+{
+    fl_model* m = s->m;
+    if (m->T == 1) return FL_OK;
+    const int epoch = ++s->pf_epoch, parity = epoch & 1;
+    const size_t slot_off = s->xchg_pf_off + (size_t)parity * s->pf_tp_rows * m->d.hidden * 4;
+    const float* slots[FL_TP_MAX];
+    int* flags[FL_TP_MAX];
+    for (int q = 0; q < m->T; q++) {
+        slots[q] = reinterpret_cast<const float*>(s->tp_peer[q] + slot_off);
+        flags[q] = reinterpret_cast<int*>(s->tp_peer[q] + FL_TP_FLAGS_OFF);
+    }
+    CK(fl_launch_tp_prefill_reduce(slots, flags, m->T, m->rank, epoch, (size_t)n * m->d.hidden, s->pf_y,
+                                   s->state + ST_ERR, s->st));
     return FL_OK;
 }
 
@@ -1465,7 +1505,8 @@ static int pf_chunk(fl_session* s, int slot, const int32_t* tokens, int n, int s
         }
         /* output projection, residual (Gemma: post-attention norm), FFN norm */
         if ((rc = pf_dequant(s, L.ro, s->pf_w))) return rc;
-        if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_y, h, qd, n))) return rc;
+        if ((rc = pf_gemm(s, s->pf_w, s->pf_act, pf_partial(s), h, qd, n))) return rc;
+        if ((rc = pf_allreduce(s, n))) return rc;
         CK(fl_launch_rows_norm(s->pf_x, s->pf_y, gemma ? L.post_attn_norm : nullptr, L.ffn_norm, n, h, eps, gemma,
                                s->pf_act, s->st));
         /* gate and up stacked: columns [0, F) gate, [F, 2F) up */
@@ -1474,7 +1515,8 @@ static int pf_chunk(fl_session* s, int slot, const int32_t* tokens, int n, int s
         if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_y, 2 * F, h, n))) return rc;
         CK(fl_launch_glu(s->pf_y, n, F, gemma ? 1 : 0, s->pf_act, s->st));
         if ((rc = pf_dequant(s, L.rdown, s->pf_w))) return rc;
-        if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_y, h, F, n))) return rc;
+        if ((rc = pf_gemm(s, s->pf_w, s->pf_act, pf_partial(s), h, F, n))) return rc;
+        if ((rc = pf_allreduce(s, n))) return rc;
     }
     return FL_OK;
 }
@@ -1489,7 +1531,6 @@ static int prefill_impl(fl_session* s, int slot, const int32_t* tokens, int32_t 
     if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     fl_model* m = s->m;
     const fl_model_desc& d = m->d;
-    if (m->T > 1) return fail(FL_ERR_UNSUPPORTED, "the batched prompt path runs on one GPU (tp_size 1)");
     if (slot < 0 || slot >= s->n_slots) return fail(FL_ERR_ARG, "sequence slot %d outside [0, %d)", slot, s->n_slots);
     const int have = slot_length(s, slot);
     if (n < 0 || start_pos < 0 || start_pos > have || start_pos + n > s->max_ctx)
@@ -1502,6 +1543,7 @@ static int prefill_impl(fl_session* s, int slot, const int32_t* tokens, int32_t 
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
     int rc = FL_OK;
     if (!s->pf_cap && (rc = pf_alloc(s))) return rc;
+    if (m->T > 1) CK(cudaMemcpy(&s->pf_epoch, s->tp_epoch, 4, cudaMemcpyDeviceToHost)); /* continues the token loop's */
     cudaEvent_t ev[2] = {nullptr, nullptr};
     if (ms) {
         CK(cudaEventCreate(&ev[0]));
@@ -1512,6 +1554,8 @@ static int prefill_impl(fl_session* s, int slot, const int32_t* tokens, int32_t 
         const int len = std::min(s->pf_cap, n - c);
         rc = pf_chunk(s, slot, tokens + c, len, start_pos + c);
     }
+    if (m->T > 1 && !rc && cudaMemcpyAsync(s->tp_epoch, &s->pf_epoch, 4, cudaMemcpyHostToDevice, s->st) != cudaSuccess)
+        rc = fail(FL_ERR_CUDA, "epoch update failed");
     if (ms && !rc && cudaEventRecord(ev[1], s->st) != cudaSuccess) rc = fail(FL_ERR_CUDA, "cudaEventRecord failed");
     if (!rc && cudaStreamSynchronize(s->st) != cudaSuccess) rc = fail(FL_ERR_CUDA, "prefill: stream failed");
     if (!rc) rc = check_device_err(s);

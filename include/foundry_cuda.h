@@ -163,7 +163,9 @@ int fl_forward(fl_session* s, int32_t token, int32_t position, float* logits, in
  * dequantized bit-exactly, and every activation as an fp16 hi + lo pair;
  * the three significant cross products accumulated in fp32); norms, RoPE,
  * attention and the FFN activation in fp32.  start_pos must not skip cached
- * positions.  One GPU (tp_size 1). */
+ * positions.  With tensor parallelism every rank calls it with the same tokens
+ * (each computes its heads and FFN rows; the partial sums after attn_output and
+ * ffn_down are exchanged over NVLink through the connected exchange regions). */
 int fl_prefill(fl_session* s, const int32_t* tokens, int32_t n, int32_t start_pos);
 
 /* Greedy decode of n_steps tokens entirely on the device: step i feeds the

@@ -5,7 +5,8 @@ algorithm) and by two ranks of the token kernel, each holding its shard and
 exchanging partial sums and the argmax over NVLink.  Same bars as the
 single-GPU parity tests: logits within 1e-3 + 1e-2·|ref| at every
 teacher-forced step, greedy tokens identical, the device loop equal to the
-host loop; and every rank must see identical (full-vocabulary) logits.
+host loop; every rank must see identical (full-vocabulary) logits; and the
+same after the prompt went through the tensor-parallel prompt path.
 """
 from __future__ import annotations
 
@@ -64,3 +65,8 @@ def test_two_ranks_match_the_oracle(name, tmp_path):
     assert diverge is None or diverge >= 32, f"{name}: greedy token {diverge} differs"
     np.testing.assert_array_equal(r0["device"], r0["greedy"][:32])
     np.testing.assert_array_equal(r1["device"], r0["device"])
+    # after the tensor-parallel prompt path
+    np.testing.assert_array_equal(r0["pf_logits"], r1["pf_logits"])
+    err = np.abs(r0["pf_logits"] - logs)
+    worst = np.unravel_index(np.argmax(err - bound), err.shape)
+    assert (err <= bound).all(), f"{name} prefill: step {worst[0]} id {worst[1]}: {r0['pf_logits'][worst]} vs {logs[worst]}"

@@ -2,7 +2,8 @@
 tests/test_gpu_tp.py): loads this rank's shard of a generated GGUF, connects
 the ranks' sessions (handles gathered over a gloo group) and records, under
 teacher forcing, the logits and argmax of every decode step, then the greedy
-tokens of the host loop and of the device-resident loop."""
+tokens of the host loop and of the device-resident loop, and the teacher-forced
+logits again after the prompt went through the tensor-parallel fl_prefill."""
 from __future__ import annotations
 
 import argparse
@@ -54,8 +55,17 @@ def main() -> None:
     for i in range(len(prompt) - 1):
         fwd.forward(int(prompt[i]), i, kv, want_logits=False)
     device = fwd.decode_greedy(int(prompt[-1]), len(prompt) - 1, 32)
+    # the prompt path (tensor-parallel fl_prefill), then the same teacher-forced steps
+    kv = object()
+    fwd.prefill(prompt[:-1], 0, kv)
+    pos = len(prompt) - 1
+    pf_logits = []
+    for tok in [int(prompt[-1])] + [int(t) for t in toks[:-1]]:
+        fwd.forward(tok, pos, kv)
+        pf_logits.append(fwd.logits.copy())
+        pos += 1
     np.savez(Path(args.out) / f"rank{rank}.npz", logits=np.stack(logits), argmax=np.array(argmax),
-             greedy=np.array(greedy), device=np.array(device))
+             greedy=np.array(greedy), device=np.array(device), pf_logits=np.stack(pf_logits))
     dist.barrier()  # no rank unmaps or frees its exchange region while a peer may still use it
     fwd.close()
     model.close()
