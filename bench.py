@@ -286,6 +286,17 @@ def prefill_record(p: dict, d, peaks: dict, ws: int, cpu: dict) -> dict:
     }
 
 
+def profiler_range(args):
+    """With --profile-range: cudaProfilerStart now (the caller stops), through
+    the CUDA runtime the native library uses; else None."""
+    if not args.profile_range:
+        return None
+    import ctypes
+    cudart = ctypes.CDLL("libcudart.so.12")
+    cudart.cudaProfilerStart()
+    return cudart
+
+
 def run_batch(args):
     """Mistral-7B-architecture Q8_0, 32 concurrent
     sequences, each a 512-token random prompt (fl_prefill_seq into its own
@@ -312,6 +323,7 @@ def run_batch(args):
         nxt = fwd.forward_batch(nxt, pos, slots)
         pos += 1
     pos_timed = int(pos[0])
+    cudart = profiler_range(args)
     clocks = ClockSampler(0)
     clocks.start()
     t0 = time.perf_counter()
@@ -320,6 +332,8 @@ def run_batch(args):
         pos += 1
     dt = time.perf_counter() - t0
     clk = clocks.stop()
+    if cudart:
+        cudart.cudaProfilerStop()
     kvd = d.n_kv_heads * d.head_dim
     avg_ctx = pos_timed + args.steps / 2 + 1
     kv_bytes = B * d.n_layers * kvd * 4 * (2 * avg_ctx + 2)
@@ -481,6 +495,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true", help="profiling only: skip the CPU sample")
     ap.add_argument("--workload", default="decode", choices=["decode", "batch"],
                     help="decode: the bs=1 headline (default); batch: Mistral-7B Q8_0, 32 sequences (BASELINE configs[2])")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="profiling only: bracket the timed steps with cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off)")
     ap.add_argument("--prefill-only", action="store_true",
                     help="profiling only: the prompt path alone (one GPU), W + K device-timed passes")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],

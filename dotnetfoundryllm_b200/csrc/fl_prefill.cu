@@ -49,13 +49,39 @@ __device__ __forceinline__ void store_split(__half* row3, int K, int c, float v,
     row3[2 * K + c] = weight ? lo : hi;
 }
 
+/* An activation value of row r, column c (K per row): the split layout
+ * [hi | lo | hi] (rows of 3K) when stack == 0; else stacked, hi in row r and
+ * lo in row stack + r (rows of K), the input of the two-GEMM form. */
+__device__ __forceinline__ void store_act(__half* out, int K, int r, int c, float v, int stack)
+{
+    if (stack == 0) {
+        store_split(out + (size_t)r * 3 * K, K, c, v, false);
+        return;
+    }
+    const __half hi = __float2half_rn(v);
+    out[(size_t)r * K + c] = hi;
+    out[(size_t)(stack + r) * K + c] = __float2half_rn(v - __half2float(hi));
+}
+
+/* A weight value: [hi | hi | lo] rows of 3K (layout 0) or [hi | lo] rows of 2K (layout 1). */
+__device__ __forceinline__ void store_weight(__half* dst, int64_t r, int K, int c, float v, int layout)
+{
+    if (layout == 0) {
+        store_split(dst + r * 3 * K, K, c, v, true);
+        return;
+    }
+    const __half hi = __float2half_rn(v);
+    dst[r * 2 * K + c] = hi;
+    dst[r * 2 * K + K + c] = __float2half_rn(v - __half2float(hi));
+}
+
 __global__ void dequant_split_kernel(int type, const uint8_t* __restrict__ raw, int64_t n, int cols,
-                                     __half* __restrict__ dst)
+                                     __half* __restrict__ dst, int layout)
 {
     for (int64_t f = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; f < n; f += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = f / cols;
         const int c = (int)(f - r * cols);
-        store_split(dst + r * 3 * cols, cols, c, fl_dequant_elem(type, raw, f) * FL_PF_WSCALE, true);
+        store_weight(dst, r, cols, c, fl_dequant_elem(type, raw, f) * FL_PF_WSCALE, layout);
     }
 }
 
@@ -114,7 +140,8 @@ __device__ __forceinline__ void dequant8(const uint8_t* __restrict__ raw, int64_
 /* Weights in the split layout [hi | hi | lo] (scaled by FL_PF_WSCALE), 8
  * values per thread, each part written as one 16-byte store. */
 template <int TYPE>
-__global__ void dequant_split8_kernel(const uint8_t* __restrict__ raw, int64_t n8, int cols, __half* __restrict__ dst)
+__global__ void dequant_split8_kernel(const uint8_t* __restrict__ raw, int64_t n8, int cols, __half* __restrict__ dst,
+                                      int layout)
 {
     for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < n8; g += (int64_t)gridDim.x * blockDim.x) {
         const int64_t f0 = g * 8;
@@ -129,11 +156,17 @@ __global__ void dequant_split8_kernel(const uint8_t* __restrict__ raw, int64_t n
             hi[i] = __float2half_rn(x);
             lo[i] = __float2half_rn(x - __half2float(hi[i]));
         }
-        __half* row3 = dst + r * 3 * (int64_t)cols;
         const uint4 h4 = *reinterpret_cast<const uint4*>(hi), l4 = *reinterpret_cast<const uint4*>(lo);
-        *reinterpret_cast<uint4*>(row3 + c) = h4;
-        *reinterpret_cast<uint4*>(row3 + cols + c) = h4;
-        *reinterpret_cast<uint4*>(row3 + 2 * cols + c) = l4;
+        if (layout == 0) {
+            __half* row3 = dst + r * 3 * (int64_t)cols;
+            *reinterpret_cast<uint4*>(row3 + c) = h4;
+            *reinterpret_cast<uint4*>(row3 + cols + c) = h4;
+            *reinterpret_cast<uint4*>(row3 + 2 * cols + c) = l4;
+        } else {
+            __half* row2 = dst + r * 2 * (int64_t)cols;
+            *reinterpret_cast<uint4*>(row2 + c) = h4;
+            *reinterpret_cast<uint4*>(row2 + cols + c) = l4;
+        }
     }
 }
 
@@ -165,22 +198,29 @@ __device__ float block_sum(float v, float* red)
 /* One row per CTA: optionally x += y (Gemma: x += GemmaRmsNorm(y, post_w)),
  * then out = norm(x) * w as fp16 (RmsNorm, or GemmaRmsNorm with w + 1). */
 __global__ void rows_norm_kernel(float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ post_w,
-                                 const float* __restrict__ w, int h, float eps, int gemma, __half* __restrict__ out)
+                                 const float* __restrict__ w, int h, float eps, int gemma, __half* __restrict__ out,
+                                 int stack, const float* __restrict__ y_lo)
 {
+    /* y_lo (the two-GEMM form's second half, or NULL) is part of y */
     __shared__ float red[32];
     const int r = blockIdx.x;
     float* xr = x + (size_t)r * h;
     if (y) {
         const float* yr = y + (size_t)r * h;
+        const float* yl = y_lo ? y_lo + (size_t)r * h : nullptr;
+        auto yv = [&](int i) { return yl ? __fadd_rn(yr[i], yl[i]) : yr[i]; };
         float rp = 1.0f;
         if (post_w) {
             float sp = 0.0f;
-            for (int i = threadIdx.x; i < h; i += blockDim.x) sp = fmaf(yr[i], yr[i], sp);
+            for (int i = threadIdx.x; i < h; i += blockDim.x) {
+                const float v = yv(i);
+                sp = fmaf(v, v, sp);
+            }
             sp = block_sum(sp, red);
             rp = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(sp, (float)h), 1e-6f));
         }
         for (int i = threadIdx.x; i < h; i += blockDim.x) {
-            const float add = post_w ? __fmul_rn(__fmul_rn(yr[i], rp), __fadd_rn(post_w[i], 1.0f)) : yr[i];
+            const float add = post_w ? __fmul_rn(__fmul_rn(yv(i), rp), __fadd_rn(post_w[i], 1.0f)) : yv(i);
             xr[i] = __fadd_rn(xr[i], add);
         }
         __syncthreads();
@@ -192,7 +232,7 @@ __global__ void rows_norm_kernel(float* __restrict__ x, const float* __restrict_
     const float rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)h), eps));
     for (int i = threadIdx.x; i < h; i += blockDim.x) {
         const float wi = gemma ? __fadd_rn(w[i], 1.0f) : w[i];
-        store_split(out + (size_t)r * 3 * h, h, i, __fmul_rn(__fmul_rn(xr[i], rms), wi), false);
+        store_act(out, h, r, i, __fmul_rn(__fmul_rn(xr[i], rms), wi), stack);
     }
 }
 
@@ -203,7 +243,7 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, const float* __res
                                const float* __restrict__ bv, const float* __restrict__ rope_cs, int start_pos, int qd,
                                int kvd, int hd, float* __restrict__ q_out, float* __restrict__ k_cache,
                                float* __restrict__ v_cache, const int* __restrict__ row_pos,
-                               const int* __restrict__ row_slot, size_t slot_stride)
+                               const int* __restrict__ row_slot, size_t slot_stride, const float* __restrict__ qkv_lo)
 {
     /* row r is position start_pos + r of one sequence, or (batched decode)
      * position row_pos[r] of the sequence in cache slot row_slot[r] */
@@ -214,13 +254,15 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, const float* __res
     }
     const int width = qd + 2 * kvd;
     const float* row = qkv + (size_t)r * width;
+    const float* row_lo = qkv_lo ? qkv_lo + (size_t)r * width : nullptr; /* the second half, or NULL */
+    auto at = [&](int j) { return row_lo ? __fadd_rn(row[j], row_lo[j]) : row[j]; };
     for (int j = threadIdx.x; j < width; j += blockDim.x) {
         if (j < qd + kvd) {
             const bool is_q = j < qd;
             const int e = is_q ? j : j - qd;
             const float* b = is_q ? bq : bk;
             const int pe = e ^ 1;
-            float v = row[j], partner = row[is_q ? pe : qd + pe];
+            float v = at(j), partner = at(is_q ? pe : qd + pe);
             if (b) {
                 v = __fadd_rn(v, b[e]);
                 partner = __fadd_rn(partner, b[pe]);
@@ -234,7 +276,7 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, const float* __res
             else k_cache[(size_t)pos * kvd + e] = o;
         } else {
             const int e = j - qd - kvd;
-            float v = row[j];
+            float v = at(j);
             if (bv) v = __fadd_rn(v, bv[e]);
             v_cache[(size_t)pos * kvd + e] = v;
         }
@@ -245,60 +287,90 @@ __global__ void rope_kv_kernel(const float* __restrict__ qkv, const float* __res
  * ComputeAttention (LlamaForwardPass.cs:158-211, windows and softcap as in the
  * Mistral/Gemma passes) for row b, kv head g: the grp query heads of the
  * group against keys [max(0, p+1-window), p+1) of the row's cache slot.  Each
- * of the 8 warps takes every 8th key; lanes own head_dim/32 dims; a warp keeps
- * a running (max, sum, output) per head; the warps are merged in warp order. */
+ * of the 8 warps takes KPW = 1024/head_dim keys per round (head_dim/32 lanes
+ * per key for the scores, then every lane owns head_dim/32 dims of the
+ * values; the round's key and value loads are issued together) and keeps a
+ * running (max, sum, output) per head, updated once per round; the warps are
+ * merged in warp order. */
 template <int HD>
 __global__ void __launch_bounds__(256) batch_attn_kernel(const float* __restrict__ q, const float* __restrict__ k_cache,
                                                         const float* __restrict__ v_cache,
                                                         const int* __restrict__ row_pos,
                                                         const int* __restrict__ row_slot, size_t slot_stride, int nh,
                                                         int nkv, int window, float scale, float softcap,
-                                                        __half* __restrict__ out)
+                                                        __half* __restrict__ out, int stack)
 {
-    constexpr int PER = HD / 32, GM = HD == 256 ? 4 : 8, NWB = 8; /* GM: largest query-head group */
+    constexpr int GM = HD == 256 ? 4 : 8, NWB = 8; /* GM: largest query-head group */
+    constexpr int LPK = HD / 32, KPW = 32 / LPK, PER = HD / 32;
+    __shared__ __align__(16) float sq[GM][HD];
     __shared__ float s_o[NWB][GM][HD];
     __shared__ float s_ml[NWB][GM][2];
     const int b = blockIdx.x, g = blockIdx.y, grp = nh / nkv;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd4 = lane % LPK, kj = lane / LPK;
     const int qd = nh * HD, kvd = nkv * HD;
     const int pos = row_pos[b];
     const int k_lo = window < pos + 1 ? pos + 1 - window : 0;
-    const float* kc = k_cache + (size_t)row_slot[b] * slot_stride + (size_t)g * HD + lane * PER;
-    const float* vc = v_cache + (size_t)row_slot[b] * slot_stride + (size_t)g * HD + lane * PER;
+    const int n = pos + 1 - k_lo;
+    const float* kc = k_cache + (size_t)row_slot[b] * slot_stride + (size_t)k_lo * kvd + (size_t)g * HD;
+    const float* vc = v_cache + (size_t)row_slot[b] * slot_stride + (size_t)k_lo * kvd + (size_t)g * HD + lane * PER;
     const float inv_cap = softcap > 0.0f ? 1.0f / softcap : 0.0f;
-    float qv[GM][PER], o[GM][PER], m[GM], l[GM];
+    for (int i = threadIdx.x; i < grp * HD; i += blockDim.x) sq[i / HD][i % HD] = q[(size_t)b * qd + (size_t)g * grp * HD + i];
+    __syncthreads();
+    float m[GM], l[GM], o[GM][PER];
 #pragma unroll
     for (int h = 0; h < GM; h++) {
         m[h] = -INFINITY;
         l[h] = 0.0f;
 #pragma unroll
-        for (int p = 0; p < PER; p++) {
-            qv[h][p] = h < grp ? q[(size_t)b * qd + (size_t)(g * grp + h) * HD + lane * PER + p] : 0.0f;
-            o[h][p] = 0.0f;
-        }
+        for (int p = 0; p < PER; p++) o[h][p] = 0.0f;
     }
-    for (int k = k_lo + warp; k <= pos; k += NWB) {
-        float kk[PER], vv[PER];
+    for (int base = warp * KPW; base < n; base += NWB * KPW) {
+        const bool valid = base + kj < n;
+        float4 kv[8];
+        float vv[KPW][PER];
+        const int kk = min(base + kj, n - 1);
 #pragma unroll
-        for (int p = 0; p < PER; p++) {
-            kk[p] = kc[(size_t)k * kvd + p];
-            vv[p] = vc[(size_t)k * kvd + p];
+        for (int c = 0; c < 8; c++) kv[c] = *(reinterpret_cast<const float4*>(kc + (size_t)kk * kvd) + c * LPK + qd4);
+#pragma unroll
+        for (int j = 0; j < KPW; j++) {
+            const int t = min(base + j, n - 1);
+#pragma unroll
+            for (int p = 0; p < PER; p++) vv[j][p] = vc[(size_t)t * kvd + p];
         }
 #pragma unroll
         for (int h = 0; h < GM; h++) {
             if (h >= grp) break;
             float acc = 0.0f;
 #pragma unroll
-            for (int p = 0; p < PER; p++) acc = fmaf(qv[h][p], kk[p], acc);
-            acc = fl_warp_sum(acc);
+            for (int c = 0; c < 8; c++) {
+                const float4 q4 = reinterpret_cast<const float4*>(sq[h])[c * LPK + qd4];
+                acc = fmaf(q4.x, kv[c].x, acc);
+                acc = fmaf(q4.y, kv[c].y, acc);
+                acc = fmaf(q4.z, kv[c].z, acc);
+                acc = fmaf(q4.w, kv[c].w, acc);
+            }
+#pragma unroll
+            for (int off = 1; off < LPK; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
             float sc = __fmul_rn(acc, scale);
             if (softcap > 0.0f) sc = __fmul_rn(tanhf(__fmul_rn(sc, inv_cap)), softcap);
-            const float mn = fmaxf(m[h], sc);
-            const float corr = expf(m[h] - mn), pw = expf(sc - mn);
-            m[h] = mn;
-            l[h] = fmaf(l[h], corr, pw);
+            sc = valid ? sc : -INFINITY;
+            float mr = sc; /* the round's max (key `base` is valid) */
 #pragma unroll
-            for (int p = 0; p < PER; p++) o[h][p] = fmaf(pw, vv[p], o[h][p] * corr);
+            for (int off = LPK; off < 32; off <<= 1) mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, off));
+            const float mn = fmaxf(m[h], mr);
+            const float corr = __expf(m[h] - mn); /* 0 on the first round */
+            const float pw = __expf(sc - mn);     /* 0 past the keys */
+            m[h] = mn;
+            l[h] *= corr;
+#pragma unroll
+            for (int p = 0; p < PER; p++) o[h][p] *= corr;
+#pragma unroll
+            for (int j = 0; j < KPW; j++) {
+                const float pj = __shfl_sync(0xffffffffu, pw, j * LPK);
+                l[h] += pj;
+#pragma unroll
+                for (int p = 0; p < PER; p++) o[h][p] = fmaf(pj, vv[j][p], o[h][p]);
+            }
         }
     }
 #pragma unroll
@@ -321,12 +393,20 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(const float* __restrict
 #pragma unroll
         for (int w = 0; w < NWB; w++) {
             const float mw = s_ml[w][h][0];
-            const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+            const float f = mw == -INFINITY ? 0.0f : __expf(mw - M);
             O = fmaf(s_o[w][h][d], f, O);
             L = fmaf(s_ml[w][h][1], f, L);
         }
-        store_split(out + (size_t)b * 3 * qd, qd, (g * grp + h) * HD + d, L > 0.0f ? O / L : 0.0f, false);
+        store_act(out, qd, b, (g * grp + h) * HD + d, L > 0.0f ? O / L : 0.0f, stack);
     }
+}
+
+/* The two-GEMM form's halves: y[b][j] = p[b][j] + p[B + b][j]. */
+__global__ void add_halves_kernel(const float* __restrict__ p, int B, int N, float* __restrict__ y)
+{
+    const size_t total = (size_t)B * N;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
+        y[i] = __fadd_rn(p[i], p[total + i]);
 }
 
 /* TensorOperations.SoftCap (TensorOperations.cs:120-126) on logits rows */
@@ -539,19 +619,25 @@ __global__ void attn_out_kernel(const float* __restrict__ O, int n, int nh, int 
     }
 }
 
-__global__ void glu_kernel(const float* __restrict__ g, int n, int F, int gelu, __half* __restrict__ act)
+__global__ void glu_kernel(const float* __restrict__ g, int n, int F, int gelu, __half* __restrict__ act, int stack,
+                           const float* __restrict__ g_lo)
 {
     const int64_t total = (int64_t)n * F;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / F, c = i % F;
-        const float gv = g[r * 2 * F + c], up = g[r * 2 * F + F + c];
-        store_split(act + r * 3 * F, F, (int)c, __fmul_rn(gelu ? pf_gelu(gv) : pf_silu(gv), up), false);
+        float gv = g[r * 2 * F + c], up = g[r * 2 * F + F + c];
+        if (g_lo) {
+            gv = __fadd_rn(gv, g_lo[r * 2 * F + c]);
+            up = __fadd_rn(up, g_lo[r * 2 * F + F + c]);
+        }
+        store_act(act, F, (int)r, (int)c, __fmul_rn(gelu ? pf_gelu(gv) : pf_silu(gv), up), stack);
     }
 }
 
 } // namespace
 
-cudaError_t fl_launch_dequant_split(int32_t type, const uint8_t* raw, int rows, int cols, __half* dst, cudaStream_t st)
+cudaError_t fl_launch_dequant_split(int32_t type, const uint8_t* raw, int rows, int cols, __half* dst, cudaStream_t st,
+                                    int layout)
 {
     const int64_t n = (int64_t)rows * cols;
     if (cols % 8 == 0) {
@@ -560,18 +646,18 @@ cudaError_t fl_launch_dequant_split(int32_t type, const uint8_t* raw, int rows, 
         if (b8 > 148 * 16) b8 = 148 * 16;
         if (b8 < 1) b8 = 1;
         switch (type) {
-        case FL_T_Q4_K: dequant_split8_kernel<FL_T_Q4_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
-        case FL_T_Q5_K: dequant_split8_kernel<FL_T_Q5_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
-        case FL_T_Q6_K: dequant_split8_kernel<FL_T_Q6_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
-        case FL_T_Q8_0: dequant_split8_kernel<FL_T_Q8_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
-        case FL_T_Q4_0: dequant_split8_kernel<FL_T_Q4_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst); return cudaGetLastError();
+        case FL_T_Q4_K: dequant_split8_kernel<FL_T_Q4_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
+        case FL_T_Q5_K: dequant_split8_kernel<FL_T_Q5_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
+        case FL_T_Q6_K: dequant_split8_kernel<FL_T_Q6_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
+        case FL_T_Q8_0: dequant_split8_kernel<FL_T_Q8_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
+        case FL_T_Q4_0: dequant_split8_kernel<FL_T_Q4_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
         default: break;
         }
     }
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 32) blocks = 148 * 32;
     if (blocks < 1) blocks = 1;
-    dequant_split_kernel<<<(unsigned)blocks, 256, 0, st>>>(type, raw, n, cols, dst);
+    dequant_split_kernel<<<(unsigned)blocks, 256, 0, st>>>(type, raw, n, cols, dst, layout);
     return cudaGetLastError();
 }
 
@@ -583,9 +669,9 @@ cudaError_t fl_launch_embed_rows(int32_t type, const uint8_t* raw, const int32_t
 }
 
 cudaError_t fl_launch_rows_norm(float* x, const float* y, const float* post_w, const float* w, int n, int h, float eps,
-                                int gemma, __half* out, cudaStream_t st)
+                                int gemma, __half* out, cudaStream_t st, int stack, const float* y_lo)
 {
-    rows_norm_kernel<<<n, 256, 0, st>>>(x, y, post_w, w, h, eps, gemma, out);
+    rows_norm_kernel<<<n, n < 148 ? 1024 : 256, 0, st>>>(x, y, post_w, w, h, eps, gemma, out, stack, y_lo);
     return cudaGetLastError();
 }
 
@@ -594,31 +680,37 @@ cudaError_t fl_launch_rope_kv(const float* qkv, const float* bq, const float* bk
                               float* v_cache, cudaStream_t st)
 {
     rope_kv_kernel<<<n, 256, 0, st>>>(qkv, bq, bk, bv, rope_cs, start_pos, qd, kvd, hd, q_out, k_cache, v_cache,
-                                      nullptr, nullptr, 0);
+                                      nullptr, nullptr, 0, nullptr);
     return cudaGetLastError();
 }
 
 cudaError_t fl_launch_rope_kv_rows(const float* qkv, const float* bq, const float* bk, const float* bv,
                                    const float* rope_cs, const int* row_pos, const int* row_slot, size_t slot_stride,
                                    int n, int qd, int kvd, int hd, float* q_out, float* k_cache, float* v_cache,
-                                   cudaStream_t st)
+                                   cudaStream_t st, const float* qkv_lo)
 {
-    rope_kv_kernel<<<n, 256, 0, st>>>(qkv, bq, bk, bv, rope_cs, 0, qd, kvd, hd, q_out, k_cache, v_cache, row_pos,
-                                      row_slot, slot_stride);
+    rope_kv_kernel<<<n, n < 148 ? 1024 : 256, 0, st>>>(qkv, bq, bk, bv, rope_cs, 0, qd, kvd, hd, q_out, k_cache,
+                                                       v_cache, row_pos, row_slot, slot_stride, qkv_lo);
     return cudaGetLastError();
 }
 
 cudaError_t fl_launch_batch_attn(const float* q, const float* k_cache, const float* v_cache, const int* row_pos,
                                  const int* row_slot, size_t slot_stride, int B, int nh, int nkv, int hd, int window,
-                                 float scale, float softcap, __half* out, cudaStream_t st)
+                                 float scale, float softcap, __half* out, cudaStream_t st, int stack)
 {
     dim3 grid((unsigned)B, (unsigned)nkv);
     switch (hd) {
-    case 64: batch_attn_kernel<64><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out); break;
-    case 128: batch_attn_kernel<128><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out); break;
-    case 256: batch_attn_kernel<256><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out); break;
+    case 64: batch_attn_kernel<64><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out, stack); break;
+    case 128: batch_attn_kernel<128><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out, stack); break;
+    case 256: batch_attn_kernel<256><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out, stack); break;
     default: return cudaErrorInvalidValue;
     }
+    return cudaGetLastError();
+}
+
+cudaError_t fl_launch_add_halves(const float* p, int B, int N, float* y, cudaStream_t st)
+{
+    add_halves_kernel<<<148 * 2, 256, 0, st>>>(p, B, N, y);
     return cudaGetLastError();
 }
 
@@ -691,12 +783,13 @@ cudaError_t fl_launch_attn_out(const float* O, int n, int nh, int nkv, int hd, _
     return cudaGetLastError();
 }
 
-cudaError_t fl_launch_glu(const float* g, int n, int F, int gelu, __half* act, cudaStream_t st)
+cudaError_t fl_launch_glu(const float* g, int n, int F, int gelu, __half* act, cudaStream_t st, int stack,
+                          const float* g_lo)
 {
     const int64_t total = (int64_t)n * F;
     int64_t blocks = (total + 255) / 256;
     if (blocks > 148 * 32) blocks = 148 * 32;
     if (blocks < 1) blocks = 1;
-    glu_kernel<<<(unsigned)blocks, 256, 0, st>>>(g, n, F, gelu, act);
+    glu_kernel<<<(unsigned)blocks, 256, 0, st>>>(g, n, F, gelu, act, stack, g_lo);
     return cudaGetLastError();
 }

@@ -160,6 +160,7 @@ struct fl_session {
      * (per layer qkv, wo, gate/up, down; then the LM head) */
     int32_t *bt_pos = nullptr, *bt_slot = nullptr, *bt_argmax = nullptr;
     float* bt_logits = nullptr;
+    float* bt_y2 = nullptr; /* [2 * slots][widest projection] partial halves of the two-GEMM form */
     bool bt_cache_tried = false;
     std::vector<__half*> bt_w;
     /* attention of a chunk: split Q/K/V^T, scores, split probabilities, output */
@@ -1322,12 +1323,16 @@ extern "C" int fl_topk_device(const float* logits, int32_t n, int32_t k, int32_t
         if (st_ != CUBLAS_STATUS_SUCCESS) return fail(FL_ERR_CUDA, "%s: cuBLASLt status %d", #call, (int)st_); \
     } while (0)
 
-/* Y[n x N] (fp32, row-major, ld N) = alpha * X[n x K] · W[N x K]^T (fp16,
- * row-major, ld K): the column-major "TN" product Y^T = W · X^T on the tensor
- * cores with fp32 accumulation, `batch` times with the given element strides. */
+/* Y[n x N] (fp32, row-major, ld N) = alpha * X[n x K] · W[N x K]^T + beta * Y
+ * (fp16, row-major, leading dimensions ldw / ldx, default K): the
+ * column-major "TN" product Y^T = W · X^T on the tensor cores with fp32
+ * accumulation, `batch` times with the given element strides. */
 static int lt_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K, int n, float alpha,
-                   int batch = 1, int64_t sW = 0, int64_t sX = 0, int64_t sY = 0)
+                   int batch = 1, int64_t sW = 0, int64_t sX = 0, int64_t sY = 0, int ldw = 0, int ldx = 0,
+                   float beta = 0.0f)
 {
+    if (!ldw) ldw = K;
+    if (!ldx) ldx = K;
     cublasLtMatmulDesc_t op = nullptr;
     cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
     int rc = FL_OK;
@@ -1335,8 +1340,8 @@ static int lt_gemm(fl_session* s, const __half* W, const __half* X, float* Y, in
     const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
     if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof ta);
     if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof tb);
-    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&la, CUDA_R_16F, K, N, K);
-    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&lb, CUDA_R_16F, K, n, K);
+    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&la, CUDA_R_16F, K, N, ldw);
+    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&lb, CUDA_R_16F, K, n, ldx);
     if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&lc, CUDA_R_32F, N, n, N);
     if (batch > 1) {
         const cublasLtMatrixLayout_t ls[3] = {la, lb, lc};
@@ -1358,9 +1363,8 @@ static int lt_gemm(fl_session* s, const __half* W, const __half* X, float* Y, in
     if (st == CUBLAS_STATUS_SUCCESS)
         st = cublasLtMatmulAlgoGetHeuristic(s->lt, op, la, lb, lc, lc, pref, 1, &heur, &found);
     if (st == CUBLAS_STATUS_SUCCESS && found < 1) st = CUBLAS_STATUS_NOT_SUPPORTED;
-    const float zero = 0.0f;
     if (st == CUBLAS_STATUS_SUCCESS)
-        st = cublasLtMatmul(s->lt, op, &alpha, W, la, X, lb, &zero, Y, lc, Y, lc, &heur.algo, s->lt_ws, s->lt_ws_bytes,
+        st = cublasLtMatmul(s->lt, op, &alpha, W, la, X, lb, &beta, Y, lc, Y, lc, &heur.algo, s->lt_ws, s->lt_ws_bytes,
                             s->st);
     if (st != CUBLAS_STATUS_SUCCESS)
         rc = fail(FL_ERR_CUDA, "cuBLASLt GEMM %dx%dx%d (batch %d): status %d", N, n, K, batch, (int)st);
@@ -1383,6 +1387,13 @@ static int pf_gemm(fl_session* s, const __half* W, const __half* X, float* Y, in
 static int pf_dequant(fl_session* s, const RawMatrix& r, __half* dst)
 {
     CK(fl_launch_dequant_split(r.type, r.d, r.rows, r.cols, dst, s->st));
+    return FL_OK;
+}
+
+/* the same as [hi | lo] rows (rows x 2*cols), the batched steps' layout */
+static int bt_dequant(fl_session* s, const RawMatrix& r, __half* dst)
+{
+    CK(fl_launch_dequant_split(r.type, r.d, r.rows, r.cols, dst, s->st, 1));
     return FL_OK;
 }
 
@@ -1586,8 +1597,9 @@ extern "C" int fl_time_prefill(fl_session* s, const int32_t* tokens, int32_t n, 
 /* ── batched decode ─────────────────────────────────────────────────────── */
 
 /* The split-fp16 weights of every projection and of the LM head, kept for
- * the session's batched steps: 6 bytes per weight (8B: ~45 GB), tried once;
- * without them each step dequantizes into the prompt path's buffer. */
+ * the session's batched steps as [hi | lo] rows: 4 bytes per weight (8B:
+ * ~30 GB), tried once; without them each step dequantizes into the prompt
+ * path's buffer. */
 static void bt_cache_weights(fl_session* s)
 {
     s->bt_cache_tried = true;
@@ -1603,7 +1615,7 @@ static void bt_cache_weights(fl_session* s)
     }
     sizes.push_back((size_t)d.vocab * h);
     size_t total = 0;
-    for (size_t e : sizes) total += (e * 3 * 2 + 255) & ~(size_t)255;
+    for (size_t e : sizes) total += (e * 2 * 2 + 255) & ~(size_t)255;
     size_t free_b = 0, tot_b = 0;
     if (cudaMemGetInfo(&free_b, &tot_b) != cudaSuccess || total + ((size_t)4 << 30) > free_b) return;
     uint8_t* base = nullptr;
@@ -1615,20 +1627,34 @@ static void bt_cache_weights(fl_session* s)
     size_t off = 0;
     for (size_t e : sizes) {
         s->bt_w.push_back(reinterpret_cast<__half*>(base + off));
-        off += (e * 3 * 2 + 255) & ~(size_t)255;
+        off += (e * 2 * 2 + 255) & ~(size_t)255;
     }
     for (int l = 0; l < d.n_layers; l++) {
         const Layer& L = m->layers[(size_t)l];
         __half** w = &s->bt_w[(size_t)l * 4];
-        if (pf_dequant(s, L.rq, w[0]) || pf_dequant(s, L.rk, w[0] + (size_t)qd * 3 * h) ||
-            pf_dequant(s, L.rv, w[0] + (size_t)(qd + kvd) * 3 * h) || pf_dequant(s, L.ro, w[1]) ||
-            pf_dequant(s, L.rgate, w[2]) || pf_dequant(s, L.rup, w[2] + (size_t)F * 3 * h) ||
-            pf_dequant(s, L.rdown, w[3])) {
+        if (bt_dequant(s, L.rq, w[0]) || bt_dequant(s, L.rk, w[0] + (size_t)qd * 2 * h) ||
+            bt_dequant(s, L.rv, w[0] + (size_t)(qd + kvd) * 2 * h) || bt_dequant(s, L.ro, w[1]) ||
+            bt_dequant(s, L.rgate, w[2]) || bt_dequant(s, L.rup, w[2] + (size_t)F * 2 * h) ||
+            bt_dequant(s, L.rdown, w[3])) {
             s->bt_w.clear();
             return;
         }
     }
-    if (pf_dequant(s, m->rout, s->bt_w.back())) s->bt_w.clear();
+    if (bt_dequant(s, m->rout, s->bt_w.back())) s->bt_w.clear();
+}
+
+/* Y[B x N] = X · W^T in the two-GEMM form: X stacked ([B hi rows; B lo
+ * rows] of K), W as [hi | lo] rows of 2K (scaled by FL_PF_WSCALE); the hi
+ * weights meet both activation halves in one GEMM, the lo weights the hi
+ * half in a second accumulating into the first B rows, then the halves add.
+ * Every weight byte is read once. */
+static int bt_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K, int B)
+{
+    int rc = lt_gemm(s, W, X, s->bt_y2, N, K, 2 * B, 1.0f / FL_PF_WSCALE, 1, 0, 0, 0, 2 * K, K);
+    if (!rc) rc = lt_gemm(s, W + K, X, s->bt_y2, N, K, B, 1.0f / FL_PF_WSCALE, 1, 0, 0, 0, 2 * K, K, 1.0f);
+    if (rc) return rc;
+    if (Y) CK(fl_launch_add_halves(s->bt_y2, B, N, Y, s->st));
+    return FL_OK;
 }
 
 extern "C" int fl_forward_batch(fl_session* s, int32_t B, const int32_t* tokens, const int32_t* positions,
@@ -1656,18 +1682,22 @@ extern "C" int fl_forward_batch(fl_session* s, int32_t B, const int32_t* tokens,
     int rc = FL_OK;
     if (!s->pf_cap && (rc = pf_alloc(s))) return rc;
     if (B > s->pf_cap) return fail(FL_ERR_UNSUPPORTED, "batch %d above the prompt path's %d rows", B, s->pf_cap);
+    const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, F = m->ffn_l, hd = d.head_dim;
     if (!s->bt_pos) {
         const int S = s->n_slots;
+        const size_t widest = std::max({(size_t)(qd + 2 * kvd), (size_t)h, (size_t)2 * F, (size_t)d.vocab});
         if ((rc = dalloc(s->allocs, &s->bt_pos, (size_t)S * 4)) || (rc = dalloc(s->allocs, &s->bt_slot, (size_t)S * 4)) ||
             (rc = dalloc(s->allocs, &s->bt_argmax, (size_t)S * 4)) ||
-            (rc = dalloc(s->allocs, &s->bt_logits, (size_t)S * d.vocab * 4)))
+            (rc = dalloc(s->allocs, &s->bt_logits, (size_t)S * d.vocab * 4)) ||
+            (rc = dalloc(s->allocs, &s->bt_y2, (size_t)2 * S * widest * 4)))
             return rc;
     }
     if (!s->bt_cache_tried) bt_cache_weights(s);
     const bool cached = !s->bt_w.empty();
-    const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, F = m->ffn_l, hd = d.head_dim;
     const bool gemma = d.arch == FL_ARCH_GEMMA2;
     const float eps = gemma ? 1e-6f : d.rms_eps;
+    /* activations are stacked for the two-GEMM form: B hi rows, then B lo rows */
+    const int stk = B;
     CK(cudaMemcpyAsync(s->pf_tokens, tokens, (size_t)B * 4, cudaMemcpyHostToDevice, s->st));
     CK(cudaMemcpyAsync(s->bt_pos, positions, (size_t)B * 4, cudaMemcpyHostToDevice, s->st));
     CK(cudaMemcpyAsync(s->bt_slot, slots, (size_t)B * 4, cudaMemcpyHostToDevice, s->st));
@@ -1675,44 +1705,47 @@ extern "C" int fl_forward_batch(fl_session* s, int32_t B, const int32_t* tokens,
     for (int l = 0; l < d.n_layers; l++) {
         Layer& L = m->layers[(size_t)l];
         __half* const* cw = cached ? &s->bt_w[(size_t)l * 4] : nullptr;
-        const float* prev = l > 0 ? s->pf_y : nullptr;
+        /* a projection's output stays as the two halves in bt_y2 ([B][N], then
+         * [B][N]); the next kernel adds them as it reads */
+        const float* prev = l > 0 ? s->bt_y2 : nullptr;
+        const float* prev_lo = l > 0 ? s->bt_y2 + (size_t)B * h : nullptr;
         const float* prev_post = l > 0 && gemma ? m->layers[(size_t)l - 1].post_ffn_norm : nullptr;
-        CK(fl_launch_rows_norm(s->pf_x, prev, prev_post, L.attn_norm, B, h, eps, gemma, s->pf_act, s->st));
+        CK(fl_launch_rows_norm(s->pf_x, prev, prev_post, L.attn_norm, B, h, eps, gemma, s->pf_act, s->st, stk, prev_lo));
         const __half* w = cached ? cw[0] : s->pf_w;
-        if (!cached && ((rc = pf_dequant(s, L.rq, s->pf_w)) || (rc = pf_dequant(s, L.rk, s->pf_w + (size_t)qd * 3 * h)) ||
-                        (rc = pf_dequant(s, L.rv, s->pf_w + (size_t)(qd + kvd) * 3 * h))))
+        if (!cached && ((rc = bt_dequant(s, L.rq, s->pf_w)) || (rc = bt_dequant(s, L.rk, s->pf_w + (size_t)qd * 2 * h)) ||
+                        (rc = bt_dequant(s, L.rv, s->pf_w + (size_t)(qd + kvd) * 2 * h))))
             return rc;
-        if ((rc = pf_gemm(s, w, s->pf_act, s->pf_qkv, qd + 2 * kvd, h, B))) return rc;
+        if ((rc = bt_gemm(s, w, s->pf_act, nullptr, qd + 2 * kvd, h, B))) return rc;
         float* kc = s->kc + (size_t)l * s->max_ctx * kvd;
         float* vc = s->vc + (size_t)l * s->max_ctx * kvd;
-        CK(fl_launch_rope_kv_rows(s->pf_qkv, L.bq, L.bk, L.bv, m->rope_cs, s->bt_pos, s->bt_slot, s->slot_stride, B, qd,
-                                  kvd, hd, s->pf_q, kc, vc, s->st));
+        CK(fl_launch_rope_kv_rows(s->bt_y2, L.bq, L.bk, L.bv, m->rope_cs, s->bt_pos, s->bt_slot, s->slot_stride, B, qd,
+                                  kvd, hd, s->pf_q, kc, vc, s->st, s->bt_y2 + (size_t)B * (qd + 2 * kvd)));
         int window = INT_MAX;
         if (d.arch == FL_ARCH_MISTRAL) window = d.sliding_window;
         if (gemma && (l % 2) == 0) window = d.sliding_window; /* Gemma2ForwardPass.cs:87 */
         if (window <= 0) window = INT_MAX;
         CK(fl_launch_batch_attn(s->pf_q, kc, vc, s->bt_pos, s->bt_slot, s->slot_stride, B, m->nh_l, m->nkv_l, hd, window,
-                                d.attn_scale, gemma ? d.attn_softcap : 0.0f, s->pf_act, s->st));
+                                d.attn_scale, gemma ? d.attn_softcap : 0.0f, s->pf_act, s->st, stk));
         w = cached ? cw[1] : s->pf_w;
-        if (!cached && (rc = pf_dequant(s, L.ro, s->pf_w))) return rc;
-        if ((rc = pf_gemm(s, w, s->pf_act, s->pf_y, h, qd, B))) return rc;
-        CK(fl_launch_rows_norm(s->pf_x, s->pf_y, gemma ? L.post_attn_norm : nullptr, L.ffn_norm, B, h, eps, gemma,
-                               s->pf_act, s->st));
+        if (!cached && (rc = bt_dequant(s, L.ro, s->pf_w))) return rc;
+        if ((rc = bt_gemm(s, w, s->pf_act, nullptr, h, qd, B))) return rc;
+        CK(fl_launch_rows_norm(s->pf_x, s->bt_y2, gemma ? L.post_attn_norm : nullptr, L.ffn_norm, B, h, eps, gemma,
+                               s->pf_act, s->st, stk, s->bt_y2 + (size_t)B * h));
         w = cached ? cw[2] : s->pf_w;
-        if (!cached && ((rc = pf_dequant(s, L.rgate, s->pf_w)) || (rc = pf_dequant(s, L.rup, s->pf_w + (size_t)F * 3 * h))))
+        if (!cached && ((rc = bt_dequant(s, L.rgate, s->pf_w)) || (rc = bt_dequant(s, L.rup, s->pf_w + (size_t)F * 2 * h))))
             return rc;
-        if ((rc = pf_gemm(s, w, s->pf_act, s->pf_y, 2 * F, h, B))) return rc;
-        CK(fl_launch_glu(s->pf_y, B, F, gemma ? 1 : 0, s->pf_act, s->st));
+        if ((rc = bt_gemm(s, w, s->pf_act, nullptr, 2 * F, h, B))) return rc;
+        CK(fl_launch_glu(s->bt_y2, B, F, gemma ? 1 : 0, s->pf_act, s->st, stk, s->bt_y2 + (size_t)B * 2 * F));
         w = cached ? cw[3] : s->pf_w;
-        if (!cached && (rc = pf_dequant(s, L.rdown, s->pf_w))) return rc;
-        if ((rc = pf_gemm(s, w, s->pf_act, s->pf_y, h, F, B))) return rc;
+        if (!cached && (rc = bt_dequant(s, L.rdown, s->pf_w))) return rc;
+        if ((rc = bt_gemm(s, w, s->pf_act, nullptr, h, F, B))) return rc;
     }
     /* final norm (after the last residual) and the LM head */
-    CK(fl_launch_rows_norm(s->pf_x, s->pf_y, gemma ? m->layers.back().post_ffn_norm : nullptr, m->out_norm, B, h, eps,
-                           gemma, s->pf_act, s->st));
+    CK(fl_launch_rows_norm(s->pf_x, s->bt_y2, gemma ? m->layers.back().post_ffn_norm : nullptr, m->out_norm, B, h, eps,
+                           gemma, s->pf_act, s->st, stk, s->bt_y2 + (size_t)B * h));
     const __half* wh = cached ? s->bt_w.back() : s->pf_w;
-    if (!cached && (rc = pf_dequant(s, m->rout, s->pf_w))) return rc;
-    if ((rc = pf_gemm(s, wh, s->pf_act, s->bt_logits, d.vocab, h, B))) return rc;
+    if (!cached && (rc = bt_dequant(s, m->rout, s->pf_w))) return rc;
+    if ((rc = bt_gemm(s, wh, s->pf_act, s->bt_logits, d.vocab, h, B))) return rc;
     if (gemma && d.final_softcap > 0.0f) CK(fl_launch_softcap_rows(s->bt_logits, (size_t)B * d.vocab, d.final_softcap, s->st));
     CK(fl_launch_argmax_rows(s->bt_logits, B, d.vocab, s->bt_argmax, s->st));
     if (argmax) CK(cudaMemcpyAsync(argmax, s->bt_argmax, (size_t)B * 4, cudaMemcpyDeviceToHost, s->st));
