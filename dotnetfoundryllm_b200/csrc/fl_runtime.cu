@@ -973,7 +973,7 @@ static int session_build(fl_session* s)
     const int span = d.sliding_window > 0 ? std::min(max_ctx, d.sliding_window) : max_ctx;
     const int per_max = (span + s->attn_split - 1) / s->attn_split;
     const size_t attn =
-        (size_t)(grp * d.head_dim + FL_TK_WARPS * grp * d.head_dim + FL_TK_WARPS * 8 + per_max * grp) * 4;
+        (size_t)(grp * d.head_dim + FL_TK_WARPS * grp * d.head_dim + FL_TK_WARPS * 8 * 2 + per_max * grp) * 4;
     const size_t scratch = std::max(xenc, attn);
     const int n_feed = (int)feed.size();
     int n_slots = 1;

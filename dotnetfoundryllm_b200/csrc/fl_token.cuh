@@ -240,15 +240,14 @@ __device__ __forceinline__ void load_row_smem(const float* p, float (&v)[PER])
     }
 }
 
-/* Attention for items (kv head, split) b, b+G, ... in two passes over the
- * item's keys:
- *  1. scores: head_dim/32 lanes per key (32 dims each, log2 of that many
- *     shuffles to combine), for all query heads of the group; then the
- *     CTA-wide maximum and the softmax weights exp(s - max) of every score;
- *  2. values: lanes own head_dim/32 dims, warps split the keys, the weights
- *     come from shared memory; the warps' sums are added in warp order.
- * The item's (max, sum, unnormalized output) goes to global memory; the
- * combine phase merges the splits.
+/* Attention for items (kv head, split) b, b+G, ... in one pass over the
+ * item's keys.  A warp takes KPW = 1024/head_dim keys per round: head_dim/32
+ * lanes per key form the scores of every query head of the group, then every
+ * lane owns head_dim/32 dims of the round's values (loaded once the key
+ * registers are free).  Each warp keeps a running (max, sum, output) per
+ * query head, updated once per round (online softmax); the CTA merges its
+ * warps in warp order into the item's partial (max, sum, unnormalized
+ * output), which the combine phase merges across splits.
  * ComputeAttention: LlamaForwardPass.cs:158-211; MistralForwardPass.cs:186-240;
  * Gemma2ForwardPass.cs:126-185. */
 template <int HD, int GMAX>
@@ -258,17 +257,14 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr, uint64_t* stamps)
 #define FL_STAMP(i) \
     if (stamps && threadIdx.x == 0 && item == (int)blockIdx.x) stamps[i] = fl_globaltimer()
     const int grp = a.n_heads / a.n_kv; /* query heads per kv head, <= GMAX */
-    constexpr int LPK = HD / 32;  /* lanes per key in pass 1, 8 float4 chunks each */
-    constexpr int KPW = 32 / LPK; /* keys per warp per round */
-    constexpr int PER = HD / 32;  /* dims per lane in pass 2 */
-    constexpr int VB = 16 / PER;  /* keys per warp in flight in pass 2 */
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = lane % LPK;
+    constexpr int LPK = HD / 32;        /* lanes per key for the scores, 8 float4 chunks each */
+    constexpr int KPW = 32 / LPK;       /* keys per warp per round */
+    constexpr int PER = HD / 32;        /* value dims per lane */
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = lane % LPK, kj = lane / LPK;
     const int kv_dim = a.n_kv * HD;
-    float* sq = scr;                      /* [grp][HD] */
-    float* sacc = sq + grp * HD;          /* [NW][grp][HD] */
-    float* sred = sacc + NW * grp * HD;   /* [NW][GMAX] */
-    float* sp = sred + NW * GMAX;         /* [keys][grp] scores, then weights */
-    __shared__ float s_M[8], s_L[8];
+    float* sq = scr;                   /* [grp][HD] */
+    float* sacc = sq + grp * HD;       /* [NW][grp][HD] */
+    float* sml = sacc + NW * grp * HD; /* [NW][GMAX][2] running (max, sum) */
     const int seq = __ldcg(a.pos) + 1;
     int start = 0;
     if (a.window < seq) start = seq - a.window;
@@ -279,131 +275,108 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr, uint64_t* stamps)
         const int kvh = item / a.n_split, split = item % a.n_split;
         const int k0 = start + split * per;
         const int n = max(0, min(seq, k0 + per) - k0);
+        const float* kbase = a.k_cache + (size_t)k0 * kv_dim + (size_t)kvh * HD;
+        const float* vbase = a.v_cache + (size_t)k0 * kv_dim + (size_t)kvh * HD + lane * PER;
         for (int i = threadIdx.x; i < grp * HD; i += NC) sq[i] = __ldcg(a.q + (size_t)kvh * grp * HD + i);
         consumer_sync();
         FL_STAMP(0);
 
-        /* pass 1: scores */
-        float mloc[GMAX];
+        float m_run[GMAX], l_run[GMAX], o[GMAX][PER];
 #pragma unroll
-        for (int h = 0; h < GMAX; h++) mloc[h] = -INFINITY;
-        for (int base = 0; base < n; base += NW * KPW) {
-            const int kk = base + warp * KPW + lane / LPK;
-            float acc[GMAX];
+        for (int h = 0; h < GMAX; h++) {
+            m_run[h] = -INFINITY;
+            l_run[h] = 0.0f;
 #pragma unroll
-            for (int h = 0; h < GMAX; h++) acc[h] = 0.0f;
-            if (kk < n) {
-                const float* kr = a.k_cache + (size_t)(k0 + kk) * kv_dim + (size_t)kvh * HD;
+            for (int p = 0; p < PER; p++) o[h][p] = 0.0f;
+        }
+        for (int base = warp * KPW; base < n; base += NW * KPW) {
+            const bool valid = base + kj < n;
+            float sc[GMAX];
+#pragma unroll
+            for (int h = 0; h < GMAX; h++) sc[h] = 0.0f;
+            {
+                const float4* kr = reinterpret_cast<const float4*>(kbase + (size_t)min(base + kj, n - 1) * kv_dim);
                 float4 kv[8];
 #pragma unroll
-                for (int c = 0; c < 8; c++) kv[c] = __ldcg(reinterpret_cast<const float4*>(kr) + c * LPK + qd);
+                for (int c = 0; c < 8; c++) kv[c] = __ldcg(kr + c * LPK + qd);
 #pragma unroll
                 for (int c = 0; c < 8; c++)
 #pragma unroll
                     for (int h = 0; h < GMAX; h++) {
                         if (h >= grp) break;
                         const float4 q4 = reinterpret_cast<const float4*>(sq + h * HD)[c * LPK + qd];
-                        acc[h] = fmaf(q4.x, kv[c].x, acc[h]);
-                        acc[h] = fmaf(q4.y, kv[c].y, acc[h]);
-                        acc[h] = fmaf(q4.z, kv[c].z, acc[h]);
-                        acc[h] = fmaf(q4.w, kv[c].w, acc[h]);
+                        sc[h] = fmaf(q4.x, kv[c].x, sc[h]);
+                        sc[h] = fmaf(q4.y, kv[c].y, sc[h]);
+                        sc[h] = fmaf(q4.z, kv[c].z, sc[h]);
+                        sc[h] = fmaf(q4.w, kv[c].w, sc[h]);
                     }
             }
+            float vv[KPW][PER]; /* this lane's dims of the round's values */
 #pragma unroll
-            for (int h = 0; h < GMAX; h++)
+            for (int j = 0; j < KPW; j++) load_row<PER>(vbase + (size_t)min(base + j, n - 1) * kv_dim, vv[j]);
 #pragma unroll
-                for (int o = 1; o < LPK; o <<= 1) acc[h] += __shfl_xor_sync(0xffffffffu, acc[h], o);
-            if (kk < n) {
+            for (int h = 0; h < GMAX; h++) {
+                if (h >= grp) break;
 #pragma unroll
-                for (int h = 0; h < GMAX; h++) {
-                    if (h >= grp) break;
-                    float sc = __fmul_rn(acc[h], a.scale);
-                    if (a.softcap > 0.0f) sc = __fmul_rn(tanhf(__fmul_rn(sc, inv_cap)), a.softcap);
-                    if (qd == 0) sp[kk * grp + h] = sc;
-                    mloc[h] = fmaxf(mloc[h], sc);
+                for (int off = 1; off < LPK; off <<= 1) sc[h] += __shfl_xor_sync(0xffffffffu, sc[h], off);
+                float v = __fmul_rn(sc[h], a.scale);
+                if (a.softcap > 0.0f) v = __fmul_rn(tanhf(__fmul_rn(v, inv_cap)), a.softcap);
+                v = valid ? v : -INFINITY;
+                float mr = v; /* the round's max (key `base` is valid) */
+#pragma unroll
+                for (int off = LPK; off < 32; off <<= 1) mr = fmaxf(mr, __shfl_xor_sync(0xffffffffu, mr, off));
+                const float m_new = fmaxf(m_run[h], mr);
+                const float corr = __expf(m_run[h] - m_new); /* 0 on the first round */
+                const float pw = __expf(v - m_new);          /* 0 past the item's keys */
+                m_run[h] = m_new;
+                l_run[h] *= corr;
+#pragma unroll
+                for (int p = 0; p < PER; p++) o[h][p] *= corr;
+#pragma unroll
+                for (int j = 0; j < KPW; j++) {
+                    const float pj = __shfl_sync(0xffffffffu, pw, j * LPK);
+                    l_run[h] += pj;
+#pragma unroll
+                    for (int p = 0; p < PER; p++) o[h][p] = fmaf(pj, vv[j][p], o[h][p]);
                 }
             }
         }
         FL_STAMP(1);
 #pragma unroll
         for (int h = 0; h < GMAX; h++) {
-            const float m = fl_warp_max(mloc[h]);
-            if (lane == 0) sred[warp * GMAX + h] = m;
+            if (h >= grp) break;
+#pragma unroll
+            for (int p = 0; p < PER; p++) sacc[(warp * grp + h) * HD + lane * PER + p] = o[h][p];
+            if (lane == 0) {
+                sml[(warp * GMAX + h) * 2] = m_run[h];
+                sml[(warp * GMAX + h) * 2 + 1] = l_run[h];
+            }
         }
         consumer_sync();
         FL_STAMP(2);
-        if (threadIdx.x < grp) {
-            float M = -INFINITY;
-            for (int w = 0; w < NW; w++) M = fmaxf(M, sred[w * GMAX + threadIdx.x]);
-            s_M[threadIdx.x] = M;
-        }
-        consumer_sync();
-        FL_STAMP(3);
-        /* pass 2: weighted values; each warp forms the softmax weights
-         * exp(s - max) of its own keys and sums them */
-        float Mh[GMAX], lw[GMAX];
-#pragma unroll
-        for (int h = 0; h < GMAX; h++) {
-            Mh[h] = h < grp ? s_M[h] : 0.0f;
-            lw[h] = 0.0f;
-        }
-        const int d0 = lane * PER;
-        float o[GMAX][PER];
-#pragma unroll
-        for (int h = 0; h < GMAX; h++)
-#pragma unroll
-            for (int p = 0; p < PER; p++) o[h][p] = 0.0f;
-        for (int t0 = warp; t0 < n; t0 += VB * NW) {
-            float vv[VB][PER];
-#pragma unroll
-            for (int j = 0; j < VB; j++) {
-                const int t = t0 + j * NW;
-                if (t < n) load_row<PER>(a.v_cache + (size_t)(k0 + t) * kv_dim + (size_t)kvh * HD + d0, vv[j]);
-            }
-#pragma unroll
-            for (int j = 0; j < VB; j++) {
-                const int t = t0 + j * NW;
-                if (t < n) {
-#pragma unroll
-                    for (int h = 0; h < GMAX; h++) {
-                        if (h >= grp) break;
-                        const float pw = __expf(sp[t * grp + h] - Mh[h]);
-                        lw[h] += pw;
-#pragma unroll
-                        for (int p = 0; p < PER; p++) o[h][p] = fmaf(pw, vv[j][p], o[h][p]);
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int h = 0; h < GMAX; h++) {
-            if (h >= grp) break;
-#pragma unroll
-            for (int p = 0; p < PER; p++) sacc[(warp * grp + h) * HD + d0 + p] = o[h][p];
-            if (lane == 0) sred[warp * GMAX + h] = lw[h];
-        }
-        consumer_sync();
-        if (threadIdx.x < grp) {
-            float L = 0.0f;
-            for (int w = 0; w < NW; w++) L += sred[w * GMAX + threadIdx.x];
-            s_L[threadIdx.x] = L;
-        }
-        consumer_sync();
-        FL_STAMP(4);
+        /* the warps, in warp order, into the item's partial */
         float* part = a.part + (size_t)item * grp * (HD + 2);
         for (int i = threadIdx.x; i < grp * HD; i += NC) {
             const int h = i / HD, d = i % HD;
-            float O = 0.0f;
+            float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < NW; w++) O += sacc[(w * grp + h) * HD + d];
+            for (int w = 0; w < NW; w++) M = fmaxf(M, sml[(w * GMAX + h) * 2]);
+            float O = 0.0f, L = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; w++) {
+                const float mw = sml[(w * GMAX + h) * 2];
+                const float f = mw == -INFINITY ? 0.0f : __expf(mw - M);
+                O = fmaf(sacc[(w * grp + h) * HD + d], f, O);
+                L = fmaf(sml[(w * GMAX + h) * 2 + 1], f, L);
+            }
             part[h * (HD + 2) + 2 + d] = O;
             if (d == 0) {
-                part[h * (HD + 2)] = n > 0 ? s_M[h] : -INFINITY;
-                part[h * (HD + 2) + 1] = s_L[h];
+                part[h * (HD + 2)] = M;
+                part[h * (HD + 2) + 1] = L;
             }
         }
         consumer_sync(); /* the item's shared memory is reused by the next item */
-        FL_STAMP(5);
+        FL_STAMP(3);
     }
 #undef FL_STAMP
 }
