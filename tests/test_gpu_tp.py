@@ -1,7 +1,8 @@
-"""Tensor parallelism on 2 GPUs against the CPU restatement.
+"""Tensor parallelism on 2, 4 and 8 GPUs (as many as the box has) against
+the CPU restatement.
 
 Each family's GGUF is run by the oracle (single process, the reference's
-algorithm) and by two ranks of the token kernel, each holding its shard and
+algorithm) and by 2-8 ranks of the token kernel, each holding its shard and
 exchanging partial sums and the argmax over NVLink.  Same bars as the
 single-GPU parity tests: logits within 1e-3 + 1e-2·|ref| at every
 teacher-forced step, greedy tokens identical, the device loop equal to the
@@ -34,10 +35,10 @@ def _gpus() -> int:
     return torch.cuda.device_count()
 
 
-@pytest.mark.parametrize("name", ["small-tp", "tiny-gemma2"])
-def test_two_ranks_match_the_oracle(name, tmp_path):
-    if _gpus() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("name,ranks", [("small-tp", 2), ("tiny-gemma2", 2), ("small-tp", 4), ("small-tp", 8)])
+def test_ranks_match_the_oracle(name, ranks, tmp_path):
+    if _gpus() < ranks:
+        pytest.skip(f"needs {ranks} GPUs")
     img = ggufgen.build_model(ggufgen.SPECS[name])
     m = O.Model(img)
     prompt = ggufgen.prompt_ids(N_PROMPT, m.vocab, 1)
@@ -48,12 +49,14 @@ def test_two_ranks_match_the_oracle(name, tmp_path):
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={ranks}",
            "--master-addr=127.0.0.1", f"--master-port={port}", str(WORKER), "--model", name,
            "--ref", str(tmp_path / "ref.npz"), "--out", str(tmp_path)]
     subprocess.run(cmd, env=env, timeout=900, check=True)
-    r0, r1 = (np.load(tmp_path / f"rank{r}.npz") for r in range(2))
-    np.testing.assert_array_equal(r0["logits"], r1["logits"])
+    rs = [np.load(tmp_path / f"rank{r}.npz") for r in range(ranks)]
+    r0, r1 = rs[0], rs[-1]
+    for r in rs[1:]:
+        np.testing.assert_array_equal(r["logits"], r0["logits"])
     got = r0["logits"]
     err = np.abs(got - logs)
     bound = ATOL + RTOL * np.abs(logs)
