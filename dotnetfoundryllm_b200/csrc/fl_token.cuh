@@ -396,6 +396,16 @@ __device__ void phase_attn_combine(const FlAttnArgs& a, float* scr)
     for (int hq = blockIdx.x; hq < a.n_heads; hq += gridDim.x) {
         const int kvh = hq / grp, h = hq % grp;
         const float* base = a.part + ((size_t)kvh * S * grp + h) * (HD + 2);
+        /* this thread's outputs of its first PRE splits, loaded before the
+         * split weights exist (they overlap warp 0's work below) */
+        constexpr int PRE = 8;
+        const int d = threadIdx.x % HD, j = threadIdx.x / HD;
+        float ov_pre[PRE];
+#pragma unroll
+        for (int u = 0; u < PRE; u++) {
+            const int sp = j + u * TPO;
+            ov_pre[u] = sp < S ? __ldcg(base + sp * sstride + 2 + d) : 0.0f;
+        }
         if (warp == 0) {
             float M = -INFINITY;
             for (int s = lane; s < S; s += 32) M = fmaxf(M, __ldcg(base + s * sstride));
@@ -411,9 +421,13 @@ __device__ void phase_attn_combine(const FlAttnArgs& a, float* scr)
             if (lane == 0) w_s[S] = L;
         }
         consumer_sync();
-        const int d = threadIdx.x % HD, j = threadIdx.x / HD;
         float O = 0.0f;
-        for (int s = j; s < S; s += TPO) O = fmaf(__ldcg(base + s * sstride + 2 + d), w_s[s], O);
+#pragma unroll
+        for (int u = 0; u < PRE; u++) {
+            const int sp = j + u * TPO;
+            if (sp < S) O = fmaf(ov_pre[u], w_s[sp], O);
+        }
+        for (int sp = j + PRE * TPO; sp < S; sp += TPO) O = fmaf(__ldcg(base + sp * sstride + 2 + d), w_s[sp], O);
         red[j * HD + d] = O;
         consumer_sync();
         float amax = 0.0f;
