@@ -29,8 +29,6 @@ enum {
     FL_EPI_QKV = 2,     /* bias, RoPE, q store, K/V cache append */
     FL_EPI_GLU = 3,     /* act = silu|gelu(gate) * up over interleaved gate/up rows */
     FL_EPI_LOGITS = 4,  /* logits (+ final softcap) and greedy argmax */
-    FL_EPI_PARTIAL = 5, /* tensor parallel, row-parallel projection: push the partial
-                           output row to every rank's receive buffer (tp_out[q][row]) */
 };
 
 struct FlMvSeg {
@@ -75,9 +73,9 @@ struct FlMvArgs {
     int32_t* counter;
     int32_t* argmax_out;
     int* err;
-    /* tensor parallelism: PARTIAL epilogue → tp_out[q] = rank q's receive slot
-     * of this rank; LOGITS epilogue → tp_out[q] = rank q's full logits, rows
-     * offset by tp_row0 (the argmax index is global too).  tp_n = 0: off. */
+    /* tensor parallelism: the LOGITS epilogue writes tp_out[q] = rank q's
+     * full logits, rows offset by tp_row0 (the argmax index is global too).
+     * tp_n = 0: off. */
     int32_t tp_n, tp_row0;
     float* tp_out[FL_TP_MAX];
 };

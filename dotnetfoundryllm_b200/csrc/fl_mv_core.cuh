@@ -402,12 +402,6 @@ __device__ __forceinline__ void epilogue(const FlMvArgs& a, const FlMvSeg& sg, i
         }
         float m = fl_warp_max(fabsf(actv));
         if (lane == 0) atomicMax(reinterpret_cast<int*>(a.act_absmax), __float_as_int(m));
-    } else if constexpr (EPI == FL_EPI_PARTIAL) {
-        /* tensor parallel: this rank's share of the row, to every rank */
-        if (in_seg) {
-            const int row = sg.tile0 * 16 + row_local;
-            for (int q = 0; q < a.tp_n; q++) a.tp_out[q][row] = v;
-        }
     } else { /* FL_EPI_LOGITS */
         float val = v;
         int idx = 0x7fffffff;
@@ -461,7 +455,6 @@ __device__ __forceinline__ void epilogue_any(const FlMvArgs& a, const FlMvSeg& s
     case FL_EPI_RESID: epilogue<FL_EPI_RESID>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     case FL_EPI_QKV: epilogue<FL_EPI_QKV>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     case FL_EPI_GLU: epilogue<FL_EPI_GLU>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
-    case FL_EPI_PARTIAL: epilogue<FL_EPI_PARTIAL>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     default: epilogue<FL_EPI_LOGITS>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     }
 }
