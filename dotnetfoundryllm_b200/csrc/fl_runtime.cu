@@ -1036,9 +1036,12 @@ static int session_build(fl_session* s)
     return FL_OK;
 }
 
+static void forget_regions(const fl_session* s);
+
 extern "C" void fl_session_destroy(fl_session* s)
 {
     if (!s) return;
+    forget_regions(s);
     cudaSetDevice(s->m->d.device);
     if (s->st) cudaStreamSynchronize(s->st);
     if (s->graph) cudaGraphExecDestroy(s->graph);
@@ -1052,6 +1055,27 @@ extern "C" void fl_session_destroy(fl_session* s)
 }
 
 /* ── tensor parallelism: mapping the ranks' exchange regions ────────────── */
+
+/* Exchange regions handed out by this process: a rank whose peers live in
+ * the same process (one host thread per GPU) maps them directly with peer
+ * access, since CUDA IPC does not open a process's own handles. */
+struct LocalRegion {
+    uint8_t handle[FL_TP_HANDLE_BYTES];
+    int device;
+    uint8_t* ptr;
+    const fl_session* owner;
+};
+static std::mutex g_regions_mu;
+static std::vector<LocalRegion> g_regions;
+
+static void forget_regions(const fl_session* s)
+{
+    std::lock_guard<std::mutex> lk(g_regions_mu);
+    g_regions.erase(std::remove_if(g_regions.begin(), g_regions.end(),
+                                   [s](const LocalRegion& r) { return r.owner == s; }),
+                    g_regions.end());
+}
+
 extern "C" int fl_session_tp_handle(fl_session* s, void* handle)
 {
     if (!s || !handle) return fail(FL_ERR_ARG, "null argument");
@@ -1061,6 +1085,15 @@ extern "C" int fl_session_tp_handle(fl_session* s, void* handle)
     CK(cudaIpcGetMemHandle(&h, s->xchg));
     static_assert(sizeof(cudaIpcMemHandle_t) == FL_TP_HANDLE_BYTES, "IPC handle size");
     memcpy(handle, &h, sizeof h);
+    LocalRegion r;
+    memcpy(r.handle, &h, sizeof h);
+    r.device = s->m->d.device;
+    r.ptr = s->xchg;
+    r.owner = s;
+    std::lock_guard<std::mutex> lk(g_regions_mu);
+    for (const LocalRegion& e : g_regions)
+        if (e.owner == s) return FL_OK;
+    g_regions.push_back(r);
     return FL_OK;
 }
 
@@ -1076,8 +1109,30 @@ extern "C" int fl_session_tp_connect(fl_session* s, const void* handles)
             s->tp_peer[q] = s->xchg;
             continue;
         }
+        const uint8_t* hq = static_cast<const uint8_t*>(handles) + (size_t)q * FL_TP_HANDLE_BYTES;
+        LocalRegion local = {};
+        bool is_local = false;
+        {
+            std::lock_guard<std::mutex> lk(g_regions_mu);
+            for (const LocalRegion& e : g_regions)
+                if (!memcmp(e.handle, hq, FL_TP_HANDLE_BYTES)) {
+                    local = e;
+                    is_local = true;
+                    break;
+                }
+        }
+        if (is_local) { /* a peer in this process: its pointer, with peer access */
+            if (local.device != m->d.device) {
+                cudaError_t pe = cudaDeviceEnablePeerAccess(local.device, 0);
+                if (pe == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+                else if (pe != cudaSuccess)
+                    return fail(FL_ERR_CUDA, "peer access to device %d: %s", local.device, cudaGetErrorString(pe));
+            }
+            s->tp_peer[q] = local.ptr;
+            continue;
+        }
         cudaIpcMemHandle_t h;
-        memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)q * FL_TP_HANDLE_BYTES, sizeof h);
+        memcpy(&h, hq, sizeof h);
         void* p = nullptr;
         cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
         if (e != cudaSuccess) return fail(FL_ERR_CUDA, "mapping rank %d's exchange region: %s", q, cudaGetErrorString(e));

@@ -73,3 +73,59 @@ def test_ranks_match_the_oracle(name, ranks, tmp_path):
     err = np.abs(r0["pf_logits"] - logs)
     worst = np.unravel_index(np.argmax(err - bound), err.shape)
     assert (err <= bound).all(), f"{name} prefill: step {worst[0]} id {worst[1]}: {r0['pf_logits'][worst]} vs {logs[worst]}"
+
+
+def test_two_ranks_in_one_process(tmp_path):
+    """A host that keeps every rank in one process (the C# engine), one thread
+    per GPU: the exchange regions are mapped with peer access instead of CUDA
+    IPC.  Teacher-forced logits against the oracle, identical on both ranks."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    import threading
+
+    from dotnetfoundryllm_b200 import loader, runtime
+    name = "small-tp"
+    img = ggufgen.build_model(ggufgen.SPECS[name])
+    m = O.Model(img)
+    prompt = ggufgen.prompt_ids(24, m.vocab, 2)
+    toks, logs = m.generate_greedy(prompt, 16, collect_logits=True)
+    m.close()
+    models = [loader.load(img, device=r, tp_rank=r, tp_size=2) for r in range(2)]
+    fwds = [runtime.CudaForwardPass(mo) for mo in models]
+    handles = [f.tp_handle() for f in fwds]
+    for f in fwds:
+        f.tp_connect(handles)
+    feed = [int(t) for t in prompt] + [int(t) for t in toks[:-1]]
+    got = [[], []]
+    errors = []
+    gate = threading.Barrier(2)
+
+    def run(r):
+        try:
+            kv = object()
+            for pos, tok in enumerate(feed):
+                gate.wait()
+                want = pos >= len(prompt) - 1
+                fwds[r].forward(tok, pos, kv, want_logits=want)
+                if want:
+                    got[r].append(fwds[r].logits.copy())
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+            gate.abort()
+
+    threads = [threading.Thread(target=run, args=(r,)) for r in range(2)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=600)
+    try:
+        assert not errors, errors
+        a, b = np.stack(got[0]), np.stack(got[1])
+        np.testing.assert_array_equal(a, b)
+        err = np.abs(a - logs)
+        assert (err <= ATOL + RTOL * np.abs(logs)).all()
+    finally:
+        for f in fwds:
+            f.close()
+        for mo in models:
+            mo.close()
