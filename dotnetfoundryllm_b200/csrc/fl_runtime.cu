@@ -1122,12 +1122,11 @@ extern "C" int fl_session_tp_connect(fl_session* s, const void* handles)
                 }
         }
         if (is_local) { /* a peer in this process: its pointer, with peer access */
-            if (local.device != m->d.device) {
-                cudaError_t pe = cudaDeviceEnablePeerAccess(local.device, 0);
-                if (pe == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
-                else if (pe != cudaSuccess)
-                    return fail(FL_ERR_CUDA, "peer access to device %d: %s", local.device, cudaGetErrorString(pe));
-            }
+            if (local.device == m->d.device) return fail(FL_ERR_ARG, "ranks %d and %d share device %d", m->rank, q, local.device);
+            cudaError_t pe = cudaDeviceEnablePeerAccess(local.device, 0);
+            if (pe == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+            else if (pe != cudaSuccess)
+                return fail(FL_ERR_CUDA, "peer access to device %d: %s", local.device, cudaGetErrorString(pe));
             s->tp_peer[q] = local.ptr;
             continue;
         }
@@ -1138,6 +1137,12 @@ extern "C" int fl_session_tp_connect(fl_session* s, const void* handles)
         if (e != cudaSuccess) return fail(FL_ERR_CUDA, "mapping rank %d's exchange region: %s", q, cudaGetErrorString(e));
         s->tp_opened[q] = p;
         s->tp_peer[q] = static_cast<uint8_t*>(p);
+        /* The ranks' kernels wait on one another, so each needs a GPU of its
+         * own: two on one device are not guaranteed to be resident together. */
+        cudaPointerAttributes at;
+        if (cudaPointerGetAttributes(&at, p) == cudaSuccess && at.device == m->d.device)
+            return fail(FL_ERR_ARG, "ranks %d and %d share device %d", m->rank, q, at.device);
+        cudaGetLastError();
     }
     return session_build(s);
 }

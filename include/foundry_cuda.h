@@ -116,7 +116,9 @@ int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch, int32_t k
  * NVLink inside the token kernel.  Before its first step a tensor-parallel
  * session must be connected: every rank gets its FL_TP_HANDLE_BYTES handle,
  * the caller gathers the handles of all ranks in rank order (any host-side
- * channel) and passes the array to every rank's fl_session_tp_connect.  All
+ * channel) and passes the array to every rank's fl_session_tp_connect.
+ * Ranks in one process are mapped with peer access, others with CUDA IPC;
+ * each rank needs a device of its own (FL_ERR_ARG otherwise).  All
  * ranks must then run the same calls (same tokens and positions) in step;
  * a rank that stops makes the others' next step fail with FL_ERR_TIMEOUT
  * after ~2 s.  Logits (fl_forward) and argmax are the full-vocabulary ones

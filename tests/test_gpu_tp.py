@@ -129,3 +129,23 @@ def test_two_ranks_in_one_process(tmp_path):
             f.close()
         for mo in models:
             mo.close()
+
+
+def test_two_ranks_on_one_device_are_refused():
+    """Ranks wait on one another inside their kernels, so two on one GPU are
+    refused at connect time, before any kernel runs."""
+    if _gpus() < 1:
+        pytest.skip("needs a GPU")
+    from dotnetfoundryllm_b200 import loader, runtime
+    img = ggufgen.build_model(ggufgen.SPECS["small-tp"])
+    models = [loader.load(img, device=0, tp_rank=r, tp_size=2) for r in range(2)]
+    fwds = [runtime.CudaForwardPass(mo) for mo in models]
+    try:
+        handles = [f.tp_handle() for f in fwds]
+        with pytest.raises(runtime.ArgumentError, match="share device"):
+            fwds[0].tp_connect(handles)
+    finally:
+        for f in fwds:
+            f.close()
+        for mo in models:
+            mo.close()
