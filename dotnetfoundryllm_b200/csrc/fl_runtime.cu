@@ -1122,6 +1122,10 @@ extern "C" int fl_session_tp_connect(fl_session* s, const void* handles)
                 }
         }
         if (is_local) { /* a peer in this process: its pointer, with peer access */
+            /* The ranks' kernels wait on one another, so each needs a GPU of
+             * its own: two on one device are not guaranteed to be resident
+             * together.  (A mapping from another process does not tell its
+             * owner's device, so that case rests on the caller.) */
             if (local.device == m->d.device) return fail(FL_ERR_ARG, "ranks %d and %d share device %d", m->rank, q, local.device);
             cudaError_t pe = cudaDeviceEnablePeerAccess(local.device, 0);
             if (pe == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
@@ -1137,12 +1141,6 @@ extern "C" int fl_session_tp_connect(fl_session* s, const void* handles)
         if (e != cudaSuccess) return fail(FL_ERR_CUDA, "mapping rank %d's exchange region: %s", q, cudaGetErrorString(e));
         s->tp_opened[q] = p;
         s->tp_peer[q] = static_cast<uint8_t*>(p);
-        /* The ranks' kernels wait on one another, so each needs a GPU of its
-         * own: two on one device are not guaranteed to be resident together. */
-        cudaPointerAttributes at;
-        if (cudaPointerGetAttributes(&at, p) == cudaSuccess && at.device == m->d.device)
-            return fail(FL_ERR_ARG, "ranks %d and %d share device %d", m->rank, q, at.device);
-        cudaGetLastError();
     }
     return session_build(s);
 }

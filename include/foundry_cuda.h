@@ -118,7 +118,8 @@ int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch, int32_t k
  * the caller gathers the handles of all ranks in rank order (any host-side
  * channel) and passes the array to every rank's fl_session_tp_connect.
  * Ranks in one process are mapped with peer access, others with CUDA IPC;
- * each rank needs a device of its own (FL_ERR_ARG otherwise).  All
+ * each rank needs a device of its own (ranks of one process that share one
+ * are refused with FL_ERR_ARG).  All
  * ranks must then run the same calls (same tokens and positions) in step;
  * a rank that stops makes the others' next step fail with FL_ERR_TIMEOUT
  * after ~2 s.  Logits (fl_forward) and argmax are the full-vocabulary ones
