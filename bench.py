@@ -449,10 +449,15 @@ def run_ours(args, ws, rank, local):
     result = None
     if rank == 0:
         cpu = {"tok_s": None, "threads": 0} if args.no_cpu_baseline else cpu_sample(img, pos_timed)
-        traffic = None
+        traffic, traffic_note = None, None
         tf = ROOT / "profiles" / "traffic.json"
         if tf.exists() and not args.layers and args.prompt == PROMPT:
-            traffic = json.loads(tf.read_text()).get(CONFIG)
+            tj = json.loads(tf.read_text())
+            traffic = tj.get(CONFIG)
+            if traffic is not None and tp:
+                # a rank streams its shard: the captured traffic/algorithmic ratio applied to it
+                traffic = int(step_bytes * tj["ratio"])
+                traffic_note = "per rank: the 1-GPU capture's traffic/algorithmic ratio x this rank's bytes"
         result = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -468,6 +473,7 @@ def run_ours(args, ws, rank, local):
                          "kernel": "fl_token_kernel (one persistent launch per token)",
                          "algorithmic_bytes_per_launch": step_bytes,
                          "peak_source": peaks["source"], "frac_of_nominal_8tbs": step_gbs / NOMINAL_HBM_GBS,
+                         **({"traffic_note": traffic_note} if traffic_note else {}),
                          "matvec_phase_gbs": mv_gbs, "matvec_phase_frac": mv_gbs / peaks["hbm_gbs"]},
             "cpu_baseline": {"value": cpu["tok_s"], "unit": "tok/s", "cores": cpu["threads"], "kind": "port",
                              "sample": "oracle (C restatement of the reference CPU path, F32 weights) on 2 of 32 "
