@@ -99,3 +99,26 @@ def test_loader_desc_matches_oracle_config():
         assert np.float32(d.attn_softcap) == np.float32(m.attn_softcap)
         assert np.float32(d.final_softcap) == np.float32(m.final_softcap)
         m.close()
+
+
+def _zero(t):
+    if t in (C.c_int32, C.c_uint64, C.c_int64, C.c_int):
+        return 0
+    if t is C.c_float:
+        return 0.0
+    return None
+
+
+@pytest.mark.parametrize("name,args", [(n, a) for n, r, a in N.PUBLIC_API
+                                       if r is C.c_int and n not in ("fl_dequant",)])
+def test_entry_points_reject_null_arguments_before_device_work(name, args):
+    """Every entry point that returns a status refuses null handles/pointers
+    with FL_ERR_ARG and a message (the reference's ArgumentNullException)."""
+    rc = getattr(N.cuda(), name)(*[_zero(t) for t in args])
+    assert rc == N.FL_ERR_ARG, (name, rc)
+    assert N.last_error() != ""
+
+
+def test_destroy_of_null_handles_is_a_no_op():
+    N.cuda().fl_model_destroy(None)
+    N.cuda().fl_session_destroy(None)
