@@ -453,11 +453,12 @@ def run_ours(args, ws, rank, local):
         tf = ROOT / "profiles" / "traffic.json"
         if tf.exists() and not args.layers and args.prompt == PROMPT:
             tj = json.loads(tf.read_text())
-            traffic = tj.get(CONFIG)
-            if traffic is not None and tp:
-                # a rank streams its shard: the captured traffic/algorithmic ratio applied to it
+            if CONFIG in tj:
+                # the captured launch's traffic/algorithmic ratio applied to this launch's bytes
+                # (a tensor-parallel rank's bytes are its shard)
                 traffic = int(step_bytes * tj["ratio"])
-                traffic_note = "per rank: the 1-GPU capture's traffic/algorithmic ratio x this rank's bytes"
+                traffic_note = ("ncu traffic/algorithmic ratio of the 4-layer capture x this launch's bytes"
+                                + (" (per rank)" if tp else ""))
         result = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
