@@ -27,6 +27,7 @@ FL_PROF_MATVEC, FL_PROF_ATTN, FL_PROF_OTHER, FL_PROF_STEP, FL_PROF_N = 0, 1, 2, 
 
 FL_TOPK_DEVICE_MAX_N = 262144
 FL_TP_HANDLE_BYTES = 64
+FL_TP_ALL = -1  # fl_model_desc.tp_rank of a group driven from one thread
 
 
 class FlModelDesc(C.Structure):
@@ -107,6 +108,7 @@ PUBLIC_API = [
                             C.POINTER(C.c_int32)]),
     ("fl_session_tp_handle", C.c_int, [C.c_void_p, C.c_void_p]),
     ("fl_session_tp_connect", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("fl_init", C.c_int, [C.c_int32, C.POINTER(C.c_int32)]),
     ("fl_session_destroy", None, [C.c_void_p]),
     ("fl_dequant", C.c_int, [C.c_int32, C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64]),
     ("fl_matvec", C.c_int, [C.c_int32, C.c_void_p, C.c_uint64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),

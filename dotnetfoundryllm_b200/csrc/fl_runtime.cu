@@ -10,6 +10,9 @@
  */
 #include <algorithm>
 #include <cmath>
+#include <condition_variable>
+#include <functional>
+#include <thread>
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
@@ -93,6 +96,10 @@ struct fl_model {
     bool finalized = false;
     std::vector<void*> allocs;
     double weight_bytes = 0;
+    /* a tensor-parallel group driven from one host thread (tp_rank FL_TP_ALL):
+     * one rank model per device; the fields above stay unused */
+    bool group = false;
+    std::vector<fl_model*> ranks;
 };
 
 struct fl_session {
@@ -171,7 +178,18 @@ struct fl_session {
     void* lt_ws = nullptr;
     size_t lt_ws_bytes = 0;
     std::vector<void*> allocs;
+    /* a group session: one connected rank session per device and the worker
+     * threads that run ranks 1.. while the caller runs rank 0 */
+    bool group = false;
+    std::vector<fl_session*> ranks;
+    struct RankPool* pool = nullptr;
 };
+
+/* ── tensor-parallel groups (defined at the end of this file) ───────────── */
+static int group_model_create(const fl_model_desc& d, fl_model** out);
+static int group_session_create(fl_model* g, int32_t max_ctx, int32_t max_batch, int32_t kv_dtype, fl_session** out);
+static void group_session_destroy(fl_session* s);
+static int run_ranks(fl_session* s, const std::function<int(int)>& f);
 
 enum { ST_TOKEN = 0, ST_POS = 1, ST_ARGMAX = 2, ST_STEP = 3, ST_ERR = 4, ST_HEADCNT = 5, ST_N = 8 };
 
@@ -216,6 +234,7 @@ extern "C" int fl_model_create(const fl_model_desc* desc, fl_model** out)
     if (!desc || !out) return fail(FL_ERR_ARG, "null argument");
     if (desc->struct_size != (int32_t)sizeof(fl_model_desc)) return fail(FL_ERR_ARG, "fl_model_desc size mismatch");
     const fl_model_desc& d = *desc;
+    if (d.tp_rank == FL_TP_ALL) return group_model_create(d, out);
     if (d.arch < FL_ARCH_LLAMA || d.arch > FL_ARCH_QWEN2) return fail(FL_ERR_UNSUPPORTED, "unknown arch %d", d.arch);
     /* LlamaForwardPass.cs:48-52 */
     if (d.n_kv_heads <= 0 || d.n_heads <= 0 || d.n_kv_heads > d.n_heads || d.n_heads % d.n_kv_heads != 0)
@@ -280,6 +299,11 @@ extern "C" int fl_model_create(const fl_model_desc* desc, fl_model** out)
 extern "C" void fl_model_destroy(fl_model* m)
 {
     if (!m) return;
+    if (m->group) {
+        for (fl_model* r : m->ranks) fl_model_destroy(r);
+        delete m;
+        return;
+    }
     cudaSetDevice(m->d.device);
     for (void* p : m->allocs) cudaFree(p);
     delete m;
@@ -387,6 +411,13 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
                                const void* bytes, uint64_t nbytes)
 {
     if (!m || !name || !dims || ndims <= 0 || ndims > 4 || (!bytes && nbytes)) return fail(FL_ERR_ARG, "null argument");
+    if (m->group) { /* every rank takes its shard of the same bytes */
+        for (fl_model* r : m->ranks) {
+            int rc = fl_model_upload(r, name, type, dims, ndims, bytes, nbytes);
+            if (rc) return rc;
+        }
+        return FL_OK;
+    }
     if (m->finalized) return fail(FL_ERR_STATE, "model already finalized");
     if (!block_elems(type)) return fail(FL_ERR_UNSUPPORTED, "Tensor type %d is not supported for dequantization.", type);
     if (cudaSetDevice(m->d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
@@ -513,6 +544,14 @@ extern "C" int fl_model_upload(fl_model* m, const char* name, int32_t type, cons
 extern "C" int fl_model_finalize(fl_model* m)
 {
     if (!m) return fail(FL_ERR_ARG, "null model");
+    if (m->group) {
+        for (fl_model* r : m->ranks) {
+            int rc = fl_model_finalize(r);
+            if (rc) return rc;
+        }
+        m->finalized = true;
+        return FL_OK;
+    }
     if (m->finalized) return FL_OK;
     if (cudaSetDevice(m->d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
     const fl_model_desc& d = m->d;
@@ -555,6 +594,8 @@ extern "C" int fl_model_weight_bytes(fl_model* m, double* bytes)
 {
     if (!m || !bytes) return fail(FL_ERR_ARG, "null argument");
     *bytes = m->weight_bytes;
+    if (m->group) /* all ranks' shards */
+        for (fl_model* r : m->ranks) *bytes += r->weight_bytes;
     return FL_OK;
 }
 
@@ -822,6 +863,7 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
         int rc = fl_model_finalize(m);
         if (rc) return rc;
     }
+    if (m->group) return group_session_create(m, max_ctx, max_batch, kv_dtype, out);
     if (kv_dtype != FL_KV_F32) return fail(FL_ERR_UNSUPPORTED, "kv dtype %d", kv_dtype);
     if (max_batch < 1) max_batch = 1;
     if (max_batch > 1 && m->T > 1) return fail(FL_ERR_UNSUPPORTED, "batched sessions run on one GPU (tp_size 1)");
@@ -1041,6 +1083,7 @@ static void forget_regions(const fl_session* s);
 extern "C" void fl_session_destroy(fl_session* s)
 {
     if (!s) return;
+    if (s->group) return group_session_destroy(s);
     forget_regions(s);
     cudaSetDevice(s->m->d.device);
     if (s->st) cudaStreamSynchronize(s->st);
@@ -1079,6 +1122,7 @@ static void forget_regions(const fl_session* s)
 extern "C" int fl_session_tp_handle(fl_session* s, void* handle)
 {
     if (!s || !handle) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) return fail(FL_ERR_STATE, "a group session connects its ranks itself");
     if (s->m->T == 1) return fail(FL_ERR_STATE, "the model is not tensor-parallel");
     if (cudaSetDevice(s->m->d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
     cudaIpcMemHandle_t h;
@@ -1100,6 +1144,7 @@ extern "C" int fl_session_tp_handle(fl_session* s, void* handle)
 extern "C" int fl_session_tp_connect(fl_session* s, const void* handles)
 {
     if (!s || !handles) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) return fail(FL_ERR_STATE, "a group session connects its ranks itself");
     fl_model* m = s->m;
     if (m->T == 1) return fail(FL_ERR_STATE, "the model is not tensor-parallel");
     if (s->built) return fail(FL_ERR_STATE, "the session is already connected");
@@ -1148,6 +1193,13 @@ extern "C" int fl_session_tp_connect(fl_session* s, const void* handles)
 extern "C" int fl_session_reset(fl_session* s, int32_t seq_slot)
 {
     if (!s) return fail(FL_ERR_ARG, "null session");
+    if (s->group) {
+        for (fl_session* r : s->ranks) {
+            int rc = fl_session_reset(r, seq_slot);
+            if (rc) return rc;
+        }
+        return FL_OK;
+    }
     if (seq_slot < 0 || seq_slot >= s->n_slots)
         return fail(FL_ERR_ARG, "sequence slot %d outside [0, %d)", seq_slot, s->n_slots);
     if (seq_slot == 0) s->cur_len = 0;
@@ -1158,6 +1210,7 @@ extern "C" int fl_session_reset(fl_session* s, int32_t seq_slot)
 extern "C" int fl_session_launches_per_step(fl_session* s, int32_t* n)
 {
     if (!s || !n) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) return fl_session_launches_per_step(s->ranks[0], n);
     *n = s->launches;
     return FL_OK;
 }
@@ -1183,9 +1236,12 @@ static int set_state(fl_session* s, int token, int pos)
     return FL_OK;
 }
 
-extern "C" int fl_forward(fl_session* s, int32_t token, int32_t position, float* logits, int32_t* argmax)
+/* The checks of one token step (LlamaForwardPass.cs:85-93, KvCache.Append). A
+ * group runs them on rank 0 before any rank launches: the ranks' states are
+ * identical, and a rank that refused while the others launched would leave
+ * them waiting for its exchanges. */
+static int check_forward(const fl_session* s, int32_t token, int32_t position)
 {
-    if (!s) return fail(FL_ERR_ARG, "null session");
     if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     const fl_model_desc& d = s->m->d;
     if ((uint32_t)token >= (uint32_t)d.vocab)
@@ -1194,8 +1250,24 @@ extern "C" int fl_forward(fl_session* s, int32_t token, int32_t position, float*
         return fail(FL_ERR_ARG, "position %d is outside the KV cache [0, %d)", position, s->max_ctx);
     if (position > s->cur_len)
         return fail(FL_ERR_ARG, "position %d skips cached positions (cache holds %d)", position, s->cur_len);
+    return FL_OK;
+}
+
+extern "C" int fl_forward(fl_session* s, int32_t token, int32_t position, float* logits, int32_t* argmax)
+{
+    if (!s) return fail(FL_ERR_ARG, "null session");
+    if (s->group) {
+        int rc = check_forward(s->ranks[0], token, position);
+        if (rc) return rc;
+        return run_ranks(s, [&](int r) {
+            return fl_forward(s->ranks[r], token, position, r ? nullptr : logits, r ? nullptr : argmax);
+        });
+    }
+    int rc = check_forward(s, token, position);
+    if (rc) return rc;
+    const fl_model_desc& d = s->m->d;
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
-    int rc = set_state(s, token, position);
+    rc = set_state(s, token, position);
     if (rc) return rc;
     CK(cudaGraphLaunch(s->graph, s->st));
     if (logits) CK(cudaMemcpyAsync(logits, s->logits, (size_t)d.vocab * 4, cudaMemcpyDeviceToHost, s->st));
@@ -1208,7 +1280,7 @@ extern "C" int fl_forward(fl_session* s, int32_t token, int32_t position, float*
     return FL_OK;
 }
 
-static int run_steps(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, float* ms)
+static int check_steps(const fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps)
 {
     if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     const fl_model_desc& d = s->m->d;
@@ -1216,8 +1288,16 @@ static int run_steps(fl_session* s, int32_t token, int32_t start_pos, int32_t n_
     if (start_pos < 0 || start_pos > s->cur_len || n_steps < 0 || start_pos + n_steps > s->max_ctx)
         return fail(FL_ERR_ARG, "steps [%d, %d) do not fit the KV cache (holds %d of %d)", start_pos,
                     start_pos + n_steps, s->cur_len, s->max_ctx);
+    return FL_OK;
+}
+
+static int run_steps(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, float* ms)
+{
+    int rc = check_steps(s, token, start_pos, n_steps);
+    if (rc) return rc;
+    const fl_model_desc& d = s->m->d;
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
-    int rc = set_state(s, token, start_pos);
+    rc = set_state(s, token, start_pos);
     if (rc) return rc;
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (ms) {
@@ -1242,6 +1322,13 @@ static int run_steps(fl_session* s, int32_t token, int32_t start_pos, int32_t n_
 extern "C" int fl_decode_greedy(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, int32_t* out_tokens)
 {
     if (!s) return fail(FL_ERR_ARG, "null session");
+    if (s->group) {
+        int rc = check_steps(s->ranks[0], token, start_pos, n_steps);
+        if (rc) return rc;
+        return run_ranks(s, [&](int r) {
+            return fl_decode_greedy(s->ranks[r], token, start_pos, n_steps, r ? nullptr : out_tokens);
+        });
+    }
     int rc = run_steps(s, token, start_pos, n_steps, nullptr);
     if (rc) return rc;
     if (out_tokens && n_steps > 0) CK(cudaMemcpy(out_tokens, s->out_tokens, (size_t)n_steps * 4, cudaMemcpyDeviceToHost));
@@ -1251,6 +1338,15 @@ extern "C" int fl_decode_greedy(fl_session* s, int32_t token, int32_t start_pos,
 extern "C" int fl_time_decode(fl_session* s, int32_t token, int32_t start_pos, int32_t n_steps, float* ms)
 {
     if (!s || !ms) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) { /* the slowest rank's time */
+        int rc = check_steps(s->ranks[0], token, start_pos, n_steps);
+        if (rc) return rc;
+        std::vector<float> t(s->ranks.size(), 0.0f);
+        rc = run_ranks(s, [&](int r) { return fl_time_decode(s->ranks[r], token, start_pos, n_steps, &t[(size_t)r]); });
+        if (rc) return rc;
+        *ms = *std::max_element(t.begin(), t.end());
+        return FL_OK;
+    }
     return run_steps(s, token, start_pos, n_steps, ms);
 }
 
@@ -1259,6 +1355,7 @@ extern "C" int fl_time_decode(fl_session* s, int32_t token, int32_t start_pos, i
 extern "C" int fl_profile_step(fl_session* s, int32_t token, int32_t position, double* ms, double* bytes,
                                int32_t* launches)
 {
+    if (s && s->group) return fail(FL_ERR_UNSUPPORTED, "measurement hook of one rank: not available on a group session");
     if (s && !s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     if (!s || !ms || !bytes) return fail(FL_ERR_ARG, "null argument");
     const fl_model_desc& d = s->m->d;
@@ -1292,6 +1389,7 @@ extern "C" int fl_profile_step(fl_session* s, int32_t token, int32_t position, d
 extern "C" int fl_topk(fl_session* s, int32_t k, int32_t* ids, float* vals, float* threshold)
 {
     if (!s || !ids || !vals) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) return fl_topk(s->ranks[0], k, ids, vals, threshold); /* every rank holds the full logits */
     if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     const fl_model_desc& d = s->m->d;
     if (k < 1 || k > d.vocab) return fail(FL_ERR_ARG, "k must be in [1, %d]", d.vocab);
@@ -1308,6 +1406,7 @@ extern "C" int fl_sample(fl_session* s, const fl_sampler_desc* sd, const int32_t
                          float u, int32_t* token)
 {
     if (!s || !sd || !token || (!generated && n_generated > 0)) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) return fl_sample(s->ranks[0], sd, generated, n_generated, u, token);
     if (sd->struct_size != (int32_t)sizeof(fl_sampler_desc)) return fail(FL_ERR_ARG, "fl_sampler_desc size mismatch");
     if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     /* SamplerPipeline's constructor checks (SamplerPipeline.cs:47-48) */
@@ -1594,12 +1693,10 @@ static int pf_chunk(fl_session* s, int slot, const int32_t* tokens, int n, int s
  * the session stream and their elapsed time is returned (benchmark hook). */
 static int& slot_length(fl_session* s, int slot) { return slot == 0 ? s->cur_len : s->slot_len[(size_t)slot]; }
 
-static int prefill_impl(fl_session* s, int slot, const int32_t* tokens, int32_t n, int32_t start_pos, float* ms)
+static int check_prefill(fl_session* s, int slot, const int32_t* tokens, int32_t n, int32_t start_pos)
 {
-    if (!s || (!tokens && n)) return fail(FL_ERR_ARG, "null argument");
     if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
-    fl_model* m = s->m;
-    const fl_model_desc& d = m->d;
+    const fl_model_desc& d = s->m->d;
     if (slot < 0 || slot >= s->n_slots) return fail(FL_ERR_ARG, "sequence slot %d outside [0, %d)", slot, s->n_slots);
     const int have = slot_length(s, slot);
     if (n < 0 || start_pos < 0 || start_pos > have || start_pos + n > s->max_ctx)
@@ -1608,9 +1705,37 @@ static int prefill_impl(fl_session* s, int slot, const int32_t* tokens, int32_t 
     for (int i = 0; i < n; i++)
         if ((uint32_t)tokens[i] >= (uint32_t)d.vocab)
             return fail(FL_ERR_ARG, "Token id %d is outside the valid vocabulary range [0, %d].", tokens[i], d.vocab - 1);
-    if (n == 0) return FL_OK;
+    return FL_OK;
+}
+
+static int prefill_impl(fl_session* s, int slot, const int32_t* tokens, int32_t n, int32_t start_pos, float* ms)
+{
+    if (!s || (!tokens && n)) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) {
+        if (slot != 0) return fail(FL_ERR_UNSUPPORTED, "batched decode runs on one GPU (tp_size 1)");
+        int rc = check_prefill(s->ranks[0], 0, tokens, n, start_pos);
+        if (rc || n == 0) return rc;
+        /* every rank's prompt buffers first: a rank that failed to allocate
+         * while the others ran would leave them waiting for its exchanges */
+        rc = run_ranks(s, [&](int r) {
+            fl_session* rs = s->ranks[(size_t)r];
+            if (rs->pf_cap) return (int)FL_OK;
+            if (cudaSetDevice(rs->m->d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
+            return pf_alloc(rs);
+        });
+        if (rc) return rc;
+        std::vector<float> t(s->ranks.size(), 0.0f);
+        rc = run_ranks(s, [&](int r) {
+            return prefill_impl(s->ranks[(size_t)r], 0, tokens, n, start_pos, ms ? &t[(size_t)r] : nullptr);
+        });
+        if (!rc && ms) *ms = *std::max_element(t.begin(), t.end());
+        return rc;
+    }
+    int rc = check_prefill(s, slot, tokens, n, start_pos);
+    if (rc || n == 0) return rc;
+    fl_model* m = s->m;
+    const fl_model_desc& d = m->d;
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
-    int rc = FL_OK;
     if (!s->pf_cap && (rc = pf_alloc(s))) return rc;
     if (m->T > 1) CK(cudaMemcpy(&s->pf_epoch, s->tp_epoch, 4, cudaMemcpyDeviceToHost)); /* continues the token loop's */
     cudaEvent_t ev[2] = {nullptr, nullptr};
@@ -1719,6 +1844,7 @@ extern "C" int fl_forward_batch(fl_session* s, int32_t B, const int32_t* tokens,
                                 const int32_t* slots, float* logits, int32_t* argmax)
 {
     if (!s || !tokens || !positions || !slots) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) return fail(FL_ERR_UNSUPPORTED, "batched decode runs on one GPU (tp_size 1)");
     if (!s->built) return fail(FL_ERR_STATE, "tensor-parallel session not connected (fl_session_tp_connect)");
     fl_model* m = s->m;
     const fl_model_desc& d = m->d;
@@ -1929,6 +2055,7 @@ extern "C" int fl_matvec(int32_t type, const void* w, uint64_t nbytes, int32_t r
 extern "C" int fl_session_cta_done_ms(fl_session* s, double* out, int64_t cap, int32_t* grid)
 {
     if (!s || !out || !grid) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) return fail(FL_ERR_UNSUPPORTED, "measurement hook of one rank: not available on a group session");
     const int G = s->tk_grid;
     std::vector<uint64_t> ts((size_t)s->n_phases + 1), done((size_t)s->n_phases * G);
     CK(cudaMemcpy(ts.data(), s->timestamps, ts.size() * 8, cudaMemcpyDeviceToHost));
@@ -1945,6 +2072,7 @@ extern "C" int fl_session_cta_done_ms(fl_session* s, double* out, int64_t cap, i
 extern "C" int fl_session_detail(fl_session* s, uint64_t* out, int64_t cap, int32_t* n_phases, int32_t* n_warps)
 {
     if (!s || !out || !n_phases || !n_warps) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) return fail(FL_ERR_UNSUPPORTED, "measurement hook of one rank: not available on a group session");
     const size_t nd = (size_t)s->n_phases * (FL_TK_WARPS * 4 + 1), nt = (size_t)s->n_phases + 1;
     if ((int64_t)(nd + nt) > cap) return fail(FL_ERR_ARG, "need %zu entries", nd + nt);
     CK(cudaMemcpy(out, s->timestamps, nt * 8, cudaMemcpyDeviceToHost));
@@ -1957,9 +2085,201 @@ extern "C" int fl_session_detail(fl_session* s, uint64_t* out, int64_t cap, int3
 extern "C" int fl_session_phase_ms(fl_session* s, double* out, int32_t cap, int32_t* n)
 {
     if (!s || !out || !n) return fail(FL_ERR_ARG, "null argument");
+    if (s->group) return fail(FL_ERR_UNSUPPORTED, "measurement hook of one rank: not available on a group session");
     std::vector<uint64_t> ts((size_t)s->n_phases + 1);
     CK(cudaMemcpy(ts.data(), s->timestamps, ts.size() * 8, cudaMemcpyDeviceToHost));
     *n = s->n_phases;
     for (int p = 0; p < s->n_phases && p < cap; p++) out[p] = (double)(ts[(size_t)p + 1] - ts[(size_t)p]) * 1e-6;
     return FL_OK;
+}
+
+/* ── tensor parallelism driven from one host thread ─────────────────────── */
+
+/* The reference calls Forward from one thread per request
+ * (LlamaForwardPass.cs:29).  A group model (tp_rank FL_TP_ALL) keeps one rank
+ * model per device, and its sessions run every call on all ranks at once:
+ * rank 0 on the calling thread, the others on the session's worker threads.
+ * The ranks' kernels wait on one another inside each step, so every rank's
+ * launches are issued and waited for concurrently. */
+
+static std::mutex g_layout_mu;
+static int g_layout_tp = 0;
+static int g_layout_dev[FL_TP_MAX];
+
+extern "C" int fl_init(int32_t tp, const int32_t* devices)
+{
+    if (tp < 1 || tp > FL_TP_MAX || (tp & (tp - 1))) return fail(FL_ERR_UNSUPPORTED, "tp %d (1, 2, 4 or 8)", tp);
+    int dev[FL_TP_MAX];
+    for (int r = 0; r < tp; r++) {
+        dev[r] = devices ? devices[r] : r;
+        if (dev[r] < 0) return fail(FL_ERR_ARG, "device %d", dev[r]);
+        for (int q = 0; q < r; q++)
+            if (dev[q] == dev[r]) return fail(FL_ERR_ARG, "ranks %d and %d share device %d", q, r, dev[r]);
+    }
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(FL_ERR_CUDA, "no CUDA device");
+    }
+    for (int r = 0; r < tp; r++)
+        if (dev[r] >= n) return fail(FL_ERR_ARG, "device %d outside [0, %d)", dev[r], n);
+    for (int r = 0; r < tp; r++)
+        for (int q = 0; q < tp; q++) {
+            int can = 0;
+            if (q != r && (cudaDeviceCanAccessPeer(&can, dev[r], dev[q]) != cudaSuccess || !can))
+                return fail(FL_ERR_UNSUPPORTED, "device %d cannot access device %d's memory", dev[r], dev[q]);
+        }
+    std::lock_guard<std::mutex> lk(g_layout_mu);
+    g_layout_tp = tp;
+    for (int r = 0; r < tp; r++) g_layout_dev[r] = dev[r];
+    return FL_OK;
+}
+
+static int group_model_create(const fl_model_desc& d, fl_model** out)
+{
+    const int T = d.tp_size;
+    if (T < 2 || T > FL_TP_MAX || (T & (T - 1))) return fail(FL_ERR_UNSUPPORTED, "tp_size %d for a group (2, 4 or 8)", T);
+    int dev[FL_TP_MAX];
+    {
+        std::lock_guard<std::mutex> lk(g_layout_mu);
+        if (g_layout_tp && g_layout_tp != T)
+            return fail(FL_ERR_STATE, "fl_init set %d ranks, the model asks for %d", g_layout_tp, T);
+        for (int r = 0; r < T; r++) dev[r] = g_layout_tp ? g_layout_dev[r] : r;
+    }
+    fl_model* g = new fl_model();
+    g->d = d;
+    g->T = T;
+    g->group = true;
+    for (int r = 0; r < T; r++) {
+        fl_model_desc dr = d;
+        dr.device = dev[r];
+        dr.tp_rank = r;
+        fl_model* m = nullptr;
+        int rc = fl_model_create(&dr, &m);
+        if (rc) {
+            std::string msg = g_err;
+            fl_model_destroy(g);
+            return fail(rc, "rank %d: %s", r, msg.c_str());
+        }
+        g->ranks.push_back(m);
+    }
+    *out = g;
+    return FL_OK;
+}
+
+struct RankPool {
+    std::vector<std::thread> th;
+    std::mutex mu;
+    std::condition_variable go, done;
+    const std::function<int(int)>* job = nullptr;
+    uint64_t gen = 0;
+    int pending = 0;
+    bool stop = false;
+    std::vector<int> rc;
+    std::vector<std::string> msg;
+};
+
+static void pool_worker(RankPool* p, int r)
+{
+    uint64_t seen = 0;
+    for (;;) {
+        const std::function<int(int)>* job = nullptr;
+        {
+            std::unique_lock<std::mutex> lk(p->mu);
+            p->go.wait(lk, [&] { return p->stop || p->gen != seen; });
+            if (p->stop) return;
+            seen = p->gen;
+            job = p->job;
+        }
+        const int rc = (*job)(r);
+        std::lock_guard<std::mutex> lk(p->mu);
+        p->rc[(size_t)r] = rc;
+        if (rc) p->msg[(size_t)r] = g_err;
+        if (--p->pending == 0) p->done.notify_one();
+    }
+}
+
+static void pool_stop(RankPool* p)
+{
+    {
+        std::lock_guard<std::mutex> lk(p->mu);
+        p->stop = true;
+    }
+    p->go.notify_all();
+    for (std::thread& t : p->th) t.join();
+    delete p;
+}
+
+/* f(r) on every rank at once; the first failing rank's status and message. */
+static int run_ranks(fl_session* s, const std::function<int(int)>& f)
+{
+    RankPool* p = s->pool;
+    const int T = (int)s->ranks.size();
+    {
+        std::lock_guard<std::mutex> lk(p->mu);
+        p->job = &f;
+        p->pending = T - 1;
+        for (int r = 0; r < T; r++) {
+            p->rc[(size_t)r] = 0;
+            p->msg[(size_t)r].clear();
+        }
+        p->gen++;
+    }
+    p->go.notify_all();
+    const int rc0 = f(0);
+    const std::string msg0 = rc0 ? g_err : std::string();
+    {
+        std::unique_lock<std::mutex> lk(p->mu);
+        p->done.wait(lk, [&] { return p->pending == 0; });
+    }
+    if (rc0) return fail(rc0, "rank 0: %s", msg0.c_str());
+    for (int r = 1; r < T; r++)
+        if (p->rc[(size_t)r]) return fail(p->rc[(size_t)r], "rank %d: %s", r, p->msg[(size_t)r].c_str());
+    return FL_OK;
+}
+
+static int group_session_create(fl_model* g, int32_t max_ctx, int32_t max_batch, int32_t kv_dtype, fl_session** out)
+{
+    if (max_batch > 1) return fail(FL_ERR_UNSUPPORTED, "batched sessions run on one GPU (tp_size 1)");
+    const int T = g->T;
+    fl_session* s = new fl_session();
+    s->m = g;
+    s->group = true;
+    std::vector<uint8_t> handles((size_t)T * FL_TP_HANDLE_BYTES);
+    int rc = FL_OK;
+    for (int r = 0; r < T && !rc; r++) {
+        fl_session* rs = nullptr;
+        rc = fl_session_create(g->ranks[(size_t)r], max_ctx, 1, kv_dtype, &rs);
+        if (!rc) {
+            s->ranks.push_back(rs);
+            rc = fl_session_tp_handle(rs, handles.data() + (size_t)r * FL_TP_HANDLE_BYTES);
+        }
+    }
+    for (int r = 0; r < T && !rc; r++) rc = fl_session_tp_connect(s->ranks[(size_t)r], handles.data());
+    if (!rc) {
+        RankPool* p = new RankPool();
+        p->rc.assign((size_t)T, 0);
+        p->msg.assign((size_t)T, std::string());
+        s->pool = p;
+        try {
+            for (int r = 1; r < T; r++) p->th.emplace_back(pool_worker, p, r);
+        } catch (...) {
+            rc = fail(FL_ERR_STATE, "could not start the rank threads");
+        }
+    }
+    if (rc) {
+        std::string msg = g_err;
+        fl_session_destroy(s);
+        return fail(rc, "%s", msg.c_str());
+    }
+    s->max_ctx = s->ranks[0]->max_ctx;
+    *out = s;
+    return FL_OK;
+}
+
+static void group_session_destroy(fl_session* s)
+{
+    if (s->pool) pool_stop(s->pool);
+    for (fl_session* r : s->ranks) fl_session_destroy(r);
+    delete s;
 }

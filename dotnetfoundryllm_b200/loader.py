@@ -85,7 +85,9 @@ def build_desc(g: GgufFile, device: int = 0, max_ctx: int | None = None, tp_rank
 
 def load(gguf_image, device: int = 0, max_ctx: int | None = None, tp_rank: int = 0, tp_size: int = 1) -> CudaModel:
     """Parses a GGUF image (bytes / numpy / memmap) and uploads it (this rank's
-    shard when tp_size > 1: the shim slices the raw blocks)."""
+    shard when tp_size > 1: the shim slices the raw blocks).  tp_rank
+    FL_TP_ALL (-1) makes a group of tp_size ranks on the devices `fl_init`
+    chose (runtime.init_tensor_parallel), driven from the calling thread."""
     g = gguf_image if isinstance(gguf_image, GgufFile) else parse(gguf_image)
     desc = build_desc(g, device, max_ctx, tp_rank, tp_size)
     model = CudaModel(desc)

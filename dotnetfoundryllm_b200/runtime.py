@@ -419,6 +419,15 @@ def matvec(ggml_type: int, raw: np.ndarray, rows: int, cols: int, x: np.ndarray)
     return y
 
 
+def init_tensor_parallel(tp: int, devices: list[int] | None = None) -> None:
+    """fl_init: the devices of the process's tensor-parallel groups (models
+    loaded with tp_rank=FL_TP_ALL, tp_size=tp); None = devices 0..tp-1."""
+    arr = (C.c_int32 * tp)(*devices) if devices is not None else None
+    if devices is not None and len(devices) != tp:
+        raise ArgumentError(f"{len(devices)} devices for {tp} ranks")
+    check(N.cuda().fl_init(tp, arr), "fl_init")
+
+
 def connect_tensor_parallel(fwd, all_gather) -> None:
     """Connects one rank's session to its peers: `all_gather(bytes)` must return
     every rank's bytes in rank order (a torch.distributed gather, a file, ...)."""

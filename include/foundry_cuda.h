@@ -67,7 +67,8 @@ typedef struct fl_model_desc {
     float final_softcap;      /* Gemma2 FinalLogitSoftcap (0 = off) */
     float attn_scale;         /* 1/sqrt(head_dim), or Gemma2 QueryPreAttnScalar */
     int32_t device;           /* CUDA device ordinal for this rank */
-    int32_t tp_rank, tp_size; /* tensor parallelism inside one box (1 = off); see fl_session_tp_connect */
+    int32_t tp_rank, tp_size; /* tensor parallelism inside one box (1 = off); see fl_session_tp_connect,
+                                 and FL_TP_ALL / fl_init for a group driven from one thread */
     const void* nccl_id;      /* reserved (NULL): ranks connect through fl_session_tp_connect */
 } fl_model_desc;
 
@@ -125,6 +126,22 @@ int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch, int32_t k
  * after ~2 s.  Logits (fl_forward) and argmax are the full-vocabulary ones
  * on every rank. */
 #define FL_TP_HANDLE_BYTES 64
+
+/* Tensor parallelism driven from one host thread, as the reference calls
+ * Forward (LlamaForwardPass.cs:29).  fl_init sets the process's layout: tp
+ * ranks on devices[0..tp) (NULL: devices 0..tp-1), distinct, each able to
+ * access the others' memory.  A model created with tp_rank = FL_TP_ALL and
+ * tp_size = tp is then a group: the shim creates one rank per device, each
+ * fl_model_upload shards the same bytes to every rank, and fl_session_create
+ * connects the ranks' sessions itself (peer access).  A group session takes
+ * the calls of a one-GPU session (fl_forward, fl_decode_greedy, fl_prefill,
+ * fl_topk, fl_sample, fl_session_reset, fl_time_*) and runs each on all ranks
+ * at once, rank 0 on the calling thread and the others on the session's
+ * worker threads; logits, argmax and tokens are rank 0's (the full ones).
+ * Without fl_init a group uses devices 0..tp_size-1.  fl_forward_batch,
+ * fl_prefill_seq and fl_profile_step are one-GPU calls (FL_ERR_UNSUPPORTED). */
+#define FL_TP_ALL (-1)
+int fl_init(int32_t tp, const int32_t* devices);
 int fl_session_tp_handle(fl_session* s, void* handle);
 int fl_session_tp_connect(fl_session* s, const void* handles);
 

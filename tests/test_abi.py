@@ -110,7 +110,7 @@ def _zero(t):
 
 
 @pytest.mark.parametrize("name,args", [(n, a) for n, r, a in N.PUBLIC_API
-                                       if r is C.c_int and n not in ("fl_dequant",)])
+                                       if r is C.c_int and n not in ("fl_dequant", "fl_init")])
 def test_entry_points_reject_null_arguments_before_device_work(name, args):
     """Every entry point that returns a status refuses null handles/pointers
     with FL_ERR_ARG and a message (the reference's ArgumentNullException)."""
@@ -122,3 +122,23 @@ def test_entry_points_reject_null_arguments_before_device_work(name, args):
 def test_destroy_of_null_handles_is_a_no_op():
     N.cuda().fl_model_destroy(None)
     N.cuda().fl_session_destroy(None)
+
+
+def test_init_and_group_checks_before_device_work():
+    """fl_init refuses rank counts other than 1, 2, 4, 8 and shared or negative
+    devices before any device call; a group model needs 2, 4 or 8 ranks."""
+    lib = N.cuda()
+    assert lib.fl_init(3, None) == N.FL_ERR_UNSUPPORTED
+    assert lib.fl_init(0, None) == N.FL_ERR_UNSUPPORTED
+    assert lib.fl_init(2, (C.c_int32 * 2)(0, 0)) == N.FL_ERR_ARG
+    assert "share device" in N.last_error()
+    assert lib.fl_init(2, (C.c_int32 * 2)(1, -1)) == N.FL_ERR_ARG
+    import torch
+    if torch.cuda.device_count() == 0:
+        assert lib.fl_init(2, None) == N.FL_ERR_CUDA
+    from conftest import model_image
+    from dotnetfoundryllm_b200 import gguf
+    d = loader.build_desc(gguf.parse(model_image("tiny")), tp_rank=N.FL_TP_ALL, tp_size=1)
+    h = C.c_void_p()
+    assert lib.fl_model_create(C.byref(d), C.byref(h)) == N.FL_ERR_UNSUPPORTED
+    assert "group" in N.last_error()

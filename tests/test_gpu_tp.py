@@ -149,3 +149,64 @@ def test_two_ranks_on_one_device_are_refused():
             f.close()
         for mo in models:
             mo.close()
+
+
+def test_group_driven_from_one_thread():
+    """fl_init + a model loaded with tp_rank FL_TP_ALL: the shim creates and
+    connects one rank per GPU and runs each call on all of them, so a single
+    host thread (the reference's Forward loop) drives tensor parallelism.
+    Prompt path, token loop and device greedy loop against the oracle; a bad
+    call is refused before any rank launches and the group keeps working."""
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    from dotnetfoundryllm_b200 import _native as N
+    from dotnetfoundryllm_b200 import loader, runtime
+    img = ggufgen.build_model(ggufgen.SPECS["small-tp"])
+    m = O.Model(img)
+    prompt = ggufgen.prompt_ids(24, m.vocab, 4)
+    n_gen = 16
+    toks, logs = m.generate_greedy(prompt, n_gen, collect_logits=True)
+    m.close()
+    runtime.init_tensor_parallel(2, [0, 1])
+    model = loader.load(img, tp_rank=N.FL_TP_ALL, tp_size=2)
+    fwd = runtime.CudaForwardPass(model)
+    try:
+        p = len(prompt) - 1
+        feed = [int(prompt[-1])] + [int(t) for t in toks[:-1]]
+        bound = ATOL + RTOL * np.abs(logs)
+        for path in ("prompt path", "token loop"):
+            kv = object()
+            if path == "prompt path":
+                fwd.prefill(prompt[:-1], 0, kv)
+            else:
+                for i in range(p):
+                    fwd.forward(int(prompt[i]), i, kv, want_logits=False)
+            got = []
+            for s, tok in enumerate(feed):
+                am = fwd.forward(tok, p + s, kv)
+                got.append(fwd.logits.copy())
+                assert am == int(np.argmax(got[-1]))
+            err = np.abs(np.stack(got) - logs)
+            worst = np.unravel_index(np.argmax(err - bound), err.shape)
+            assert (err <= bound).all(), f"{path}: step {worst[0]} id {worst[1]}"
+        # the device-resident greedy loop after the prompt path
+        kv = object()
+        fwd.prefill(prompt[:-1], 0, kv)
+        dev = fwd.decode_greedy(int(prompt[-1]), p, n_gen)
+        d = next((i for i in range(n_gen) if int(dev[i]) != int(toks[i])), None)
+        if d is not None:
+            srt = np.sort(logs[d])
+            assert srt[-1] - srt[-2] < 1e-3, f"greedy token {d} differs"
+        with pytest.raises(runtime.ArgumentOutOfRangeError):
+            fwd.forward(model.desc.vocab, p + n_gen, kv)
+        with pytest.raises(runtime.ArgumentError):
+            fwd.forward(1, p + n_gen + 5, kv)
+        with pytest.raises(runtime.NotSupportedError):
+            fwd.profile_step(1, p + n_gen)
+        fwd.forward(int(dev[-1]), p + n_gen, kv)
+        assert np.isfinite(fwd.logits).all()
+        ids, vals, _ = fwd.topk(5)
+        assert int(ids[0]) == int(np.argmax(fwd.logits))
+    finally:
+        fwd.close()
+        model.close()
