@@ -6,7 +6,10 @@ decoder blocks instead of 32-42, so the CPU restatement finishes in seconds.
 This covers what the tiny parity models cannot:
 - 128k- and 256k-row LM heads (hundreds of row tiles per SM in the argmax);
 - 4096-wide inputs and 14336-wide FFNs in the x encoding and the unit ranges;
-- head_dim 128 and 256 at 8 kv heads.
+- head_dim 128 and 256 at 8 kv heads;
+- the 70B shapes: 8192-wide inputs and the 28672-wide input of the FFN down
+  projection, more k-blocks than the token kernel's prologue keeps in
+  registers (its one-k-block-at-a-time path).
 
 Bars as everywhere: teacher-forced logits within 1e-3 + 1e-2*|ref|, through
 the token loop and after the prompt path; greedy tokens identical.
@@ -27,7 +30,7 @@ pytestmark = pytest.mark.gpu
 PROMPT, N_GEN = 40, 6
 
 
-@pytest.mark.parametrize("name", ["llama3-8b", "mistral-7b", "gemma2-9b"])
+@pytest.mark.parametrize("name", ["llama3-8b", "mistral-7b", "gemma2-9b", "llama3-70b"])
 def test_real_shapes_match_the_oracle(name):
     spec = dataclasses.replace(ggufgen.SPECS[name], n_layers=2, ctx=512)
     img = ggufgen.build_model(spec)
