@@ -419,7 +419,10 @@ def run_ours(args, ws, rank, local):
     if clocks:
         clocks.start()
     barrier(ws)
+    cudart = profiler_range(args)
     ms = fwd.time_decode(tok, pos, args.steps)
+    if cudart:
+        cudart.cudaProfilerStop()
     clk = clocks.stop() if clocks else None
     ms_max = allreduce_max(ms, ws)
     pos_timed = pos
