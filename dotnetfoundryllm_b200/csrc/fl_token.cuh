@@ -406,7 +406,16 @@ __device__ void phase_attn_combine(const FlAttnArgs& a, float* scr)
             const int sp = j + u * TPO;
             ov_pre[u] = sp < S ? __ldcg(base + sp * sstride + 2 + d) : 0.0f;
         }
-        if (warp == 0) {
+        if (warp == 0 && S <= 32) {
+            /* one split per lane: its (M, L) loaded once, together */
+            const float ms = lane < S ? __ldcg(base + lane * sstride) : -INFINITY;
+            const float ls = lane < S ? __ldcg(base + lane * sstride + 1) : 0.0f;
+            const float M = fl_warp_max(ms);
+            const float f = ms == -INFINITY ? 0.0f : expf(ms - M);
+            if (lane < S) w_s[lane] = f;
+            const float L = fl_warp_sum(fmaf(ls, f, 0.0f));
+            if (lane == 0) w_s[S] = L;
+        } else if (warp == 0) {
             float M = -INFINITY;
             for (int s = lane; s < S; s += 32) M = fmaxf(M, __ldcg(base + s * sstride));
             M = fl_warp_max(M);
