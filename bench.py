@@ -118,9 +118,13 @@ def dist_setup():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if ws > 1:
         import datetime
+        import tempfile
 
         import torch
         import torch.distributed as dist
+        # NCCL's log (with NCCL_DEBUG set, rank 0 prints its version line on
+        # stdout) goes to a file, so stdout carries only the result line
+        os.environ.setdefault("NCCL_DEBUG_FILE", os.path.join(tempfile.gettempdir(), "bench_nccl.%h.%p.log"))
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local))
