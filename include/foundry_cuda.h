@@ -227,7 +227,10 @@ void fl_session_destroy(fl_session* s);
 /* Allocation-free top-k.  No counterpart in the reference: its sampler works
  * on a managed logits array (TopKSampler.ApplyTopK, TopKSampler.cs:42-71);
  * this entry point serves callers that keep logits on the device and must not
- * allocate per call.  Same selection and order as fl_topk (value descending,
+ * allocate per call: an engine whose device memory is one arena reserved up
+ * front by its own pool (a .NET host's allocator, a framework's caching
+ * allocator), where a cudaMalloc/cudaFree per token would synchronize the
+ * device and escape the pool's accounting.  Same selection and order as fl_topk (value descending,
  * index ascending): logits, ids and vals are DEVICE pointers (n floats in, k
  * ints and k floats out), enqueued on `stream` (a cudaStream_t; NULL = the
  * legacy default stream) without synchronizing.

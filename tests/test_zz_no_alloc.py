@@ -1,6 +1,11 @@
 """fl_topk_device, the allocation-free top-k (its scratch is a static device
 array), against fl_topk, the session entry point, on the same logits.
 
+It exists for callers that may not allocate device memory per call: an
+engine whose device memory is one arena owned by its own pool, where a
+cudaMalloc/cudaFree per token would synchronize the device and escape the
+pool's accounting.
+
 The file name sorts last, so in a full run it is collected after every other
 test; it also passes alone.
 """
