@@ -118,7 +118,6 @@ def dist_setup():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if ws > 1:
         import datetime
-        import tempfile
 
         import torch
         import torch.distributed as dist
