@@ -229,6 +229,12 @@ def cpu_sample(img: np.ndarray, position: int, repeats: int = 3, threads: int | 
             "head_s": min(t_head), "n_layers": n_layers, "tok_s_1thread": 1.0 / per_tok_1}
 
 
+def decode_workload(pos_timed: int, steps: int, prompt: int) -> str:
+    """config.workload of the decode line, the same string on both arms."""
+    return (f"{CONFIG} Q4_K/Q6_K bs=1 greedy decode, positions {pos_timed}..{pos_timed + steps - 1} "
+            f"after a {prompt}-token prompt")
+
+
 def run_reference(args, ws, rank):
     if rank != 0:
         return
@@ -250,19 +256,32 @@ def run_reference(args, ws, rank):
         t2 = time.perf_counter()
         if i >= args.warmup:
             times.append((t1 - t0) / 2 * m.n_layers + (t2 - t1))
+    # the reference's own Forward loop is single-threaded (LlamaForwardPass.cs:29): one step on one thread
+    O.set_threads(1)
+    s.fake_length(pos + args.warmup)
+    t0 = time.perf_counter()
+    s.forward_layers(1, pos + args.warmup, 2)
+    t1 = time.perf_counter()
+    s.forward_head()
+    t2 = time.perf_counter()
+    one_thread = 1.0 / ((t1 - t0) / 2 * m.n_layers + (t2 - t1))
     s.close()
     m.close()
     per = sum(times) / len(times)
     value = 1.0 / per
-    sample = (f"per step: 2 of 32 decoder layers (F32 weights dequantized at load, as the reference does) at "
-              f"positions {pos}..{pos + args.warmup + args.steps - 1} plus the LM head, layer time x16")
+    pos_timed = pos + args.warmup
+    sample = (f"C restatement of the reference CPU path on all {threads} host threads (the reference itself is "
+              f"single-threaded: single_thread_value); per step 2 of {m.n_layers} decoder layers (F32 weights "
+              f"dequantized at load, as the reference does) at positions {pos_timed}.."
+              f"{pos_timed + args.steps - 1} plus the LM head, layer time x{m.n_layers // 2}")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF)",
-        "config": {"workload": f"{CONFIG} Q4_K/Q6_K bs=1 decode after a {args.prompt}-token prompt",
+        "config": {"workload": decode_workload(pos_timed, args.steps, args.prompt),
                    "model": CONFIG, "global_batch": 1, "seq_len": args.prompt},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample,
+                         "single_thread_value": one_thread},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -481,8 +500,7 @@ def run_ours(args, ws, rank, local):
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF, N(0,0.02) weights)",
-            "config": {"workload": f"{CONFIG} Q4_K/Q6_K bs=1 greedy decode, positions {pos_timed}.."
-                                   f"{pos_timed + args.steps - 1} after a {args.prompt}-token prompt",
+            "config": {"workload": decode_workload(pos_timed, args.steps, args.prompt),
                        "model": CONFIG, "global_batch": streams, "seq_len": args.prompt,
                        "parallelism": f"tp{ws}" if tp else (f"replicas x{ws}" if ws > 1 else "single GPU"),
                        "l2": "inputs larger than L2 (4.9 GB of weights per step)"},
@@ -494,8 +512,10 @@ def run_ours(args, ws, rank, local):
                          **({"traffic_note": traffic_note} if traffic_note else {}),
                          "matvec_phase_gbs": mv_gbs, "matvec_phase_frac": mv_gbs / peaks["hbm_gbs"]},
             "cpu_baseline": {"value": cpu["tok_s"], "unit": "tok/s", "cores": cpu["threads"], "kind": "port",
-                             "sample": "oracle (C restatement of the reference CPU path, F32 weights) on 2 of 32 "
-                                       f"decoder layers at position {pos_timed} + the LM head, layer time x16",
+                             "sample": f"oracle (C restatement of the reference CPU path, F32 weights) on all "
+                                       f"{cpu['threads']} host threads (the reference is single-threaded: "
+                                       f"single_thread_value), 2 of 32 decoder layers at position {pos_timed} "
+                                       "+ the LM head, layer time x16",
                              "single_thread_value": cpu.get("tok_s_1thread")},
             "e2e": {"value": streams * args.steps / e2e_max, "unit": "tok/s", "h2d_bytes_per_step": 16 * ws,
                     "d2h_bytes_per_step": 4 * ws},

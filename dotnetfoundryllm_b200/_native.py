@@ -108,6 +108,7 @@ PUBLIC_API = [
                             C.POINTER(C.c_int32)]),
     ("fl_session_tp_handle", C.c_int, [C.c_void_p, C.c_void_p]),
     ("fl_session_tp_connect", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("fl_session_tp_reset", C.c_int, [C.c_void_p]),
     ("fl_init", C.c_int, [C.c_int32, C.POINTER(C.c_int32)]),
     ("fl_session_destroy", None, [C.c_void_p]),
     ("fl_dequant", C.c_int, [C.c_int32, C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64]),

@@ -137,6 +137,9 @@ FL_HD void fl_unit_afrag(const uint8_t* unit, int fmt, int expanded, int c, int 
 FL_HD float fl_half_to_float(uint16_t h)
 {
 #ifdef __CUDA_ARCH__
+    /* a NaN comes back quiet with its payload, as (float)Half does on the host */
+    if ((h & 0x7C00u) == 0x7C00u && (h & 0x3FFu))
+        return __uint_as_float(((uint32_t)(h & 0x8000u) << 16) | 0x7FC00000u | ((uint32_t)(h & 0x3FFu) << 13));
     return __half2float(__ushort_as_half(h));
 #else
     uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
@@ -149,7 +152,7 @@ FL_HD float fl_half_to_float(uint16_t h)
             man &= 0x3FFu;
             out = sign | ((uint32_t)(127 - 15 - e) << 23) | (man << 13);
         }
-    } else if (exp == 0x1F) out = sign | 0x7F800000u | (man << 13);
+    } else if (exp == 0x1F) out = man ? (sign | 0x7FC00000u | (man << 13)) : (sign | 0x7F800000u);
     else out = sign | ((exp + 112u) << 23) | (man << 13);
     float f;
     memcpy(&f, &out, 4);

@@ -11,7 +11,7 @@
 
 #include "fl_decode.h"
 
-__device__ __forceinline__ float fl_dq_half(const uint8_t* p) { return __half2float(__ushort_as_half((uint16_t)(p[0] | (p[1] << 8)))); }
+__device__ __forceinline__ float fl_dq_half(const uint8_t* p) { return fl_half_to_float((uint16_t)(p[0] | (p[1] << 8))); }
 
 /* Dequantizer.cs element formulas with the reference's rounding order
  * (explicit _rn intrinsics: no contraction into FMA). */

@@ -49,6 +49,11 @@ __device__ __forceinline__ uint64_t fl_globaltimer()
     return t;
 }
 
+/* An error already recorded by a bounded wait of this launch (or an earlier
+ * phase): later waits on other CTAs or ranks return at once, so a launch that
+ * lost a peer ends after one wait limit instead of one per exchange. */
+__device__ __forceinline__ bool fl_err_set(const int* err) { return err && *(volatile const int*)err != 0; }
+
 /* Bounded wait on an mbarrier phase: gives up after ~2 s (or 2^26 polls),
  * records FL_DEV_ERR_TIMEOUT in *err and returns false.  Never traps. */
 /* Non-blocking test of a phase's completion. */

@@ -248,7 +248,6 @@ cudaError_t fl_launch_sample_scale(float* w, int n, float inv, cudaStream_t st);
 cudaError_t fl_launch_sample_topk_mask(float* w, int n, const float* vals, int k, cudaStream_t st);
 cudaError_t fl_launch_sample_finish(float* w, int n, int greedy, float top_p, float u, int* token, cudaStream_t st);
 /* fl_launch_topk on the file-scope scratch of fl_topk_device (n <= FL_TOPK_DEVICE_MAX_N). */
-#define FL_MAX_DEVICES 64
 cudaError_t fl_launch_topk_static(const float* logits, int32_t n, int32_t k, int32_t* ids, float* vals,
                                   cudaStream_t st);
 

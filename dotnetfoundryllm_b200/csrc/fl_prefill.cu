@@ -484,12 +484,12 @@ __global__ void tp_pf_reduce_kernel(TpSlots sl, int T, int epoch, size_t count, 
 {
     __shared__ int s_ok;
     if (threadIdx.x == 0) {
-        int ok = 1;
+        int ok = !fl_err_set(err); /* an earlier exchange of this prompt already gave up */
         const uint64_t t0 = fl_globaltimer();
         for (int q = 0; q < T && ok; q++)
             for (uint32_t it = 0; fl_ld_acquire_sys(sl.my_flags + q) < epoch; it++)
-                if ((it & 255u) == 0 && fl_globaltimer() - t0 > 2000000000ull) {
-                    atomicExch(err, FL_DEV_ERR_TIMEOUT);
+                if ((it & 255u) == 0 && (fl_err_set(err) || fl_globaltimer() - t0 > 2000000000ull)) {
+                    if (!fl_err_set(err)) atomicExch(err, FL_DEV_ERR_TIMEOUT);
                     ok = 0;
                     break;
                 }

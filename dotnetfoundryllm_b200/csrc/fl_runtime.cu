@@ -1207,6 +1207,26 @@ extern "C" int fl_session_reset(fl_session* s, int32_t seq_slot)
     return FL_OK;
 }
 
+extern "C" int fl_session_tp_reset(fl_session* s)
+{
+    if (!s) return fail(FL_ERR_ARG, "null session");
+    if (s->group) {
+        for (fl_session* r : s->ranks) {
+            int rc = fl_session_tp_reset(r);
+            if (rc) return rc;
+        }
+        return FL_OK;
+    }
+    if (!s->xchg || !s->tp_epoch) return fail(FL_ERR_STATE, "not a tensor-parallel session");
+    /* this rank's epoch counter and the flags its peers raise in its region */
+    CK(cudaMemsetAsync(s->tp_epoch, 0, 16, s->st));
+    CK(cudaMemsetAsync(s->xchg + FL_TP_FLAGS_OFF, 0, FL_TP_RECV_OFF - FL_TP_FLAGS_OFF, s->st));
+    CK(cudaStreamSynchronize(s->st));
+    s->pf_epoch = 0;
+    s->cur_len = 0;
+    return FL_OK;
+}
+
 extern "C" int fl_session_launches_per_step(fl_session* s, int32_t* n)
 {
     if (!s || !n) return fail(FL_ERR_ARG, "null argument");

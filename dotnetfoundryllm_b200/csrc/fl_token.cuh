@@ -98,14 +98,17 @@ __device__ void grid_sync(int* bar, int target, int* err, uint64_t* done_stamp)
     if (threadIdx.x == 0) {
         if (done_stamp) *done_stamp = fl_globaltimer();
         asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(bar) : "memory");
-        if (ld_acquire(bar) < target) {
+        if (ld_acquire(bar) < target && !fl_err_set(err)) {
             const uint64_t t0 = fl_globaltimer();
             for (uint32_t it = 0;; it++) {
                 if (ld_acquire(bar) >= target) break;
                 if (it > 256) __nanosleep(32);
-                if ((it & 255u) == 0 && (fl_globaltimer() - t0 > 2000000000ull || it > (1u << 26))) {
-                    atomicExch(err, FL_DEV_ERR_TIMEOUT);
-                    break;
+                if ((it & 255u) == 0) {
+                    if (fl_err_set(err)) break;
+                    if (fl_globaltimer() - t0 > 2000000000ull || it > (1u << 26)) {
+                        atomicExch(err, FL_DEV_ERR_TIMEOUT);
+                        break;
+                    }
                 }
             }
         }
@@ -492,10 +495,10 @@ __device__ void tp_signal_wait(const FlTokenArgs& ta, int epoch, bool signal)
                 fl_st_release_sys(reinterpret_cast<int*>(ta.tp_peer[q] + FL_TP_FLAGS_OFF) + ta.tp_rank, epoch);
         const int* fl = reinterpret_cast<const int*>(ta.tp_peer[ta.tp_rank] + FL_TP_FLAGS_OFF);
         const uint64_t t0 = fl_globaltimer();
-        for (int q = 0; q < ta.tp_size; q++) {
+        for (int q = 0; q < ta.tp_size && !fl_err_set(ta.err); q++) {
             for (uint32_t it = 0; fl_ld_acquire_sys(fl + q) < epoch; it++) {
-                if ((it & 255u) == 0 && fl_globaltimer() - t0 > 2000000000ull) {
-                    atomicExch(ta.err, FL_DEV_ERR_TIMEOUT);
+                if ((it & 255u) == 0 && (fl_err_set(ta.err) || fl_globaltimer() - t0 > 2000000000ull)) {
+                    if (!fl_err_set(ta.err)) atomicExch(ta.err, FL_DEV_ERR_TIMEOUT);
                     q = ta.tp_size;
                     break;
                 }
@@ -988,7 +991,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                         bv = 0.0f;
                         bi = 0x7fffffff;
                         for (int q = 0; q < ta.tp_size; q++) {
-                            for (uint32_t it = 0; fl_ld_acquire_sys(fl + q) < epoch; it++)
+                            for (uint32_t it = 0; !fl_err_set(ta.err) && fl_ld_acquire_sys(fl + q) < epoch; it++)
                                 if ((it & 255u) == 0 && fl_globaltimer() - t0 > 2000000000ull) {
                                     atomicExch(ta.err, FL_DEV_ERR_TIMEOUT);
                                     break;

@@ -184,6 +184,13 @@ class CudaForwardPass:
         buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
         check(self.lib.fl_session_tp_connect(self.handle, buf), "fl_session_tp_connect")
 
+    def tp_reset(self) -> None:
+        """fl_session_tp_reset: after a tensor-parallel call timed out, every
+        rank calls this between two host barriers; the next forward starts a
+        new sequence at position 0."""
+        check(self.lib.fl_session_tp_reset(self.handle), "fl_session_tp_reset")
+        self._kv_key = None
+
     @property
     def logits(self) -> np.ndarray:
         """IForwardPass.Logits: logits of the most recent forward call."""

@@ -145,6 +145,16 @@ int fl_init(int32_t tp, const int32_t* devices);
 int fl_session_tp_handle(fl_session* s, void* handle);
 int fl_session_tp_connect(fl_session* s, const void* handles);
 
+/* Recovery of a tensor-parallel group after a call returned FL_ERR_TIMEOUT
+ * (a rank stopped or fell out of step).  No counterpart in the reference,
+ * which runs on one CPU.  The ranks' exchange epochs have diverged; this
+ * restarts this rank's at zero and clears its KV sequence (slot 0).  Every
+ * rank calls it once no call is in flight on any rank, and the caller
+ * synchronizes the ranks (a host barrier) before and after it; the next call
+ * then starts a new sequence at position 0.  A group session (FL_TP_ALL)
+ * resets all of its ranks. */
+int fl_session_tp_reset(fl_session* s);
+
 /* KvCache.Clear (KvCache.cs:138-144) of one sequence slot. */
 int fl_session_reset(fl_session* s, int32_t seq_slot);
 
@@ -238,8 +248,10 @@ void fl_session_destroy(fl_session* s);
  *   (2 MiB) per device; n > FL_TOPK_DEVICE_MAX_N returns FL_ERR_ARG.  Nothing
  *   in it has to start at zero.  No cudaMalloc, cudaFree or allocating library
  *   call is made.
- * - The first call on each device looks the scratch address up
- *   (cudaGetSymbolAddress); make that first call outside any stream capture.
+ * - Every call looks the scratch address up on the current device
+ *   (cudaGetSymbolAddress, which allocates nothing), so a device reset in
+ *   between is harmless.  The first call on a device also loads the module
+ *   there: make that first call outside any stream capture.
  * - All calls on one device share the scratch: calls that overlap in time
  *   (different streams or threads, or a call whose previous kernel has not
  *   finished on another stream) race and may return wrong results. */

@@ -78,7 +78,9 @@ float or_half_to_float(uint16_t h)
             out = sign | ((uint32_t)(127 - 15 - e) << 23) | (man << 13);
         }
     } else if (exp == 0x1F) {
-        out = sign | 0x7F800000u | (man << 13);
+        /* infinity, or a NaN returned quiet with its payload (the conversion
+         * behind (float)Half sets the quiet bit of a signalling NaN) */
+        out = man ? (sign | 0x7FC00000u | (man << 13)) : (sign | 0x7F800000u);
     } else {
         out = sign | ((exp + (127 - 15)) << 23) | (man << 13);
     }
@@ -797,8 +799,22 @@ static float get_float(const or_gguf* g, const char* key, float def)
 
 enum { ARCH_LLAMA = 0, ARCH_MISTRAL = 1, ARCH_GEMMA2 = 2, ARCH_QWEN2 = 3 };
 
+/* A weight matrix [rows, cols]: either dequantized once into F32 (`f`, the
+ * reference's LoadTensor) or kept as the raw GGUF blocks of the image (`raw`)
+ * and dequantized one row at a time where it is used.  A row of whole blocks
+ * decodes to the same floats either way (every block is independent), so the
+ * lazy form changes no value; it only keeps host memory at the size of the
+ * quantized file (Llama-3-8B: 4.9 GB instead of ~32 GB of F32). */
 typedef struct {
-    float *attn_norm, *wq, *wk, *wv, *wo, *ffn_norm, *gate, *up, *down;
+    float* f;
+    const uint8_t* raw;
+    int type;
+    int64_t row_bytes;
+} or_mat;
+
+typedef struct {
+    float *attn_norm, *ffn_norm;
+    or_mat wq, wk, wv, wo, gate, up, down;
     float *post_attn_norm, *post_ffn_norm; /* gemma2 */
     float *bq, *bk, *bv;                   /* qwen2 */
 } or_layer;
@@ -810,9 +826,9 @@ struct or_model {
     float rope_base, rope_factor;
     int rope_scaled;      /* RopeScalingType is linear|yarn and factor > 0 */
     float attn_softcap, final_softcap, attn_scale;
-    float* tok_embd;
+    or_mat tok_embd;
     float* out_norm;
-    float* output;        /* may alias tok_embd (tied) */
+    or_mat output;        /* may alias tok_embd (tied) */
     or_layer* layers;
     float* inv_freq;      /* [head_dim/2] */
 };
@@ -822,14 +838,14 @@ void or_model_free(or_model* m)
     if (!m) return;
     for (int l = 0; l < m->n_layers_loaded; l++) {
         or_layer* L = &m->layers[l];
-        free(L->attn_norm); free(L->wq); free(L->wk); free(L->wv); free(L->wo);
-        free(L->ffn_norm); free(L->gate); free(L->up); free(L->down);
+        free(L->attn_norm); free(L->wq.f); free(L->wk.f); free(L->wv.f); free(L->wo.f);
+        free(L->ffn_norm); free(L->gate.f); free(L->up.f); free(L->down.f);
         free(L->post_attn_norm); free(L->post_ffn_norm);
         free(L->bq); free(L->bk); free(L->bv);
     }
     free(m->layers);
-    if (m->output != m->tok_embd) free(m->output);
-    free(m->tok_embd);
+    if (m->output.f != m->tok_embd.f) free(m->output.f);
+    free(m->tok_embd.f);
     free(m->out_norm);
     free(m->inv_freq);
     free(m);
@@ -872,10 +888,59 @@ static float* load_tensor(const or_gguf* g, const char* name, int64_t expected, 
     return dst;
 }
 
+/* Elements and bytes of one block of a dequantizable type (the block
+ * constants of Dequantizer.cs:19-43); 0 for an unknown type. */
+static int block_geom(int type, int* elems, int* bytes)
+{
+    switch (type) {
+    case 0: *elems = 1; *bytes = 4; return 1;    /* F32 */
+    case 1: *elems = 1; *bytes = 2; return 1;    /* F16 */
+    case 30: *elems = 1; *bytes = 2; return 1;   /* BF16 */
+    case 2: *elems = 32; *bytes = 18; return 1;  /* Q4_0 */
+    case 8: *elems = 32; *bytes = 34; return 1;  /* Q8_0 */
+    case 12: *elems = 256; *bytes = 144; return 1; /* Q4_K */
+    case 13: *elems = 256; *bytes = 176; return 1; /* Q5_K */
+    case 14: *elems = 256; *bytes = 210; return 1; /* Q6_K */
+    case 15: *elems = 256; *bytes = 292; return 1; /* Q8_K */
+    default: return 0;
+    }
+}
+
+/* A [rows, cols] matrix: lazy (raw blocks of the image, decoded per row) when
+ * asked and every row is a whole number of blocks, else load_tensor's F32. */
+static or_mat load_matrix(const or_gguf* g, const char* name, int64_t rows, int64_t cols, int optional, int lazy,
+                          char* err, int errlen, int* fail)
+{
+    or_mat mt = {NULL, NULL, 0, 0};
+    int64_t idx = or_gguf_find_tensor(g, name);
+    int be = 0, bb = 0;
+    if (lazy && idx >= 0 && block_geom(g->ti[idx].type, &be, &bb) && cols % be == 0) {
+        const or_tinfo* t = &g->ti[idx];
+        const int64_t nbytes = compute_byte_size(t);
+        const int64_t row_bytes = cols / be * bb;
+        const int64_t abs_off = g->data_start + (int64_t)t->offset;
+        if (nbytes == rows * row_bytes && abs_off >= 0 && abs_off + nbytes <= g->len) {
+            mt.raw = g->data + abs_off;
+            mt.type = t->type;
+            mt.row_bytes = row_bytes;
+            return mt;
+        }
+    }
+    mt.f = load_tensor(g, name, rows * cols, optional, err, errlen, fail);
+    return mt;
+}
+
+/* Row r of a matrix with `cols` columns into dst (F32). */
+static void mat_row(const or_mat* w, int64_t r, int cols, float* dst)
+{
+    if (w->f) memcpy(dst, w->f + (size_t)r * cols, sizeof(float) * (size_t)cols);
+    else or_dequantize(w->type, w->raw + r * w->row_bytes, w->row_bytes, dst, cols);
+}
+
 /* GgufModelLoader.Build/BuildConfig/BuildMistral/BuildGemma2/BuildQwen2 +
  * LoadWeights/LoadGemma2Weights/LoadQwen2Weights (GgufModelLoader.cs:89-372,
  * 518-590). */
-or_model* or_model_load(const uint8_t* data, int64_t len, int max_layers, char* err, int errlen)
+or_model* or_model_load_ex(const uint8_t* data, int64_t len, int max_layers, int lazy, char* err, int errlen)
 {
     char perr[256] = {0};
     or_gguf* g = or_gguf_parse(data, len, perr, sizeof perr);
@@ -941,7 +1006,7 @@ or_model* or_model_load(const uint8_t* data, int64_t len, int max_layers, char* 
     int h = m->hidden, qd = m->n_heads * m->head_dim, kvd = m->n_kv * m->head_dim, f = m->ffn, V = m->vocab;
     int fail = 0;
     m->n_layers_loaded = (max_layers >= 0 && max_layers < m->n_layers) ? max_layers : m->n_layers;
-    m->tok_embd = load_tensor(g, "token_embd.weight", (int64_t)V * h, 0, err, errlen, &fail);
+    m->tok_embd = load_matrix(g, "token_embd.weight", V, h, 0, lazy, err, errlen, &fail);
     m->layers = (or_layer*)calloc((size_t)(m->n_layers_loaded > 0 ? m->n_layers_loaded : 1), sizeof(or_layer));
     for (int l = 0; l < m->n_layers_loaded && !fail; l++) {
         or_layer* L = &m->layers[l];
@@ -951,12 +1016,17 @@ or_model* or_model_load(const uint8_t* data, int64_t len, int max_layers, char* 
         snprintf(nm, sizeof nm, "blk.%d." suffix, l);                                 \
         if (!fail) L->field = load_tensor(g, nm, (int64_t)(cnt), 0, err, errlen, &fail); \
     } while (0)
+#define LM(field, suffix, r, c)                                                                   \
+    do {                                                                                          \
+        snprintf(nm, sizeof nm, "blk.%d." suffix, l);                                             \
+        if (!fail) L->field = load_matrix(g, nm, (int64_t)(r), (int64_t)(c), 0, lazy, err, errlen, &fail); \
+    } while (0)
         LT(attn_norm, "attn_norm.weight", h);
         if (m->arch == ARCH_GEMMA2) LT(post_attn_norm, "post_attn_norm.weight", h);
-        LT(wq, "attn_q.weight", (int64_t)qd * h);
-        LT(wk, "attn_k.weight", (int64_t)kvd * h);
-        LT(wv, "attn_v.weight", (int64_t)kvd * h);
-        LT(wo, "attn_output.weight", (int64_t)h * qd);
+        LM(wq, "attn_q.weight", qd, h);
+        LM(wk, "attn_k.weight", kvd, h);
+        LM(wv, "attn_v.weight", kvd, h);
+        LM(wo, "attn_output.weight", h, qd);
         if (m->arch == ARCH_QWEN2) {
             LT(bq, "attn_q.bias", qd);
             LT(bk, "attn_k.bias", kvd);
@@ -964,15 +1034,16 @@ or_model* or_model_load(const uint8_t* data, int64_t len, int max_layers, char* 
         }
         LT(ffn_norm, "ffn_norm.weight", h);
         if (m->arch == ARCH_GEMMA2) LT(post_ffn_norm, "post_ffn_norm.weight", h);
-        LT(gate, "ffn_gate.weight", (int64_t)f * h);
-        LT(up, "ffn_up.weight", (int64_t)f * h);
-        LT(down, "ffn_down.weight", (int64_t)h * f);
+        LM(gate, "ffn_gate.weight", f, h);
+        LM(up, "ffn_up.weight", f, h);
+        LM(down, "ffn_down.weight", h, f);
 #undef LT
+#undef LM
     }
     if (!fail) m->out_norm = load_tensor(g, "output_norm.weight", h, 0, err, errlen, &fail);
     if (!fail) {
-        m->output = load_tensor(g, "output.weight", (int64_t)V * h, 1, err, errlen, &fail);
-        if (!m->output && !fail) m->output = m->tok_embd;
+        m->output = load_matrix(g, "output.weight", V, h, 1, lazy, err, errlen, &fail);
+        if (!m->output.f && !m->output.raw && !fail) m->output = m->tok_embd;
     }
 #undef K
     or_gguf_free(g);
@@ -987,6 +1058,11 @@ or_model* or_model_load(const uint8_t* data, int64_t len, int max_layers, char* 
         m->inv_freq[i] = 1.0f / powf(m->rope_base, ex);
     }
     return m;
+}
+
+or_model* or_model_load(const uint8_t* data, int64_t len, int max_layers, char* err, int errlen)
+{
+    return or_model_load_ex(data, len, max_layers, 0, err, errlen);
 }
 
 void or_model_config(const or_model* m, int* arch, int* iv, float* fv)
@@ -1105,10 +1181,23 @@ int or_session_fake_length(or_session* s, int n)
 
 /* LinearProjection (LlamaForwardPass.cs:237-260): dst[o] = Dot(src, W[o,:]).
  * Rows are independent, so the OpenMP split does not change any value. */
-static void linear(const float* src, const float* w, float* dst, int out_dim, int in_dim)
+static void linear(const float* src, const or_mat* w, float* dst, int out_dim, int in_dim)
 {
+    if (w->f) {
 #pragma omp parallel for schedule(static) num_threads(g_threads) if (g_threads > 1)
-    for (int o = 0; o < out_dim; o++) dst[o] = or_dot(src, w + (size_t)o * in_dim, in_dim);
+        for (int o = 0; o < out_dim; o++) dst[o] = or_dot(src, w->f + (size_t)o * in_dim, in_dim);
+        return;
+    }
+#pragma omp parallel num_threads(g_threads) if (g_threads > 1)
+    {
+        float* row = (float*)malloc(sizeof(float) * (size_t)in_dim);
+#pragma omp for schedule(static)
+        for (int o = 0; o < out_dim; o++) {
+            mat_row(w, o, in_dim, row);
+            dst[o] = or_dot(src, row, in_dim);
+        }
+        free(row);
+    }
 }
 
 static void rope_all_heads(const or_model* m, float* vec, int position, int n_heads)
@@ -1157,15 +1246,15 @@ static int forward_layers(or_session* s, int token, int position, int n_layers)
     or_model* m = s->m;
     int h = m->hidden, qd = m->n_heads * m->head_dim, kvd = m->n_kv * m->head_dim, f = m->ffn;
     if ((unsigned)token >= (unsigned)m->vocab) return OR_ARGUMENT_OUT_OF_RANGE; /* :89-93 */
-    memcpy(s->x, m->tok_embd + (size_t)token * h, sizeof(float) * (size_t)h);   /* :96 */
+    mat_row(&m->tok_embd, token, h, s->x);   /* :96 */
     int gemma = m->arch == ARCH_GEMMA2;
     for (int l = 0; l < n_layers; l++) {
         or_layer* L = &m->layers[l];
         if (gemma) or_gemma_rmsnorm(s->x, L->attn_norm, s->xn, h);
         else or_rmsnorm(s->x, L->attn_norm, s->xn, h, 1e-5f);
-        linear(s->xn, L->wq, s->q, qd, h);
-        linear(s->xn, L->wk, s->k, kvd, h);
-        linear(s->xn, L->wv, s->v, kvd, h);
+        linear(s->xn, &L->wq, s->q, qd, h);
+        linear(s->xn, &L->wk, s->k, kvd, h);
+        linear(s->xn, &L->wv, s->v, kvd, h);
         if (m->arch == ARCH_QWEN2) { /* Qwen2ForwardPass.cs:83-85 */
             for (int i = 0; i < qd; i++) s->q[i] = s->q[i] + L->bq[i];
             for (int i = 0; i < kvd; i++) s->k[i] = s->k[i] + L->bk[i];
@@ -1180,18 +1269,18 @@ static int forward_layers(or_session* s, int token, int position, int n_layers)
         if (gemma) window = (l % 2 == 0) ? m->window : INT_MAX; /* Gemma2ForwardPass.cs:87 */
         rc = attention(s, l, position + 1, window);
         if (rc) return rc;
-        linear(s->att, L->wo, s->xn, h, qd);
+        linear(s->att, &L->wo, s->xn, h, qd);
         if (gemma) or_gemma_rmsnorm(s->xn, L->post_attn_norm, s->xn, h);
         for (int i = 0; i < h; i++) s->x[i] = s->x[i] + s->xn[i];
         if (gemma) or_gemma_rmsnorm(s->x, L->ffn_norm, s->xn, h);
         else or_rmsnorm(s->x, L->ffn_norm, s->xn, h, 1e-5f);
         /* ComputeSiluFfn (LlamaForwardPass.cs:217-232) / ComputeGeluFfn (Gemma2:187-199) */
-        linear(s->xn, L->gate, s->ffn_buf, f, h);
+        linear(s->xn, &L->gate, s->ffn_buf, f, h);
         if (gemma) or_gelu(s->ffn_buf, f);
         else or_silu(s->ffn_buf, f);
-        linear(s->xn, L->up, s->ffn_up, f, h);
+        linear(s->xn, &L->up, s->ffn_up, f, h);
         for (int i = 0; i < f; i++) s->ffn_buf[i] = s->ffn_buf[i] * s->ffn_up[i];
-        linear(s->ffn_buf, L->down, s->xn, h, f);
+        linear(s->ffn_buf, &L->down, s->xn, h, f);
         if (gemma) or_gemma_rmsnorm(s->xn, L->post_ffn_norm, s->xn, h);
         for (int i = 0; i < h; i++) s->x[i] = s->x[i] + s->xn[i];
     }
@@ -1204,7 +1293,7 @@ int or_forward_head(or_session* s, float* logits_out)
     int h = m->hidden;
     if (m->arch == ARCH_GEMMA2) or_gemma_rmsnorm(s->x, m->out_norm, s->xn, h);
     else or_rmsnorm(s->x, m->out_norm, s->xn, h, 1e-5f);
-    linear(s->xn, m->output, s->logits, m->vocab, h);
+    linear(s->xn, &m->output, s->logits, m->vocab, h);
     if (m->arch == ARCH_GEMMA2 && m->final_softcap > 0.0f) or_softcap(s->logits, m->vocab, m->final_softcap);
     if (logits_out) memcpy(logits_out, s->logits, sizeof(float) * (size_t)m->vocab);
     return OR_OK;

@@ -87,6 +87,9 @@ typedef struct or_session or_session;
  * max_layers < 0 loads every layer; a smaller value loads only the first
  * max_layers blocks (used to time a bounded sample of a large model). */
 or_model* or_model_load(const uint8_t* data, int64_t len, int max_layers, char* err, int errlen);
+/* lazy = 1: weight matrices stay as the image's raw blocks (the caller keeps
+ * `data` alive) and are dequantized row by row where used; same values. */
+or_model* or_model_load_ex(const uint8_t* data, int64_t len, int max_layers, int lazy, char* err, int errlen);
 void or_model_free(or_model* m);
 /* Config readback: arch (0 llama, 1 mistral, 2 gemma2, 3 qwen2), dims[...] */
 void or_model_config(const or_model* m, int* arch, int* ints12, float* floats8);

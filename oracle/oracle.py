@@ -64,6 +64,7 @@ def lib() -> C.CDLL:
             "or_gguf_data_start": (i64, [vp]),
             "or_gguf_find_tensor": (i64, [vp, C.c_char_p]),
             "or_gguf_tensor_info": (i32, [vp, i64, vp, vp, vp, vp, vp]),
+            "or_model_load_ex": (vp, [vp, i64, i32, i32, C.c_char_p, i32]),
             "or_model_load": (vp, [vp, i64, i32, C.c_char_p, i32]),
             "or_model_free": (None, [vp]),
             "or_model_config": (None, [vp, vp, vp, vp]),
@@ -114,10 +115,14 @@ def matvec(t: int, raw: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.n
 
 
 class Model:
-    def __init__(self, image: np.ndarray, max_layers: int = -1):
+    """``lazy=True`` keeps the weight matrices as the image's quantized blocks
+    and dequantizes each row where it is used (the same floats, so the same
+    results): host memory stays at the size of the file instead of F32."""
+
+    def __init__(self, image: np.ndarray, max_layers: int = -1, lazy: bool = False):
         self.image = np.ascontiguousarray(image, dtype=np.uint8)
         err = C.create_string_buffer(512)
-        self.h = lib().or_model_load(_p(self.image), self.image.size, max_layers, err, 512)
+        self.h = lib().or_model_load_ex(_p(self.image), self.image.size, max_layers, int(lazy), err, 512)
         if not self.h:
             raise RuntimeError(err.value.decode())
         arch = C.c_int()

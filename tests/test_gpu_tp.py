@@ -75,6 +75,39 @@ def test_ranks_match_the_oracle(name, ranks, tmp_path):
     assert (err <= bound).all(), f"{name} prefill: step {worst[0]} id {worst[1]}: {r0['pf_logits'][worst]} vs {logs[worst]}"
 
 
+def test_a_rank_that_misses_a_step_times_out_fast_and_the_group_recovers(tmp_path):
+    """Failure detection without a GPU fault: rank 1 skips one step, so rank
+    0's token kernel finds no peer flags.  Its first bounded wait gives up
+    after ~2 s and every later exchange of the step returns at once, so the
+    call fails with FL_ERR_TIMEOUT in a few seconds (not one limit per
+    exchange: 2 per layer + 1).  After fl_session_tp_reset on both ranks the
+    teacher-forced logits match the oracle again, identical on both ranks."""
+    ranks = 2
+    if _gpus() < ranks:
+        pytest.skip(f"needs {ranks} GPUs")
+    name = "small-tp"
+    img = ggufgen.build_model(ggufgen.SPECS[name])
+    m = O.Model(img)
+    prompt = ggufgen.prompt_ids(16, m.vocab, 6)
+    toks, logs = m.generate_greedy(prompt, 8, collect_logits=True)
+    m.close()
+    np.savez(tmp_path / "ref.npz", prompt=prompt, toks=np.array(toks))
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={ranks}",
+           "--master-addr=127.0.0.1", f"--master-port={port}", str(WORKER), "--model", name,
+           "--ref", str(tmp_path / "ref.npz"), "--out", str(tmp_path), "--scenario", "lost-step"]
+    subprocess.run(cmd, env=env, timeout=600, check=True)
+    r0, r1 = (np.load(tmp_path / f"rank{r}.npz") for r in range(ranks))
+    assert bool(r0["timed_out"]), "the step without its peer did not report FL_ERR_TIMEOUT"
+    assert float(r0["elapsed"]) < 10.0, f"timed-out step took {float(r0['elapsed']):.1f} s"
+    np.testing.assert_array_equal(r0["logits"], r1["logits"])
+    err = np.abs(r0["logits"] - logs)
+    assert (err <= ATOL + RTOL * np.abs(logs)).all()
+
+
 def test_two_ranks_in_one_process(tmp_path):
     """A host that keeps every rank in one process (the C# engine), one thread
     per GPU: the exchange regions are mapped with peer access instead of CUDA

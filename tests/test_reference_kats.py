@@ -31,6 +31,20 @@ def test_half_to_float(e):
     assert O.lib().or_half_to_float(e["bits"]) == e["value"]
 
 
+@pytest.mark.parametrize("bits,want", [(0x7C01, 0x7FC02000), (0xFC01, 0xFFC02000), (0x7E00, 0x7FC00000),
+                                       (0x7DFF, 0x7FFFE000), (0x7C00, 0x7F800000), (0xFC00, 0xFF800000)])
+def test_half_nan_comes_back_quiet_with_its_payload(bits, want):
+    """HalfToFloat is (float)BitConverter.UInt16BitsToHalf(bits)
+    (Dequantizer.cs:49-51): .NET's Half-to-float conversion returns a NaN with
+    the quiet bit set and the payload moved to the top of the float mantissa
+    (as the x86 F16C instruction does); infinities stay infinities.  No
+    reference test holds a NaN vector, so this pins the oracle to that
+    documented conversion; the GPU is pinned to the oracle bit for bit
+    (tests/test_gpu_kernels.py, F16 on random bytes)."""
+    got = np.float32(O.lib().or_half_to_float(bits)).view(np.uint32)
+    assert int(got) == want, hex(int(got))
+
+
 @pytest.mark.parametrize("e", KATS["bf16_to_float"], ids=lambda e: hex(e["bits"]))
 def test_bf16_to_float(e):
     assert O.lib().or_bf16_to_float(e["bits"]) == e["value"]

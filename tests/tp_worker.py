@@ -20,11 +20,55 @@ import torch.distributed as dist  # noqa: E402
 from dotnetfoundryllm_b200 import ggufgen, loader, runtime  # noqa: E402
 
 
+def _teacher_forced(fwd, prompt, toks):
+    kv = object()
+    for i in range(len(prompt) - 1):
+        fwd.forward(int(prompt[i]), i, kv, want_logits=False)
+    pos, out = len(prompt) - 1, []
+    for tok in [int(prompt[-1])] + [int(t) for t in toks[:-1]]:
+        fwd.forward(tok, pos, kv)
+        out.append(fwd.logits.copy())
+        pos += 1
+    return np.stack(out)
+
+
+def lost_step(fwd, prompt, toks, rank: int, out: str) -> None:
+    """A rank that misses a step: the ranks run a few steps together, then
+    every rank but 0 skips one.  Rank 0's step must fail with FL_ERR_TIMEOUT
+    after about one wait limit (~2 s), not one per exchange of the step.
+    After fl_session_tp_reset on every rank (between host barriers) the group
+    runs the teacher-forced sequence again, as on a fresh session."""
+    import time
+    kv = object()
+    for i in range(4):
+        fwd.forward(int(prompt[i]), i, kv, want_logits=False)
+    dist.barrier()
+    elapsed, timed_out = 0.0, False
+    if rank == 0:
+        t0 = time.monotonic()
+        try:
+            fwd.forward(int(prompt[4]), 4, kv, want_logits=False)
+        except runtime.DeviceTimeoutError:
+            timed_out = True
+        elapsed = time.monotonic() - t0
+    dist.barrier()
+    fwd.tp_reset()
+    dist.barrier()
+    logits = _teacher_forced(fwd, prompt, toks)
+    np.savez(Path(out) / f"rank{rank}.npz", logits=logits, timed_out=np.array(timed_out),
+             elapsed=np.array(elapsed))
+    dist.barrier()
+    fwd.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", required=True)
     ap.add_argument("--ref", required=True, help="npz with the prompt and the reference's greedy tokens")
     ap.add_argument("--out", required=True, help="output directory (rank<r>.npz)")
+    ap.add_argument("--scenario", default="parity", choices=["parity", "lost-step"])
     args = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
@@ -41,6 +85,9 @@ def main() -> None:
     model = loader.load(img, device=local, tp_rank=rank, tp_size=world)
     fwd = runtime.CudaForwardPass(model)
     runtime.connect_tensor_parallel(fwd, gather)
+    if args.scenario == "lost-step":
+        lost_step(fwd, prompt, toks, rank, args.out)
+        return
     kv = object()
     for i in range(len(prompt) - 1):
         fwd.forward(int(prompt[i]), i, kv, want_logits=False)
