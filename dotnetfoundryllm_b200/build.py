@@ -25,7 +25,7 @@ LIB = PKG / "_lib"
 OBJ = PKG / "_build"
 
 CUDA_SOURCES = ["fl_matvec.cu", "fl_misc.cu", "fl_token.cu", "fl_token_hd64.cu", "fl_token_hd128.cu",
-                "fl_token_hd256.cu", "fl_prefill.cu", "fl_sample.cu", "fl_runtime.cu"]
+                "fl_token_hd256.cu", "fl_prefill.cu", "fl_sample.cu", "fl_tc_gemm.cu", "fl_runtime.cu"]
 HOST_SOURCES = ["fl_repack.cpp"]
 HEADERS = ["fl_layout.h", "fl_decode.h", "fl_device.cuh", "fl_kernels.h", "fl_repack.h", "fl_mv_core.cuh", "fl_dequant.cuh",
            "fl_token.cuh"]

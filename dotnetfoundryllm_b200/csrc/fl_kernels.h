@@ -235,6 +235,23 @@ cudaError_t fl_launch_attn_out(const float* O, int n, int nh, int nkv, int hd, _
 cudaError_t fl_launch_glu(const float* g, int n, int F, int gelu, __half* act, cudaStream_t st, int stack = 0,
                           const float* g_lo = nullptr);
 
+/* ── the tcgen05 GEMM (fl_tc_gemm.cu) ──────────────────────────────────────
+ * Y[b][n][m] = alpha * sum_k A[b][m][k] * B[b][n][k] (+ beta * Y[b][n][m]),
+ * A and B fp16 K-major (row strides lda / ldb elements, 16-byte aligned rows),
+ * Y fp32.  With batch > 1, batch b's rows start at row b * a_batch_rows of A
+ * and b * b_batch_rows of B, and at Y + b * y_batch. */
+struct FlTcGemm {
+    int M, N, K, batch;
+    int a_batch_rows, b_batch_rows;
+    float* Y;
+    long long ldy, y_batch;
+    float alpha, beta;
+    int* err;
+};
+cudaError_t fl_tc_gemm(const __half* A, long long lda, const __half* B, long long ldb, const FlTcGemm& p,
+                       cudaStream_t st);
+size_t fl_tc_gemm_smem_bytes(int bn);
+
 /* Bit-exact block dequantization (fl_dequant). */
 cudaError_t fl_launch_dequant(int32_t ggml_type, const uint8_t* src, int64_t n_blocks, float* dst, cudaStream_t st);
 

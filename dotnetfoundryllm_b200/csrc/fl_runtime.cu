@@ -2011,6 +2011,58 @@ extern "C" int fl_dequant_split_test(int32_t type, const void* src, uint64_t nby
     return FL_OK;
 }
 
+extern "C" int fl_gemm_f16(const void* a, int64_t lda, const void* b, int64_t ldb, int32_t M, int32_t N, int32_t K,
+                           int32_t batch, int32_t a_batch_rows, int32_t b_batch_rows, float alpha, float beta, float* y)
+{
+    if (!a || !b || !y) return fail(FL_ERR_ARG, "null argument");
+    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || lda < K || ldb < K || (lda % 8) || (ldb % 8))
+        return fail(FL_ERR_ARG, "bad GEMM shape (M %d, N %d, K %d, lda %lld, ldb %lld: strides multiples of 8)", M, N,
+                    K, (long long)lda, (long long)ldb);
+    if (batch > 1 && (a_batch_rows < M || b_batch_rows < N)) return fail(FL_ERR_ARG, "batch rows below M / N");
+    const long long arows = batch > 1 ? (long long)batch * a_batch_rows : M;
+    const long long brows = batch > 1 ? (long long)batch * b_batch_rows : N;
+    const size_t ab = (size_t)arows * lda * 2, bb = (size_t)brows * ldb * 2, yb = (size_t)batch * N * M * 4;
+    std::vector<void*> al;
+    __half *da = nullptr, *db = nullptr;
+    float* dy = nullptr;
+    int* derr = nullptr;
+    int rc = dalloc(al, &da, ab);
+    if (!rc) rc = dalloc(al, &db, bb);
+    if (!rc) rc = dalloc(al, &dy, yb);
+    if (!rc) rc = dalloc(al, &derr, 16);
+    cudaError_t e = cudaSuccess;
+    if (!rc) {
+        e = cudaMemcpy(da, a, ab, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(db, b, bb, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(dy, y, yb, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemset(derr, 0, 16);
+        if (e == cudaSuccess) {
+            FlTcGemm p;
+            p.M = M;
+            p.N = N;
+            p.K = K;
+            p.batch = batch;
+            p.a_batch_rows = batch > 1 ? a_batch_rows : M;
+            p.b_batch_rows = batch > 1 ? b_batch_rows : N;
+            p.Y = dy;
+            p.ldy = M;
+            p.y_batch = (long long)N * M;
+            p.alpha = alpha;
+            p.beta = beta;
+            p.err = derr;
+            e = fl_tc_gemm(da, lda, db, ldb, p, 0);
+        }
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        int herr = 0;
+        if (e == cudaSuccess) e = cudaMemcpy(&herr, derr, 4, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess) e = cudaMemcpy(y, dy, yb, cudaMemcpyDeviceToHost);
+        if (e == cudaSuccess && herr) rc = fail(FL_ERR_TIMEOUT, "a bounded wait of the GEMM expired");
+        if (e != cudaSuccess) rc = fail(FL_ERR_CUDA, "fl_gemm_f16: %s", cudaGetErrorString(e));
+    }
+    for (void* p : al) cudaFree(p);
+    return rc;
+}
+
 extern "C" int fl_matvec(int32_t type, const void* w, uint64_t nbytes, int32_t rows, int32_t cols, const float* x,
                          float* y)
 {

@@ -271,7 +271,17 @@ int fl_dequant(int32_t ggml_type, const void* src, uint64_t nbytes, float* dst, 
 int fl_matvec(int32_t ggml_type, const void* w, uint64_t nbytes, int32_t rows, int32_t cols, const float* x,
               float* y);
 
-/* Timing helpers for the benchmark: runs one token step and reads the
+/* Test hook: the tensor-core GEMM of the prompt path and of batched decode
+ * (tcgen05, fp16 operands, fp32 accumulation), the LinearProjection of
+ * LlamaForwardPass.cs:237-260 over a chunk of rows.  Host memory in and out:
+ * for each batch b < batch, y[b][n][m] = alpha * sum_k a[b][m][k] * b[b][n][k]
+ * + beta * y[b][n][m], with a (fp16 bits) holding batch * a_batch_rows rows
+ * of lda elements (M rows when batch is 1), b likewise, y dense
+ * [batch][N][M] fp32.  lda and ldb are multiples of 8. */
+int fl_gemm_f16(const void* a, int64_t lda, const void* b, int64_t ldb, int32_t M, int32_t N, int32_t K,
+                int32_t batch, int32_t a_batch_rows, int32_t b_batch_rows, float alpha, float beta, float* y);
+
+/* Timing helpers for the benchmark/* Timing helpers for the benchmark: runs one token step and reads the
  * device timestamps the token kernel takes at every phase boundary; fills
  * ms[class] (time spent in phases of that class) and bytes[class]
  * (algorithmic bytes) for the FL_PROF_* classes, and *launches with the
