@@ -305,7 +305,7 @@ def prefill_record(p: dict, d, peaks: dict, ws: int, cpu: dict) -> dict:
     fl = streams * prefill_flops(d, p["tokens"])
     tflops = fl / (p["ms"] / 1e3) / 1e12
     return {
-        "path": "fl_prefill: split-fp16 tensor-core GEMMs (cuBLASLt) for the projections and for attention's "
+        "path": "fl_prefill: split-fp16 GEMMs on the hand-written tcgen05 kernel (fl_tc_gemm) for the projections and for attention's "
                 "QK^T and PV; own dequant, norm, RoPE/KV-append, masked-softmax and GLU kernels",
         "tokens": p["tokens"], "ms": p["ms"], "tok_s": streams * p["tokens"] / (p["ms"] / 1e3),
         "e2e_tok_s": streams * p["tokens"] / p["e2e_s"],

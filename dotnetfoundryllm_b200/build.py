@@ -93,7 +93,7 @@ def build_cuda(force: bool = False, verbose_ptxas: bool = False) -> Path:
     with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 4))) as ex:
         list(ex.map(_run, jobs))
     if force or jobs or _stale(out, objs):
-        _run([nvcc, *ARCH, "-shared", "-o", str(out), *map(str, objs), "-lcublasLt", "-lcudart", "-lpthread"])
+        _run([nvcc, *ARCH, "-shared", "-o", str(out), *map(str, objs), "-lcudart", "-lpthread"])
     return out
 
 

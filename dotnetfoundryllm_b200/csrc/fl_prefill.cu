@@ -4,8 +4,8 @@
  * 133-137; the values are those of LlamaForwardPass.Forward for each token).
  *
  * The projections are dense contractions of the chunk's [n x K] activations
- * with the layer's weights, on the tensor cores through cuBLASLt in split
- * fp16 ("fp16x3"): every operand value v is stored as hi = fp16(v) and
+ * with the layer's weights, on the tcgen05 tensor cores (fl_tc_gemm.cu) in
+ * split fp16 ("fp16x3"): every operand value v is stored as hi = fp16(v) and
  * lo = fp16(v - hi), and one GEMM over K' = 3K with rows [x_hi | x_lo | x_hi]
  * and [w_hi | w_hi | w_lo] sums x_hi*w_hi + x_lo*w_hi + x_hi*w_lo in fp32 —
  * close to fp32 products of the bit-exact dequantized weights (weights are

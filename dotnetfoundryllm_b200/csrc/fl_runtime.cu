@@ -22,7 +22,6 @@
 #include <string>
 #include <vector>
 
-#include <cublasLt.h>
 
 #include "../../include/foundry_cuda.h"
 #include "fl_kernels.h"
@@ -174,9 +173,6 @@ struct fl_session {
     int pf_nkmax = 0;
     __half *pf_qs = nullptr, *pf_ks = nullptr, *pf_vt = nullptr, *pf_p = nullptr;
     float *pf_s = nullptr, *pf_o = nullptr;
-    cublasLtHandle_t lt = nullptr;
-    void* lt_ws = nullptr;
-    size_t lt_ws_bytes = 0;
     std::vector<void*> allocs;
     /* a group session: one connected rank session per device and the worker
      * threads that run ranks 1.. while the caller runs rank 0 */
@@ -1088,7 +1084,6 @@ extern "C" void fl_session_destroy(fl_session* s)
     cudaSetDevice(s->m->d.device);
     if (s->st) cudaStreamSynchronize(s->st);
     if (s->graph) cudaGraphExecDestroy(s->graph);
-    if (s->lt) cublasLtDestroy(s->lt);
     for (void* p : s->tp_opened)
         if (p) cudaIpcCloseMemHandle(p);
     for (void* p : s->allocs) cudaFree(p);
@@ -1494,70 +1489,37 @@ extern "C" int fl_topk_device(const float* logits, int32_t n, int32_t k, int32_t
 }
 
 /* ── the prompt path ────────────────────────────────────────────────────── */
-#define LTCK(call)                                                                                  \
-    do {                                                                                           \
-        cublasStatus_t st_ = (call);                                                               \
-        if (st_ != CUBLAS_STATUS_SUCCESS) return fail(FL_ERR_CUDA, "%s: cuBLASLt status %d", #call, (int)st_); \
-    } while (0)
 
 /* Y[n x N] (fp32, row-major, ld N) = alpha * X[n x K] · W[N x K]^T + beta * Y
- * (fp16, row-major, leading dimensions ldw / ldx, default K): the
- * column-major "TN" product Y^T = W · X^T on the tensor cores with fp32
- * accumulation, `batch` times with the given element strides. */
-static int lt_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K, int n, float alpha,
+ * (fp16, row-major, leading dimensions ldw / ldx, default K) on the tcgen05
+ * tensor cores (fl_tc_gemm), `batch` times with the given element strides. */
+static int tc_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K, int n, float alpha,
                    int batch = 1, int64_t sW = 0, int64_t sX = 0, int64_t sY = 0, int ldw = 0, int ldx = 0,
                    float beta = 0.0f)
 {
     if (!ldw) ldw = K;
     if (!ldx) ldx = K;
-    cublasLtMatmulDesc_t op = nullptr;
-    cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
-    int rc = FL_OK;
-    cublasStatus_t st = cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F);
-    const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
-    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof ta);
-    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof tb);
-    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&la, CUDA_R_16F, K, N, ldw);
-    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&lb, CUDA_R_16F, K, n, ldx);
-    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatrixLayoutCreate(&lc, CUDA_R_32F, N, n, N);
-    if (batch > 1) {
-        const cublasLtMatrixLayout_t ls[3] = {la, lb, lc};
-        const int64_t strides[3] = {sW, sX, sY};
-        for (int i = 0; i < 3 && st == CUBLAS_STATUS_SUCCESS; i++) {
-            st = cublasLtMatrixLayoutSetAttribute(ls[i], CUBLASLT_MATRIX_LAYOUT_BATCH_COUNT, &batch, sizeof batch);
-            if (st == CUBLAS_STATUS_SUCCESS)
-                st = cublasLtMatrixLayoutSetAttribute(ls[i], CUBLASLT_MATRIX_LAYOUT_STRIDED_BATCH_OFFSET, &strides[i],
-                                                      sizeof strides[i]);
-        }
-    }
-    cublasLtMatmulPreference_t pref = nullptr;
-    cublasLtMatmulHeuristicResult_t heur;
-    int found = 0;
-    if (st == CUBLAS_STATUS_SUCCESS) st = cublasLtMatmulPreferenceCreate(&pref);
-    if (st == CUBLAS_STATUS_SUCCESS)
-        st = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &s->lt_ws_bytes,
-                                                  sizeof s->lt_ws_bytes);
-    if (st == CUBLAS_STATUS_SUCCESS)
-        st = cublasLtMatmulAlgoGetHeuristic(s->lt, op, la, lb, lc, lc, pref, 1, &heur, &found);
-    if (st == CUBLAS_STATUS_SUCCESS && found < 1) st = CUBLAS_STATUS_NOT_SUPPORTED;
-    if (st == CUBLAS_STATUS_SUCCESS)
-        st = cublasLtMatmul(s->lt, op, &alpha, W, la, X, lb, &beta, Y, lc, Y, lc, &heur.algo, s->lt_ws, s->lt_ws_bytes,
-                            s->st);
-    if (st != CUBLAS_STATUS_SUCCESS)
-        rc = fail(FL_ERR_CUDA, "cuBLASLt GEMM %dx%dx%d (batch %d): status %d", N, n, K, batch, (int)st);
-    if (pref) cublasLtMatmulPreferenceDestroy(pref);
-    if (lc) cublasLtMatrixLayoutDestroy(lc);
-    if (lb) cublasLtMatrixLayoutDestroy(lb);
-    if (la) cublasLtMatrixLayoutDestroy(la);
-    if (op) cublasLtMatmulDescDestroy(op);
-    return rc;
+    if (batch > 1 && ((sW % ldw) || (sX % ldx))) return fail(FL_ERR_ARG, "GEMM batch strides are not whole rows");
+    FlTcGemm p;
+    p.M = N;
+    p.N = n;
+    p.K = K;
+    p.batch = batch;
+    p.a_batch_rows = batch > 1 ? (int)(sW / ldw) : N;
+    p.b_batch_rows = batch > 1 ? (int)(sX / ldx) : n;
+    p.Y = Y;
+    p.ldy = N;
+    p.y_batch = sY;
+    p.alpha = alpha;
+    p.beta = beta;
+    p.err = s->state + ST_ERR;
+    CK(fl_tc_gemm(W, ldw, X, ldx, p, s->st));
+    return FL_OK;
 }
 
-/* A projection in split fp16: X is [n x 3K0] ([hi | lo | hi]), W is
- * [N x 3K0] ([hi | hi | lo], scaled by FL_PF_WSCALE, which alpha undoes). */
 static int pf_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K0, int n)
 {
-    return lt_gemm(s, W, X, Y, N, 3 * K0, n, 1.0f / FL_PF_WSCALE);
+    return tc_gemm(s, W, X, Y, N, 3 * K0, n, 1.0f / FL_PF_WSCALE);
 }
 
 /* split-fp16 weights of a raw matrix into dst (rows x 3*cols) */
@@ -1606,11 +1568,8 @@ static int pf_alloc(fl_session* s)
     AL(s->pf_p, (size_t)cap * m->nh_l * nkmax * 3 * 2);
     AL(s->pf_o, (size_t)cap * qd * 4);
     s->pf_nkmax = nkmax;
-    s->lt_ws_bytes = (size_t)32 << 20;
-    AL(s->lt_ws, s->lt_ws_bytes);
 #undef AL
     if (rc) return rc;
-    LTCK(cublasLtCreate(&s->lt));
     s->pf_cap = cap;
     return FL_OK;
 }
@@ -1681,12 +1640,12 @@ static int pf_chunk(fl_session* s, int slot, const int32_t* tokens, int n, int s
             const int nkv = m->nkv_l, grp = m->nh_l / nkv, nk = start + n, nkp = (nk + 7) & ~7, rows = n * grp;
             CK(fl_launch_attn_q_split(s->pf_q, n, m->nh_l, nkv, hd, s->pf_qs, s->st));
             CK(fl_launch_attn_kv_split(kc, vc, nk, nkp, kvd, hd, s->pf_ks, s->pf_vt, s->st));
-            if ((rc = lt_gemm(s, s->pf_ks, s->pf_qs, s->pf_s, nkp, 3 * hd, rows, 1.0f, nkv, (int64_t)nkp * 3 * hd,
+            if ((rc = tc_gemm(s, s->pf_ks, s->pf_qs, s->pf_s, nkp, 3 * hd, rows, 1.0f, nkv, (int64_t)nkp * 3 * hd,
                               (int64_t)rows * 3 * hd, (int64_t)rows * nkp)))
                 return rc;
             CK(fl_launch_attn_softmax(s->pf_s, nkv * rows, n, grp, nkp, start, window, d.attn_scale,
                                       gemma ? d.attn_softcap : 0.0f, s->pf_p, s->st));
-            if ((rc = lt_gemm(s, s->pf_vt, s->pf_p, s->pf_o, hd, 3 * nkp, rows, 1.0f / 1024.0f, nkv,
+            if ((rc = tc_gemm(s, s->pf_vt, s->pf_p, s->pf_o, hd, 3 * nkp, rows, 1.0f / 1024.0f, nkv,
                               (int64_t)hd * 3 * nkp, (int64_t)rows * 3 * nkp, (int64_t)rows * hd)))
                 return rc;
             CK(fl_launch_attn_out(s->pf_o, n, m->nh_l, nkv, hd, s->pf_act, s->st));
@@ -1853,8 +1812,8 @@ static void bt_cache_weights(fl_session* s)
  * Every weight byte is read once. */
 static int bt_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K, int B)
 {
-    int rc = lt_gemm(s, W, X, s->bt_y2, N, K, 2 * B, 1.0f / FL_PF_WSCALE, 1, 0, 0, 0, 2 * K, K);
-    if (!rc) rc = lt_gemm(s, W + K, X, s->bt_y2, N, K, B, 1.0f / FL_PF_WSCALE, 1, 0, 0, 0, 2 * K, K, 1.0f);
+    int rc = tc_gemm(s, W, X, s->bt_y2, N, K, 2 * B, 1.0f / FL_PF_WSCALE, 1, 0, 0, 0, 2 * K, K);
+    if (!rc) rc = tc_gemm(s, W + K, X, s->bt_y2, N, K, B, 1.0f / FL_PF_WSCALE, 1, 0, 0, 0, 2 * K, K, 1.0f);
     if (rc) return rc;
     if (Y) CK(fl_launch_add_halves(s->bt_y2, B, N, Y, s->st));
     return FL_OK;

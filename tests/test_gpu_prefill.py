@@ -82,8 +82,8 @@ def test_greedy_tokens_after_prefill(family):
 
 def test_chunked_prefill_equals_one_pass(family):
     """Two calls (the second attends to the first's cached keys) = one call,
-    up to summation order: the GEMM library picks its reduction split per
-    shape, so logits may differ by a few 1e-5."""
+    up to summation order: attention's score rows span a different number of
+    cached keys, so logits may differ by a few 1e-5."""
     name, model, fwd = family
     prompt, toks, logs = reference(name)
     feed = [int(prompt[-1])] + [int(t) for t in toks[:7]]
