@@ -11,6 +11,7 @@
 
 #define FL_DEV_ERR_TIMEOUT 1
 #define FL_DEV_ERR_TOKEN 2
+#define FL_DEV_ERR_RANGE 3 /* a prompt-path operand outside the fp16 range of its tensor-core GEMM */
 
 __device__ __forceinline__ uint32_t fl_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

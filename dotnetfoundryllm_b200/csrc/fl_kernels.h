@@ -198,15 +198,15 @@ cudaError_t fl_launch_token(const void* kernel, const FlTokenArgs& ta, int grid,
 
 /* ── the prompt path (fl_prefill.cu) ───────────────────────────────────── */
 #include <cuda_fp16.h>
-/* split-fp16 operands: [n x 3K] halves per matrix (see fl_prefill.cu) */
+/* split-fp16 operands: [n x 3K] per matrix, activations [lo | hi | hi], weights [hi | lo | hi] (see fl_prefill.cu) */
 #define FL_PF_WSCALE 256.0f
 cudaError_t fl_launch_dequant_split(int32_t type, const uint8_t* raw, int rows, int cols, __half* dst, cudaStream_t st,
-                                    int layout = 0); /* 0: [hi | hi | lo] rows, 1: [hi | lo] rows */
+                                    int layout = 0, int* err = nullptr); /* 0: [hi | lo | hi] rows, 1: [hi | lo] rows */
 cudaError_t fl_launch_embed_rows(int32_t type, const uint8_t* raw, const int32_t* tokens, int n, int h, int vocab,
                                  float* x, int* err, cudaStream_t st);
 cudaError_t fl_launch_rows_norm(float* x, const float* y, const float* post_w, const float* w, int n, int h, float eps,
                                 int gemma, __half* out, cudaStream_t st, int stack = 0,
-                                const float* y_lo = nullptr); /* y_lo: a second half added to y */
+                                const float* y_lo = nullptr, int* err = nullptr); /* y_lo: a second half added to y */
 cudaError_t fl_launch_rope_kv(const float* qkv, const float* bq, const float* bk, const float* bv, const float* rope_cs,
                               int start_pos, int n, int qd, int kvd, int hd, float* q_out, float* k_cache,
                               float* v_cache, cudaStream_t st);
@@ -217,7 +217,8 @@ cudaError_t fl_launch_rope_kv_rows(const float* qkv, const float* bq, const floa
                                    cudaStream_t st, const float* qkv_lo = nullptr);
 cudaError_t fl_launch_batch_attn(const float* q, const float* k_cache, const float* v_cache, const int* row_pos,
                                  const int* row_slot, size_t slot_stride, int B, int nh, int nkv, int hd, int window,
-                                 float scale, float softcap, __half* out, cudaStream_t st, int stack = 0);
+                                 float scale, float softcap, __half* out, cudaStream_t st, int stack = 0,
+                                 int* err = nullptr);
 cudaError_t fl_launch_softcap_rows(float* x, size_t n, float cap, cudaStream_t st);
 cudaError_t fl_launch_add_halves(const float* p, int B, int N, float* y, cudaStream_t st);
 cudaError_t fl_launch_argmax_rows(const float* x, int rows, int n, int* out, cudaStream_t st);
@@ -226,14 +227,16 @@ cudaError_t fl_launch_argmax_rows(const float* x, int rows, int n, int* out, cud
  * have raised their flag to epoch */
 cudaError_t fl_launch_tp_prefill_reduce(const float* const* slots, int* const* flags, int T, int rank, int epoch,
                                         size_t count, float* y, int* err, cudaStream_t st);
-cudaError_t fl_launch_attn_q_split(const float* q, int n, int nh, int nkv, int hd, __half* qs, cudaStream_t st);
+cudaError_t fl_launch_attn_q_split(const float* q, int n, int nh, int nkv, int hd, __half* qs, cudaStream_t st,
+                                   int* err = nullptr);
 cudaError_t fl_launch_attn_kv_split(const float* kc, const float* vc, int nk, int nkp, int kvd, int hd, __half* ks,
-                                    __half* vt, cudaStream_t st);
+                                    __half* vt, cudaStream_t st, int* err = nullptr);
 cudaError_t fl_launch_attn_softmax(const float* S, int rows, int n, int grp, int nkp, int start, int window, float scale,
                                    float softcap, __half* P, cudaStream_t st);
-cudaError_t fl_launch_attn_out(const float* O, int n, int nh, int nkv, int hd, __half* act, cudaStream_t st);
+cudaError_t fl_launch_attn_out(const float* O, int n, int nh, int nkv, int hd, __half* act, cudaStream_t st,
+                               int* err = nullptr);
 cudaError_t fl_launch_glu(const float* g, int n, int F, int gelu, __half* act, cudaStream_t st, int stack = 0,
-                          const float* g_lo = nullptr);
+                          const float* g_lo = nullptr, int* err = nullptr);
 
 /* ── the tcgen05 GEMM (fl_tc_gemm.cu) ──────────────────────────────────────
  * Y[b][n][m] = alpha * sum_k A[b][m][k] * B[b][n][k] (+ beta * Y[b][n][m]),

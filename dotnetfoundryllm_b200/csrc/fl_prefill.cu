@@ -6,11 +6,17 @@
  * The projections are dense contractions of the chunk's [n x K] activations
  * with the layer's weights, on the tcgen05 tensor cores (fl_tc_gemm.cu) in
  * split fp16 ("fp16x3"): every operand value v is stored as hi = fp16(v) and
- * lo = fp16(v - hi), and one GEMM over K' = 3K with rows [x_hi | x_lo | x_hi]
- * and [w_hi | w_hi | w_lo] sums x_hi*w_hi + x_lo*w_hi + x_hi*w_lo in fp32 —
+ * lo = fp16(v - hi), and one GEMM over K' = 3K with rows [x_lo | x_hi | x_hi]
+ * and [w_hi | w_lo | w_hi] sums x_lo*w_hi + x_hi*w_lo + x_hi*w_hi in fp32 —
  * close to fp32 products of the bit-exact dequantized weights (weights are
- * scaled by FL_PF_WSCALE first so their lo parts stay normal fp16).  These
- * kernels do the rest:
+ * scaled by FL_PF_WSCALE first so their lo parts stay normal fp16).  The two
+ * small cross terms come first: the tensor cores' fp32 accumulation keeps
+ * fewer bits of a term added to a larger running sum, so adding them before
+ * the hi*hi products, while the sum is small, keeps their bits (measured: 4x
+ * less error over K = 14336 than hi*hi first).  A value whose hi part
+ * overflows fp16 (|weight| > 65504 / FL_PF_WSCALE, |activation| > 65504) is
+ * reported (FL_DEV_ERR_RANGE) instead of stored as infinity.  These kernels do
+ * the rest:
  * embedding rows, the residual adds fused with the norms, bias + RoPE + K/V
  * append, causal attention over the KV cache, and the gated FFN activation.
  */
@@ -38,50 +44,60 @@ __device__ __forceinline__ float pf_gelu(float v)
     return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner)));
 }
 
-/* v into the split layout of its row: [hi | lo | hi] (activations) or
- * [hi | hi | lo] (weights), K values per part */
-__device__ __forceinline__ void store_split(__half* row3, int K, int c, float v, bool weight)
+/* A finite value whose fp16 hi part overflowed: recorded once (an earlier
+ * error of the launch is kept). */
+__device__ __forceinline__ void check_range(__half hi, float v, int* err)
+{
+    if (err && __hisinf(hi) && isfinite(v)) atomicCAS(err, 0, FL_DEV_ERR_RANGE);
+}
+
+/* v into the split layout of its row: [lo | hi | hi] (activations) or
+ * [hi | lo | hi] (weights), K values per part */
+__device__ __forceinline__ void store_split(__half* row3, int K, int c, float v, bool weight, int* err)
 {
     const __half hi = __float2half_rn(v);
     const __half lo = __float2half_rn(v - __half2float(hi));
-    row3[c] = hi;
-    row3[K + c] = weight ? hi : lo;
-    row3[2 * K + c] = weight ? lo : hi;
+    check_range(hi, v, err);
+    row3[c] = weight ? hi : lo;
+    row3[K + c] = weight ? lo : hi;
+    row3[2 * K + c] = hi;
 }
 
 /* An activation value of row r, column c (K per row): the split layout
- * [hi | lo | hi] (rows of 3K) when stack == 0; else stacked, hi in row r and
+ * [lo | hi | hi] (rows of 3K) when stack == 0; else stacked, hi in row r and
  * lo in row stack + r (rows of K), the input of the two-GEMM form. */
-__device__ __forceinline__ void store_act(__half* out, int K, int r, int c, float v, int stack)
+__device__ __forceinline__ void store_act(__half* out, int K, int r, int c, float v, int stack, int* err)
 {
     if (stack == 0) {
-        store_split(out + (size_t)r * 3 * K, K, c, v, false);
+        store_split(out + (size_t)r * 3 * K, K, c, v, false, err);
         return;
     }
     const __half hi = __float2half_rn(v);
+    check_range(hi, v, err);
     out[(size_t)r * K + c] = hi;
     out[(size_t)(stack + r) * K + c] = __float2half_rn(v - __half2float(hi));
 }
 
-/* A weight value: [hi | hi | lo] rows of 3K (layout 0) or [hi | lo] rows of 2K (layout 1). */
-__device__ __forceinline__ void store_weight(__half* dst, int64_t r, int K, int c, float v, int layout)
+/* A weight value: [hi | lo | hi] rows of 3K (layout 0) or [hi | lo] rows of 2K (layout 1). */
+__device__ __forceinline__ void store_weight(__half* dst, int64_t r, int K, int c, float v, int layout, int* err)
 {
     if (layout == 0) {
-        store_split(dst + r * 3 * K, K, c, v, true);
+        store_split(dst + r * 3 * K, K, c, v, true, err);
         return;
     }
     const __half hi = __float2half_rn(v);
+    check_range(hi, v, err);
     dst[r * 2 * K + c] = hi;
     dst[r * 2 * K + K + c] = __float2half_rn(v - __half2float(hi));
 }
 
 __global__ void dequant_split_kernel(int type, const uint8_t* __restrict__ raw, int64_t n, int cols,
-                                     __half* __restrict__ dst, int layout)
+                                     __half* __restrict__ dst, int layout, int* err)
 {
     for (int64_t f = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; f < n; f += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = f / cols;
         const int c = (int)(f - r * cols);
-        store_weight(dst, r, cols, c, fl_dequant_elem(type, raw, f) * FL_PF_WSCALE, layout);
+        store_weight(dst, r, cols, c, fl_dequant_elem(type, raw, f) * FL_PF_WSCALE, layout, err);
     }
 }
 
@@ -137,11 +153,11 @@ __device__ __forceinline__ void dequant8(const uint8_t* __restrict__ raw, int64_
     }
 }
 
-/* Weights in the split layout [hi | hi | lo] (scaled by FL_PF_WSCALE), 8
+/* Weights in the split layout [hi | lo | hi] (scaled by FL_PF_WSCALE), 8
  * values per thread, each part written as one 16-byte store. */
 template <int TYPE>
 __global__ void dequant_split8_kernel(const uint8_t* __restrict__ raw, int64_t n8, int cols, __half* __restrict__ dst,
-                                      int layout)
+                                      int layout, int* err)
 {
     for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < n8; g += (int64_t)gridDim.x * blockDim.x) {
         const int64_t f0 = g * 8;
@@ -155,13 +171,14 @@ __global__ void dequant_split8_kernel(const uint8_t* __restrict__ raw, int64_t n
             const float x = v[i] * FL_PF_WSCALE;
             hi[i] = __float2half_rn(x);
             lo[i] = __float2half_rn(x - __half2float(hi[i]));
+            check_range(hi[i], x, err);
         }
         const uint4 h4 = *reinterpret_cast<const uint4*>(hi), l4 = *reinterpret_cast<const uint4*>(lo);
         if (layout == 0) {
             __half* row3 = dst + r * 3 * (int64_t)cols;
             *reinterpret_cast<uint4*>(row3 + c) = h4;
-            *reinterpret_cast<uint4*>(row3 + cols + c) = h4;
-            *reinterpret_cast<uint4*>(row3 + 2 * cols + c) = l4;
+            *reinterpret_cast<uint4*>(row3 + cols + c) = l4;
+            *reinterpret_cast<uint4*>(row3 + 2 * cols + c) = h4;
         } else {
             __half* row2 = dst + r * 2 * (int64_t)cols;
             *reinterpret_cast<uint4*>(row2 + c) = h4;
@@ -199,7 +216,7 @@ __device__ float block_sum(float v, float* red)
  * then out = norm(x) * w as fp16 (RmsNorm, or GemmaRmsNorm with w + 1). */
 __global__ void rows_norm_kernel(float* __restrict__ x, const float* __restrict__ y, const float* __restrict__ post_w,
                                  const float* __restrict__ w, int h, float eps, int gemma, __half* __restrict__ out,
-                                 int stack, const float* __restrict__ y_lo)
+                                 int stack, const float* __restrict__ y_lo, int* err)
 {
     /* y_lo (the two-GEMM form's second half, or NULL) is part of y */
     __shared__ float red[32];
@@ -232,7 +249,7 @@ __global__ void rows_norm_kernel(float* __restrict__ x, const float* __restrict_
     const float rms = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, (float)h), eps));
     for (int i = threadIdx.x; i < h; i += blockDim.x) {
         const float wi = gemma ? __fadd_rn(w[i], 1.0f) : w[i];
-        store_act(out, h, r, i, __fmul_rn(__fmul_rn(xr[i], rms), wi), stack);
+        store_act(out, h, r, i, __fmul_rn(__fmul_rn(xr[i], rms), wi), stack, err);
     }
 }
 
@@ -298,7 +315,7 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(const float* __restrict
                                                         const int* __restrict__ row_pos,
                                                         const int* __restrict__ row_slot, size_t slot_stride, int nh,
                                                         int nkv, int window, float scale, float softcap,
-                                                        __half* __restrict__ out, int stack)
+                                                        __half* __restrict__ out, int stack, int* err)
 {
     constexpr int GM = HD == 256 ? 4 : 8, NWB = 8; /* GM: largest query-head group */
     constexpr int LPK = HD / 32, KPW = 32 / LPK, PER = HD / 32;
@@ -397,7 +414,7 @@ __global__ void __launch_bounds__(256) batch_attn_kernel(const float* __restrict
             O = fmaf(s_o[w][h][d], f, O);
             L = fmaf(s_ml[w][h][1], f, L);
         }
-        store_act(out, qd, b, (g * grp + h) * HD + d, L > 0.0f ? O / L : 0.0f, stack);
+        store_act(out, qd, b, (g * grp + h) * HD + d, L > 0.0f ? O / L : 0.0f, stack, err);
     }
 }
 
@@ -512,22 +529,23 @@ __global__ void tp_pf_reduce_kernel(TpSlots sl, int T, int epoch, size_t count, 
  * and the softmax; a second split-fp16 GEMM multiplies the probabilities
  * (times 2^10, so their lo parts stay normal) by the values. */
 
-/* Q rows into [hi | lo | hi] per head, grouped by kv head. */
-__global__ void attn_q_split_kernel(const float* __restrict__ q, int n, int nh, int nkv, int hd, __half* __restrict__ qs)
+/* Q rows into [lo | hi | hi] per head, grouped by kv head. */
+__global__ void attn_q_split_kernel(const float* __restrict__ q, int n, int nh, int nkv, int hd, __half* __restrict__ qs,
+                                    int* err)
 {
     const int t = blockIdx.x, qd = nh * hd, grp = nh / nkv;
     for (int i = threadIdx.x; i < qd; i += blockDim.x) {
         const int head = i / hd, d = i - head * hd, g = head / grp, h = head - g * grp;
         __half* row = qs + ((size_t)g * n * grp + (size_t)t * grp + h) * 3 * hd;
-        store_split(row, hd, d, q[(size_t)t * qd + i], false);
+        store_split(row, hd, d, q[(size_t)t * qd + i], false, err);
     }
 }
 
-/* Keys 0..nkp of every kv head into [hi | hi | lo] rows; values transposed,
- * one [hi | hi | lo] row of nkp keys per (kv head, dim); zero past nk.  A
+/* Keys 0..nkp of every kv head into [hi | lo | hi] rows; values transposed,
+ * one [hi | lo | hi] row of nkp keys per (kv head, dim); zero past nk.  A
  * 32-key x 32-dim tile per block, staged so both sides are coalesced. */
 __global__ void attn_kv_split_kernel(const float* __restrict__ kc, const float* __restrict__ vc, int nk, int nkp,
-                                     int kvd, int hd, __half* __restrict__ ks, __half* __restrict__ vt)
+                                     int kvd, int hd, __half* __restrict__ ks, __half* __restrict__ vt, int* err)
 {
     __shared__ float tile[32][33];
     const int k0 = blockIdx.x * 32, c0 = blockIdx.y * 32, tx = threadIdx.x, ty = threadIdx.y;
@@ -538,7 +556,7 @@ __global__ void attn_kv_split_kernel(const float* __restrict__ kc, const float* 
         const float vv = ok ? vc[(size_t)key * kvd + c] : 0.0f;
         if (key < nkp && c < kvd) {
             const int g = c / hd, d = c - g * hd;
-            store_split(ks + ((size_t)g * nkp + key) * 3 * hd, hd, d, kv, true);
+            store_split(ks + ((size_t)g * nkp + key) * 3 * hd, hd, d, kv, true, err);
         }
         tile[r][tx] = vv;
     }
@@ -547,7 +565,7 @@ __global__ void attn_kv_split_kernel(const float* __restrict__ kc, const float* 
         const int c = c0 + r, key = k0 + tx;
         if (c < kvd && key < nkp) {
             const int g = c / hd, d = c - g * hd;
-            store_split(vt + ((size_t)g * hd + d) * 3 * nkp, nkp, key, tile[tx][r], true);
+            store_split(vt + ((size_t)g * hd + d) * 3 * nkp, nkp, key, tile[tx][r], true, err);
         }
     }
 }
@@ -570,7 +588,7 @@ __device__ float attn_block_reduce(float v, bool is_max, float* red)
 
 /* Row (g, t, h): ComputeAttention's score (dot * scale [→ softcap]) over the
  * keys [max(0, p+1-window), p+1) of position p = start + t, then Softmax
- * (max, exp(s - max), sum, divide); written as 2^10 * p in [hi | lo | hi]. */
+ * (max, exp(s - max), sum, divide); written as 2^10 * p in [lo | hi | hi]. */
 template <bool STAGED>
 __global__ void attn_softmax_kernel(const float* __restrict__ S, int n, int grp, int nkp, int start, int window,
                                     float scale, float softcap, __half* __restrict__ P)
@@ -605,22 +623,23 @@ __global__ void attn_softmax_kernel(const float* __restrict__ S, int n, int grp,
     for (int k = threadIdx.x; k < nkp; k += blockDim.x) {
         float p = 0.0f;
         if (k >= k_lo && k <= k_hi) p = __fdiv_rn(STAGED ? srow_s[k] : expf(__fsub_rn(score(k), mx)), sum);
-        store_split(prow, nkp, k, p * 1024.0f, false);
+        store_split(prow, nkp, k, p * 1024.0f, false, nullptr); /* |2^10 p| <= 1024 */
     }
 }
 
 /* The attention output rows (g, t, h) into the Wo input layout [t][qd]. */
-__global__ void attn_out_kernel(const float* __restrict__ O, int n, int nh, int nkv, int hd, __half* __restrict__ act)
+__global__ void attn_out_kernel(const float* __restrict__ O, int n, int nh, int nkv, int hd, __half* __restrict__ act,
+                                int* err)
 {
     const int t = blockIdx.x, qd = nh * hd, grp = nh / nkv;
     for (int i = threadIdx.x; i < qd; i += blockDim.x) {
         const int head = i / hd, d = i - head * hd, g = head / grp, h = head - g * grp;
-        store_split(act + (size_t)t * 3 * qd, qd, i, O[((size_t)g * n * grp + (size_t)t * grp + h) * hd + d], false);
+        store_split(act + (size_t)t * 3 * qd, qd, i, O[((size_t)g * n * grp + (size_t)t * grp + h) * hd + d], false, err);
     }
 }
 
 __global__ void glu_kernel(const float* __restrict__ g, int n, int F, int gelu, __half* __restrict__ act, int stack,
-                           const float* __restrict__ g_lo)
+                           const float* __restrict__ g_lo, int* err)
 {
     const int64_t total = (int64_t)n * F;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -630,14 +649,14 @@ __global__ void glu_kernel(const float* __restrict__ g, int n, int F, int gelu, 
             gv = __fadd_rn(gv, g_lo[r * 2 * F + c]);
             up = __fadd_rn(up, g_lo[r * 2 * F + F + c]);
         }
-        store_act(act, F, (int)r, (int)c, __fmul_rn(gelu ? pf_gelu(gv) : pf_silu(gv), up), stack);
+        store_act(act, F, (int)r, (int)c, __fmul_rn(gelu ? pf_gelu(gv) : pf_silu(gv), up), stack, err);
     }
 }
 
 } // namespace
 
 cudaError_t fl_launch_dequant_split(int32_t type, const uint8_t* raw, int rows, int cols, __half* dst, cudaStream_t st,
-                                    int layout)
+                                    int layout, int* err)
 {
     const int64_t n = (int64_t)rows * cols;
     if (cols % 8 == 0) {
@@ -646,18 +665,18 @@ cudaError_t fl_launch_dequant_split(int32_t type, const uint8_t* raw, int rows, 
         if (b8 > 148 * 16) b8 = 148 * 16;
         if (b8 < 1) b8 = 1;
         switch (type) {
-        case FL_T_Q4_K: dequant_split8_kernel<FL_T_Q4_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
-        case FL_T_Q5_K: dequant_split8_kernel<FL_T_Q5_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
-        case FL_T_Q6_K: dequant_split8_kernel<FL_T_Q6_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
-        case FL_T_Q8_0: dequant_split8_kernel<FL_T_Q8_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
-        case FL_T_Q4_0: dequant_split8_kernel<FL_T_Q4_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout); return cudaGetLastError();
+        case FL_T_Q4_K: dequant_split8_kernel<FL_T_Q4_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout, err); return cudaGetLastError();
+        case FL_T_Q5_K: dequant_split8_kernel<FL_T_Q5_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout, err); return cudaGetLastError();
+        case FL_T_Q6_K: dequant_split8_kernel<FL_T_Q6_K><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout, err); return cudaGetLastError();
+        case FL_T_Q8_0: dequant_split8_kernel<FL_T_Q8_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout, err); return cudaGetLastError();
+        case FL_T_Q4_0: dequant_split8_kernel<FL_T_Q4_0><<<(unsigned)b8, 256, 0, st>>>(raw, n8, cols, dst, layout, err); return cudaGetLastError();
         default: break;
         }
     }
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 32) blocks = 148 * 32;
     if (blocks < 1) blocks = 1;
-    dequant_split_kernel<<<(unsigned)blocks, 256, 0, st>>>(type, raw, n, cols, dst, layout);
+    dequant_split_kernel<<<(unsigned)blocks, 256, 0, st>>>(type, raw, n, cols, dst, layout, err);
     return cudaGetLastError();
 }
 
@@ -669,9 +688,9 @@ cudaError_t fl_launch_embed_rows(int32_t type, const uint8_t* raw, const int32_t
 }
 
 cudaError_t fl_launch_rows_norm(float* x, const float* y, const float* post_w, const float* w, int n, int h, float eps,
-                                int gemma, __half* out, cudaStream_t st, int stack, const float* y_lo)
+                                int gemma, __half* out, cudaStream_t st, int stack, const float* y_lo, int* err)
 {
-    rows_norm_kernel<<<n, n < 148 ? 1024 : 256, 0, st>>>(x, y, post_w, w, h, eps, gemma, out, stack, y_lo);
+    rows_norm_kernel<<<n, n < 148 ? 1024 : 256, 0, st>>>(x, y, post_w, w, h, eps, gemma, out, stack, y_lo, err);
     return cudaGetLastError();
 }
 
@@ -696,13 +715,13 @@ cudaError_t fl_launch_rope_kv_rows(const float* qkv, const float* bq, const floa
 
 cudaError_t fl_launch_batch_attn(const float* q, const float* k_cache, const float* v_cache, const int* row_pos,
                                  const int* row_slot, size_t slot_stride, int B, int nh, int nkv, int hd, int window,
-                                 float scale, float softcap, __half* out, cudaStream_t st, int stack)
+                                 float scale, float softcap, __half* out, cudaStream_t st, int stack, int* err)
 {
     dim3 grid((unsigned)B, (unsigned)nkv);
     switch (hd) {
-    case 64: batch_attn_kernel<64><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out, stack); break;
-    case 128: batch_attn_kernel<128><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out, stack); break;
-    case 256: batch_attn_kernel<256><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out, stack); break;
+    case 64: batch_attn_kernel<64><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out, stack, err); break;
+    case 128: batch_attn_kernel<128><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out, stack, err); break;
+    case 256: batch_attn_kernel<256><<<grid, 256, 0, st>>>(q, k_cache, v_cache, row_pos, row_slot, slot_stride, nh, nkv, window, scale, softcap, out, stack, err); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -746,17 +765,17 @@ cudaError_t fl_launch_tp_prefill_reduce(const float* const* slots, int* const* f
     return cudaGetLastError();
 }
 
-cudaError_t fl_launch_attn_q_split(const float* q, int n, int nh, int nkv, int hd, __half* qs, cudaStream_t st)
+cudaError_t fl_launch_attn_q_split(const float* q, int n, int nh, int nkv, int hd, __half* qs, cudaStream_t st, int* err)
 {
-    attn_q_split_kernel<<<n, 256, 0, st>>>(q, n, nh, nkv, hd, qs);
+    attn_q_split_kernel<<<n, 256, 0, st>>>(q, n, nh, nkv, hd, qs, err);
     return cudaGetLastError();
 }
 
 cudaError_t fl_launch_attn_kv_split(const float* kc, const float* vc, int nk, int nkp, int kvd, int hd, __half* ks,
-                                    __half* vt, cudaStream_t st)
+                                    __half* vt, cudaStream_t st, int* err)
 {
     dim3 grid((unsigned)((nkp + 31) / 32), (unsigned)((kvd + 31) / 32));
-    attn_kv_split_kernel<<<grid, dim3(32, 8), 0, st>>>(kc, vc, nk, nkp, kvd, hd, ks, vt);
+    attn_kv_split_kernel<<<grid, dim3(32, 8), 0, st>>>(kc, vc, nk, nkp, kvd, hd, ks, vt, err);
     return cudaGetLastError();
 }
 
@@ -777,19 +796,19 @@ cudaError_t fl_launch_attn_softmax(const float* S, int rows, int n, int grp, int
     return cudaGetLastError();
 }
 
-cudaError_t fl_launch_attn_out(const float* O, int n, int nh, int nkv, int hd, __half* act, cudaStream_t st)
+cudaError_t fl_launch_attn_out(const float* O, int n, int nh, int nkv, int hd, __half* act, cudaStream_t st, int* err)
 {
-    attn_out_kernel<<<n, 256, 0, st>>>(O, n, nh, nkv, hd, act);
+    attn_out_kernel<<<n, 256, 0, st>>>(O, n, nh, nkv, hd, act, err);
     return cudaGetLastError();
 }
 
 cudaError_t fl_launch_glu(const float* g, int n, int F, int gelu, __half* act, cudaStream_t st, int stack,
-                          const float* g_lo)
+                          const float* g_lo, int* err)
 {
     const int64_t total = (int64_t)n * F;
     int64_t blocks = (total + 255) / 256;
     if (blocks > 148 * 32) blocks = 148 * 32;
     if (blocks < 1) blocks = 1;
-    glu_kernel<<<(unsigned)blocks, 256, 0, st>>>(g, n, F, gelu, act, stack, g_lo);
+    glu_kernel<<<(unsigned)blocks, 256, 0, st>>>(g, n, F, gelu, act, stack, g_lo, err);
     return cudaGetLastError();
 }

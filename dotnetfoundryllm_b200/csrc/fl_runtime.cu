@@ -1238,6 +1238,10 @@ static int check_device_err(fl_session* s)
     int32_t zero = 0;
     cudaMemcpy(s->state + ST_ERR, &zero, 4, cudaMemcpyHostToDevice);
     if (err == 1) return fail(FL_ERR_TIMEOUT, "a bounded device wait expired");
+    if (err == 3)
+        return fail(FL_ERR_UNSUPPORTED,
+                    "a value of the prompt path or batched step is outside the fp16 range of its tensor-core operands "
+                    "(|weight| > 255.9 or |activation| > 65504): feed these tokens through fl_forward");
     return fail(FL_ERR_ARG, "device reported error %d", err);
 }
 
@@ -1525,14 +1529,14 @@ static int pf_gemm(fl_session* s, const __half* W, const __half* X, float* Y, in
 /* split-fp16 weights of a raw matrix into dst (rows x 3*cols) */
 static int pf_dequant(fl_session* s, const RawMatrix& r, __half* dst)
 {
-    CK(fl_launch_dequant_split(r.type, r.d, r.rows, r.cols, dst, s->st));
+    CK(fl_launch_dequant_split(r.type, r.d, r.rows, r.cols, dst, s->st, 0, s->state + ST_ERR));
     return FL_OK;
 }
 
 /* the same as [hi | lo] rows (rows x 2*cols), the batched steps' layout */
 static int bt_dequant(fl_session* s, const RawMatrix& r, __half* dst)
 {
-    CK(fl_launch_dequant_split(r.type, r.d, r.rows, r.cols, dst, s->st, 1));
+    CK(fl_launch_dequant_split(r.type, r.d, r.rows, r.cols, dst, s->st, 1, s->state + ST_ERR));
     return FL_OK;
 }
 
@@ -1622,7 +1626,8 @@ static int pf_chunk(fl_session* s, int slot, const int32_t* tokens, int n, int s
         /* residual of the previous FFN (Gemma: its post-norm first), then the attention norm */
         const float* prev = l > 0 ? s->pf_y : nullptr;
         const float* prev_post = l > 0 && gemma ? m->layers[(size_t)l - 1].post_ffn_norm : nullptr;
-        CK(fl_launch_rows_norm(s->pf_x, prev, prev_post, L.attn_norm, n, h, eps, gemma, s->pf_act, s->st));
+        CK(fl_launch_rows_norm(s->pf_x, prev, prev_post, L.attn_norm, n, h, eps, gemma, s->pf_act, s->st, 0, nullptr,
+                               s->state + ST_ERR));
         /* q, k, v */
         if ((rc = pf_dequant(s, L.rq, s->pf_w))) return rc;
         if ((rc = pf_dequant(s, L.rk, s->pf_w + (size_t)qd * 3 * h))) return rc;
@@ -1638,8 +1643,8 @@ static int pf_chunk(fl_session* s, int slot, const int32_t* tokens, int n, int s
         if (l == d.n_layers - 1) break; /* the prompt's last-layer outputs feed nothing: only its K/V are kept */
         {
             const int nkv = m->nkv_l, grp = m->nh_l / nkv, nk = start + n, nkp = (nk + 7) & ~7, rows = n * grp;
-            CK(fl_launch_attn_q_split(s->pf_q, n, m->nh_l, nkv, hd, s->pf_qs, s->st));
-            CK(fl_launch_attn_kv_split(kc, vc, nk, nkp, kvd, hd, s->pf_ks, s->pf_vt, s->st));
+            CK(fl_launch_attn_q_split(s->pf_q, n, m->nh_l, nkv, hd, s->pf_qs, s->st, s->state + ST_ERR));
+            CK(fl_launch_attn_kv_split(kc, vc, nk, nkp, kvd, hd, s->pf_ks, s->pf_vt, s->st, s->state + ST_ERR));
             if ((rc = tc_gemm(s, s->pf_ks, s->pf_qs, s->pf_s, nkp, 3 * hd, rows, 1.0f, nkv, (int64_t)nkp * 3 * hd,
                               (int64_t)rows * 3 * hd, (int64_t)rows * nkp)))
                 return rc;
@@ -1648,19 +1653,19 @@ static int pf_chunk(fl_session* s, int slot, const int32_t* tokens, int n, int s
             if ((rc = tc_gemm(s, s->pf_vt, s->pf_p, s->pf_o, hd, 3 * nkp, rows, 1.0f / 1024.0f, nkv,
                               (int64_t)hd * 3 * nkp, (int64_t)rows * 3 * nkp, (int64_t)rows * hd)))
                 return rc;
-            CK(fl_launch_attn_out(s->pf_o, n, m->nh_l, nkv, hd, s->pf_act, s->st));
+            CK(fl_launch_attn_out(s->pf_o, n, m->nh_l, nkv, hd, s->pf_act, s->st, s->state + ST_ERR));
         }
         /* output projection, residual (Gemma: post-attention norm), FFN norm */
         if ((rc = pf_dequant(s, L.ro, s->pf_w))) return rc;
         if ((rc = pf_gemm(s, s->pf_w, s->pf_act, pf_partial(s), h, qd, n))) return rc;
         if ((rc = pf_allreduce(s, n))) return rc;
         CK(fl_launch_rows_norm(s->pf_x, s->pf_y, gemma ? L.post_attn_norm : nullptr, L.ffn_norm, n, h, eps, gemma,
-                               s->pf_act, s->st));
+                               s->pf_act, s->st, 0, nullptr, s->state + ST_ERR));
         /* gate and up stacked: columns [0, F) gate, [F, 2F) up */
         if ((rc = pf_dequant(s, L.rgate, s->pf_w))) return rc;
         if ((rc = pf_dequant(s, L.rup, s->pf_w + (size_t)F * 3 * h))) return rc;
         if ((rc = pf_gemm(s, s->pf_w, s->pf_act, s->pf_y, 2 * F, h, n))) return rc;
-        CK(fl_launch_glu(s->pf_y, n, F, gemma ? 1 : 0, s->pf_act, s->st));
+        CK(fl_launch_glu(s->pf_y, n, F, gemma ? 1 : 0, s->pf_act, s->st, 0, nullptr, s->state + ST_ERR));
         if ((rc = pf_dequant(s, L.rdown, s->pf_w))) return rc;
         if ((rc = pf_gemm(s, s->pf_w, s->pf_act, pf_partial(s), h, F, n))) return rc;
         if ((rc = pf_allreduce(s, n))) return rc;
@@ -1735,7 +1740,11 @@ static int prefill_impl(fl_session* s, int slot, const int32_t* tokens, int32_t 
     if (ms && !rc && cudaEventElapsedTime(ms, ev[0], ev[1]) != cudaSuccess) rc = fail(FL_ERR_CUDA, "cudaEventElapsedTime failed");
     for (cudaEvent_t e : ev)
         if (e) cudaEventDestroy(e);
-    if (rc) return rc;
+    if (rc) {
+        /* positions from start_pos on may hold a partial prompt: the cache keeps those before it */
+        slot_length(s, slot) = std::min(slot_length(s, slot), (int)start_pos);
+        return rc;
+    }
     slot_length(s, slot) = start_pos + n;
     return FL_OK;
 }
@@ -1873,7 +1882,8 @@ extern "C" int fl_forward_batch(fl_session* s, int32_t B, const int32_t* tokens,
         const float* prev = l > 0 ? s->bt_y2 : nullptr;
         const float* prev_lo = l > 0 ? s->bt_y2 + (size_t)B * h : nullptr;
         const float* prev_post = l > 0 && gemma ? m->layers[(size_t)l - 1].post_ffn_norm : nullptr;
-        CK(fl_launch_rows_norm(s->pf_x, prev, prev_post, L.attn_norm, B, h, eps, gemma, s->pf_act, s->st, stk, prev_lo));
+        CK(fl_launch_rows_norm(s->pf_x, prev, prev_post, L.attn_norm, B, h, eps, gemma, s->pf_act, s->st, stk, prev_lo,
+                               s->state + ST_ERR));
         const __half* w = cached ? cw[0] : s->pf_w;
         if (!cached && ((rc = bt_dequant(s, L.rq, s->pf_w)) || (rc = bt_dequant(s, L.rk, s->pf_w + (size_t)qd * 2 * h)) ||
                         (rc = bt_dequant(s, L.rv, s->pf_w + (size_t)(qd + kvd) * 2 * h))))
@@ -1888,24 +1898,25 @@ extern "C" int fl_forward_batch(fl_session* s, int32_t B, const int32_t* tokens,
         if (gemma && (l % 2) == 0) window = d.sliding_window; /* Gemma2ForwardPass.cs:87 */
         if (window <= 0) window = INT_MAX;
         CK(fl_launch_batch_attn(s->pf_q, kc, vc, s->bt_pos, s->bt_slot, s->slot_stride, B, m->nh_l, m->nkv_l, hd, window,
-                                d.attn_scale, gemma ? d.attn_softcap : 0.0f, s->pf_act, s->st, stk));
+                                d.attn_scale, gemma ? d.attn_softcap : 0.0f, s->pf_act, s->st, stk, s->state + ST_ERR));
         w = cached ? cw[1] : s->pf_w;
         if (!cached && (rc = bt_dequant(s, L.ro, s->pf_w))) return rc;
         if ((rc = bt_gemm(s, w, s->pf_act, nullptr, h, qd, B))) return rc;
         CK(fl_launch_rows_norm(s->pf_x, s->bt_y2, gemma ? L.post_attn_norm : nullptr, L.ffn_norm, B, h, eps, gemma,
-                               s->pf_act, s->st, stk, s->bt_y2 + (size_t)B * h));
+                               s->pf_act, s->st, stk, s->bt_y2 + (size_t)B * h, s->state + ST_ERR));
         w = cached ? cw[2] : s->pf_w;
         if (!cached && ((rc = bt_dequant(s, L.rgate, s->pf_w)) || (rc = bt_dequant(s, L.rup, s->pf_w + (size_t)F * 2 * h))))
             return rc;
         if ((rc = bt_gemm(s, w, s->pf_act, nullptr, 2 * F, h, B))) return rc;
-        CK(fl_launch_glu(s->bt_y2, B, F, gemma ? 1 : 0, s->pf_act, s->st, stk, s->bt_y2 + (size_t)B * 2 * F));
+        CK(fl_launch_glu(s->bt_y2, B, F, gemma ? 1 : 0, s->pf_act, s->st, stk, s->bt_y2 + (size_t)B * 2 * F,
+                         s->state + ST_ERR));
         w = cached ? cw[3] : s->pf_w;
         if (!cached && (rc = bt_dequant(s, L.rdown, s->pf_w))) return rc;
         if ((rc = bt_gemm(s, w, s->pf_act, nullptr, h, F, B))) return rc;
     }
     /* final norm (after the last residual) and the LM head */
     CK(fl_launch_rows_norm(s->pf_x, s->bt_y2, gemma ? m->layers.back().post_ffn_norm : nullptr, m->out_norm, B, h, eps,
-                           gemma, s->pf_act, s->st, stk, s->bt_y2 + (size_t)B * h));
+                           gemma, s->pf_act, s->st, stk, s->bt_y2 + (size_t)B * h, s->state + ST_ERR));
     const __half* wh = cached ? s->bt_w.back() : s->pf_w;
     if (!cached && (rc = bt_dequant(s, m->rout, s->pf_w))) return rc;
     if ((rc = bt_gemm(s, wh, s->pf_act, s->bt_logits, d.vocab, h, B))) return rc;
@@ -1948,7 +1959,8 @@ extern "C" int fl_dequant(int32_t type, const void* src, uint64_t nbytes, float*
 }
 
 /* Test hook (internal): the prefill's split-fp16 weight layout of a raw
- * matrix, rows x 3*cols halves ([hi | hi | lo] of value * FL_PF_WSCALE). */
+ * matrix, rows x 3*cols halves ([hi | lo | hi] of value * FL_PF_WSCALE; values
+ * past the fp16 range are written as they fall, without the range flag). */
 extern "C" int fl_dequant_split_test(int32_t type, const void* src, uint64_t nbytes, int32_t rows, int32_t cols,
                                      uint16_t* dst)
 {

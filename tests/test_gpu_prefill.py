@@ -105,7 +105,7 @@ def test_prefill_argument_errors(family):
 @pytest.mark.parametrize("t", [12, 13, 14, 8, 2])  # Q4_K, Q5_K, Q6_K, Q8_0, Q4_0
 def test_split_weights_are_the_exact_values(t):
     """The prefill's weight layout: every value bit-exactly dequantized, times
-    FL_PF_WSCALE, as fp16 hi and lo = fp16(v - hi), in [hi | hi | lo]."""
+    FL_PF_WSCALE, as fp16 hi and lo = fp16(v - hi), in [hi | lo | hi]."""
     import ctypes as C
     from dotnetfoundryllm_b200 import _native as N
     from oracle import oracle as O
@@ -120,10 +120,39 @@ def test_split_weights_are_the_exact_values(t):
         rc, v = O.dequantize(t, blob, rows * cols)
         assert rc == O.OK
         x = (v.astype(np.float32) * np.float32(256.0)).reshape(rows, cols)
-        hi = x.astype(np.float16)
-        lo = (x - hi.astype(np.float32)).astype(np.float16)
+        with np.errstate(over="ignore", invalid="ignore"):  # random bytes: values past the fp16 range
+            hi = x.astype(np.float16)
+            lo = (x - hi.astype(np.float32)).astype(np.float16)
         got = out.view(np.float16).reshape(rows, 3 * cols)
         finite = np.isfinite(x)
-        for part, want in ((0, hi), (1, hi), (2, lo)):
+        for part, want in ((0, hi), (1, lo), (2, hi)):
             g = got[:, part * cols:(part + 1) * cols]
             np.testing.assert_array_equal(g.view(np.uint16)[finite], want.view(np.uint16)[finite])
+
+
+def test_weight_past_the_fp16_range_is_reported_not_stored_as_infinity():
+    """The prompt path's tensor-core operands are fp16 (weights times
+    FL_PF_WSCALE = 256): a weight of magnitude > 255.9 cannot be represented.
+    fl_prefill reports it (FL_ERR_UNSUPPORTED, NotSupportedError) instead of
+    computing with infinities, the cache keeps only the positions before the
+    prompt, and the token loop (no such limit) runs the same tokens."""
+    from dotnetfoundryllm_b200 import gguf
+    img = model_image("tiny").copy()
+    g = gguf.parse(img)
+    t = g.find_tensor("blk.0.attn_q.weight")
+    assert t.type == 12  # Q4_K: f16 d at byte 0 of each 144-byte block
+    off = g.data_start + t.offset
+    img[off:off + 2] = np.frombuffer(np.float16(60000.0).tobytes(), np.uint8)  # d * scale * q >> 256
+    model = loader.load(img, max_ctx=64)
+    fwd = runtime.CudaForwardPass(model, max_ctx=64)
+    try:
+        kv = object()
+        with pytest.raises(runtime.NotSupportedError, match="fp16 range"):
+            fwd.prefill([1, 2, 3, 4], 0, kv)
+        with pytest.raises(runtime.ArgumentError):
+            fwd.forward(5, 4, kv)  # nothing of the refused prompt is cached
+        for i, tok in enumerate([1, 2, 3, 4]):
+            fwd.forward(tok, i, kv, want_logits=False)
+    finally:
+        fwd.close()
+        model.close()
