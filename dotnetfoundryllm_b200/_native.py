@@ -114,7 +114,8 @@ PUBLIC_API = [
     ("fl_dequant", C.c_int, [C.c_int32, C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64]),
     ("fl_matvec", C.c_int, [C.c_int32, C.c_void_p, C.c_uint64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
     ("fl_gemm_f16", C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_int32, C.c_int32, C.c_int32,
-                              C.c_int32, C.c_int32, C.c_int32, C.c_float, C.c_float, C.c_void_p]),
+                              C.c_int32, C.c_int32, C.c_int32, C.c_float, C.c_float, C.c_int32, C.c_int32,
+                              C.c_int32, C.c_int32, C.c_int32, C.c_void_p]),
     ("fl_profile_step", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("fl_time_decode", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_float)]),
     ("fl_time_prefill", C.c_int, [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.POINTER(C.c_float)]),

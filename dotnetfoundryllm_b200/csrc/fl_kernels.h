@@ -250,6 +250,17 @@ struct FlTcGemm {
     long long ldy, y_batch;
     float alpha, beta;
     int* err;
+    /* ksplit > 1: each output tile's K range in ksplit parts (more CTAs for
+     * few tiles); part holds ksplit * batch * N * M floats, summed in split
+     * order by a second kernel (deterministic) */
+    int ksplit = 1;
+    float* part = nullptr;
+    /* causal attention of a prompt chunk, B rows = c_grp query rows per token
+     * of tokens c_start..: 1 = A rows are keys, tiles past every key a B row
+     * may see are skipped (never written); 2 = K is c_seg segments of
+     * c_seglen keys (a multiple of 64), each cut to the keys a B row may see
+     * (the rest multiply zeros) */
+    int causal = 0, c_grp = 1, c_start = 0, c_seg = 0, c_seglen = 0;
 };
 cudaError_t fl_tc_gemm(const __half* A, long long lda, const __half* B, long long ldb, const FlTcGemm& p,
                        cudaStream_t st);

@@ -64,8 +64,8 @@ __device__ __forceinline__ void store_split(__half* row3, int K, int c, float v,
 }
 
 /* An activation value of row r, column c (K per row): the split layout
- * [lo | hi | hi] (rows of 3K) when stack == 0; else stacked, hi in row r and
- * lo in row stack + r (rows of K), the input of the two-GEMM form. */
+ * [lo | hi | hi] (rows of 3K) when stack == 0; else stacked for the batched
+ * steps' GEMM (rows of 2K): [hi | hi] in row r, [0 | lo] in row stack + r. */
 __device__ __forceinline__ void store_act(__half* out, int K, int r, int c, float v, int stack, int* err)
 {
     if (stack == 0) {
@@ -74,11 +74,15 @@ __device__ __forceinline__ void store_act(__half* out, int K, int r, int c, floa
     }
     const __half hi = __float2half_rn(v);
     check_range(hi, v, err);
-    out[(size_t)r * K + c] = hi;
-    out[(size_t)(stack + r) * K + c] = __float2half_rn(v - __half2float(hi));
+    __half* rh = out + (size_t)r * 2 * K;
+    __half* rl = out + (size_t)(stack + r) * 2 * K;
+    rh[c] = hi;
+    rh[K + c] = hi;
+    rl[c] = __float2half_rn(0.0f);
+    rl[K + c] = __float2half_rn(v - __half2float(hi));
 }
 
-/* A weight value: [hi | lo | hi] rows of 3K (layout 0) or [hi | lo] rows of 2K (layout 1). */
+/* A weight value: [hi | lo | hi] rows of 3K (layout 0) or [lo | hi] rows of 2K (layout 1). */
 __device__ __forceinline__ void store_weight(__half* dst, int64_t r, int K, int c, float v, int layout, int* err)
 {
     if (layout == 0) {
@@ -87,8 +91,8 @@ __device__ __forceinline__ void store_weight(__half* dst, int64_t r, int K, int 
     }
     const __half hi = __float2half_rn(v);
     check_range(hi, v, err);
-    dst[r * 2 * K + c] = hi;
-    dst[r * 2 * K + K + c] = __float2half_rn(v - __half2float(hi));
+    dst[r * 2 * K + c] = __float2half_rn(v - __half2float(hi));
+    dst[r * 2 * K + K + c] = hi;
 }
 
 __global__ void dequant_split_kernel(int type, const uint8_t* __restrict__ raw, int64_t n, int cols,
@@ -181,8 +185,8 @@ __global__ void dequant_split8_kernel(const uint8_t* __restrict__ raw, int64_t n
             *reinterpret_cast<uint4*>(row3 + 2 * cols + c) = h4;
         } else {
             __half* row2 = dst + r * 2 * (int64_t)cols;
-            *reinterpret_cast<uint4*>(row2 + c) = h4;
-            *reinterpret_cast<uint4*>(row2 + cols + c) = l4;
+            *reinterpret_cast<uint4*>(row2 + c) = l4;
+            *reinterpret_cast<uint4*>(row2 + cols + c) = h4;
         }
     }
 }

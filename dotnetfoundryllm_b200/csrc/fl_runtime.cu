@@ -166,7 +166,8 @@ struct fl_session {
      * (per layer qkv, wo, gate/up, down; then the LM head) */
     int32_t *bt_pos = nullptr, *bt_slot = nullptr, *bt_argmax = nullptr;
     float* bt_logits = nullptr;
-    float* bt_y2 = nullptr; /* [2 * slots][widest projection] partial halves of the two-GEMM form */
+    float* bt_y2 = nullptr; /* [2 * slots][widest projection] the two output halves of a batched projection */
+    float* bt_part = nullptr; /* K-split partial products of a batched projection */
     bool bt_cache_tried = false;
     std::vector<__half*> bt_w;
     /* attention of a chunk: split Q/K/V^T, scores, split probabilities, output */
@@ -1497,9 +1498,15 @@ extern "C" int fl_topk_device(const float* logits, int32_t n, int32_t k, int32_t
 /* Y[n x N] (fp32, row-major, ld N) = alpha * X[n x K] · W[N x K]^T + beta * Y
  * (fp16, row-major, leading dimensions ldw / ldx, default K) on the tcgen05
  * tensor cores (fl_tc_gemm), `batch` times with the given element strides. */
+struct TcOpts {
+    int ksplit = 1;
+    float* part = nullptr;
+    int causal = 0, c_grp = 1, c_start = 0, c_seg = 0, c_seglen = 0;
+};
+
 static int tc_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K, int n, float alpha,
                    int batch = 1, int64_t sW = 0, int64_t sX = 0, int64_t sY = 0, int ldw = 0, int ldx = 0,
-                   float beta = 0.0f)
+                   float beta = 0.0f, const TcOpts& o = TcOpts())
 {
     if (!ldw) ldw = K;
     if (!ldx) ldx = K;
@@ -1517,6 +1524,13 @@ static int tc_gemm(fl_session* s, const __half* W, const __half* X, float* Y, in
     p.alpha = alpha;
     p.beta = beta;
     p.err = s->state + ST_ERR;
+    p.ksplit = o.ksplit;
+    p.part = o.part;
+    p.causal = o.causal;
+    p.c_grp = o.c_grp;
+    p.c_start = o.c_start;
+    p.c_seg = o.c_seg;
+    p.c_seglen = o.c_seglen;
     CK(fl_tc_gemm(W, ldw, X, ldx, p, s->st));
     return FL_OK;
 }
@@ -1533,7 +1547,7 @@ static int pf_dequant(fl_session* s, const RawMatrix& r, __half* dst)
     return FL_OK;
 }
 
-/* the same as [hi | lo] rows (rows x 2*cols), the batched steps' layout */
+/* the same as [lo | hi] rows (rows x 2*cols), the batched steps' layout */
 static int bt_dequant(fl_session* s, const RawMatrix& r, __half* dst)
 {
     CK(fl_launch_dequant_split(r.type, r.d, r.rows, r.cols, dst, s->st, 1, s->state + ST_ERR));
@@ -1547,7 +1561,7 @@ static int pf_alloc(fl_session* s)
     const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, F = m->ffn_l;
     /* scores and split probabilities take 10 bytes per (query head, key) of
      * a chunk row: the chunk shrinks so they stay within 4 GiB */
-    const int nkmax = (s->max_ctx + 7) & ~7;
+    const int nkmax = (s->max_ctx + 63) & ~63;
     const size_t per_tok = (size_t)m->nh_l * nkmax * 10;
     int cap = std::min(s->max_ctx, 2048);
     if ((size_t)cap * per_tok > ((size_t)4 << 30)) cap = std::max(16, (int)((((size_t)4 << 30) / per_tok) & ~(size_t)15));
@@ -1642,16 +1656,27 @@ static int pf_chunk(fl_session* s, int slot, const int32_t* tokens, int n, int s
         if (window <= 0) window = INT_MAX;
         if (l == d.n_layers - 1) break; /* the prompt's last-layer outputs feed nothing: only its K/V are kept */
         {
-            const int nkv = m->nkv_l, grp = m->nh_l / nkv, nk = start + n, nkp = (nk + 7) & ~7, rows = n * grp;
+            /* keys padded to a multiple of 64: the PV product cuts each of its
+             * three K segments to the keys a query row may see */
+            const int nkv = m->nkv_l, grp = m->nh_l / nkv, nk = start + n, nkp = (nk + 63) & ~63, rows = n * grp;
+            TcOpts qk, pv;
+            qk.causal = 1;
+            qk.c_grp = grp;
+            qk.c_start = start;
+            pv.causal = 2;
+            pv.c_grp = grp;
+            pv.c_start = start;
+            pv.c_seg = 3;
+            pv.c_seglen = nkp;
             CK(fl_launch_attn_q_split(s->pf_q, n, m->nh_l, nkv, hd, s->pf_qs, s->st, s->state + ST_ERR));
             CK(fl_launch_attn_kv_split(kc, vc, nk, nkp, kvd, hd, s->pf_ks, s->pf_vt, s->st, s->state + ST_ERR));
             if ((rc = tc_gemm(s, s->pf_ks, s->pf_qs, s->pf_s, nkp, 3 * hd, rows, 1.0f, nkv, (int64_t)nkp * 3 * hd,
-                              (int64_t)rows * 3 * hd, (int64_t)rows * nkp)))
+                              (int64_t)rows * 3 * hd, (int64_t)rows * nkp, 0, 0, 0.0f, qk)))
                 return rc;
             CK(fl_launch_attn_softmax(s->pf_s, nkv * rows, n, grp, nkp, start, window, d.attn_scale,
                                       gemma ? d.attn_softcap : 0.0f, s->pf_p, s->st));
             if ((rc = tc_gemm(s, s->pf_vt, s->pf_p, s->pf_o, hd, 3 * nkp, rows, 1.0f / 1024.0f, nkv,
-                              (int64_t)hd * 3 * nkp, (int64_t)rows * 3 * nkp, (int64_t)rows * hd)))
+                              (int64_t)hd * 3 * nkp, (int64_t)rows * 3 * nkp, (int64_t)rows * hd, 0, 0, 0.0f, pv)))
                 return rc;
             CK(fl_launch_attn_out(s->pf_o, n, m->nh_l, nkv, hd, s->pf_act, s->st, s->state + ST_ERR));
         }
@@ -1768,7 +1793,7 @@ extern "C" int fl_time_prefill(fl_session* s, const int32_t* tokens, int32_t n, 
 /* ── batched decode ─────────────────────────────────────────────────────── */
 
 /* The split-fp16 weights of every projection and of the LM head, kept for
- * the session's batched steps as [hi | lo] rows: 4 bytes per weight (8B:
+ * the session's batched steps as [lo | hi] rows: 4 bytes per weight (8B:
  * ~30 GB), tried once; without them each step dequantizes into the prompt
  * path's buffer. */
 static void bt_cache_weights(fl_session* s)
@@ -1814,15 +1839,27 @@ static void bt_cache_weights(fl_session* s)
     if (bt_dequant(s, m->rout, s->bt_w.back())) s->bt_w.clear();
 }
 
-/* Y[B x N] = X · W^T in the two-GEMM form: X stacked ([B hi rows; B lo
- * rows] of K), W as [hi | lo] rows of 2K (scaled by FL_PF_WSCALE); the hi
- * weights meet both activation halves in one GEMM, the lo weights the hi
- * half in a second accumulating into the first B rows, then the halves add.
- * Every weight byte is read once. */
+/* K splits of a batched projection with mt weight-row tiles and nkb 64-wide
+ * k-blocks: enough work items for two per SM, at least 8 k-blocks each. */
+static int bt_ksplit(int mt, int nkb)
+{
+    int ks = (2 * 148 + mt - 1) / mt;
+    ks = std::min(ks, std::max(1, nkb / 8));
+    return std::max(1, std::min(ks, 16));
+}
+
+/* Y[B x N] = X · W^T for the batched steps, one GEMM over K' = 2K: W as
+ * [lo | hi] rows (scaled by FL_PF_WSCALE), X as 2B rows, [hi | hi] for
+ * sequence b and [0 | lo] for row B + b.  Rows b get lo*hi + hi*hi (the small
+ * term accumulated first), rows B + b get hi*lo; the consumers add the two
+ * halves as they read.  Every weight byte is read once, the K range split
+ * across CTAs when the weight rows alone make too few work items. */
 static int bt_gemm(fl_session* s, const __half* W, const __half* X, float* Y, int N, int K, int B)
 {
-    int rc = tc_gemm(s, W, X, s->bt_y2, N, K, 2 * B, 1.0f / FL_PF_WSCALE, 1, 0, 0, 0, 2 * K, K);
-    if (!rc) rc = tc_gemm(s, W + K, X, s->bt_y2, N, K, B, 1.0f / FL_PF_WSCALE, 1, 0, 0, 0, 2 * K, K, 1.0f);
+    TcOpts o;
+    o.ksplit = bt_ksplit((N + 127) / 128, (2 * K + 63) / 64);
+    o.part = s->bt_part;
+    int rc = tc_gemm(s, W, X, s->bt_y2, N, 2 * K, 2 * B, 1.0f / FL_PF_WSCALE, 1, 0, 0, 0, 2 * K, 2 * K, 0.0f, o);
     if (rc) return rc;
     if (Y) CK(fl_launch_add_halves(s->bt_y2, B, N, Y, s->st));
     return FL_OK;
@@ -1853,7 +1890,8 @@ extern "C" int fl_forward_batch(fl_session* s, int32_t B, const int32_t* tokens,
     if (cudaSetDevice(d.device) != cudaSuccess) return fail(FL_ERR_CUDA, "cudaSetDevice failed");
     int rc = FL_OK;
     if (!s->pf_cap && (rc = pf_alloc(s))) return rc;
-    if (B > s->pf_cap) return fail(FL_ERR_UNSUPPORTED, "batch %d above the prompt path's %d rows", B, s->pf_cap);
+    if (4 * B > 3 * s->pf_cap) /* 2B stacked rows of 2K halves in the prompt path's buffer of cap rows of 3K */
+        return fail(FL_ERR_UNSUPPORTED, "batch %d above %d rows (3/4 of the prompt path's)", B, 3 * s->pf_cap / 4);
     const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, F = m->ffn_l, hd = d.head_dim;
     if (!s->bt_pos) {
         const int S = s->n_slots;
@@ -1863,12 +1901,18 @@ extern "C" int fl_forward_batch(fl_session* s, int32_t B, const int32_t* tokens,
             (rc = dalloc(s->allocs, &s->bt_logits, (size_t)S * d.vocab * 4)) ||
             (rc = dalloc(s->allocs, &s->bt_y2, (size_t)2 * S * widest * 4)))
             return rc;
+        /* the largest K-split partial buffer of any projection */
+        size_t part = 0;
+        const int shapes[5][2] = {{qd + 2 * kvd, h}, {h, qd}, {2 * F, h}, {h, F}, {d.vocab, h}};
+        for (auto& sh : shapes)
+            part = std::max(part, (size_t)bt_ksplit((sh[0] + 127) / 128, (2 * sh[1] + 63) / 64) * 2 * S * sh[0]);
+        if ((rc = dalloc(s->allocs, &s->bt_part, part * 4))) return rc;
     }
     if (!s->bt_cache_tried) bt_cache_weights(s);
     const bool cached = !s->bt_w.empty();
     const bool gemma = d.arch == FL_ARCH_GEMMA2;
     const float eps = gemma ? 1e-6f : d.rms_eps;
-    /* activations are stacked for the two-GEMM form: B hi rows, then B lo rows */
+    /* activations are stacked for bt_gemm: B [hi | hi] rows, then B [0 | lo] rows */
     const int stk = B;
     CK(cudaMemcpyAsync(s->pf_tokens, tokens, (size_t)B * 4, cudaMemcpyHostToDevice, s->st));
     CK(cudaMemcpyAsync(s->bt_pos, positions, (size_t)B * 4, cudaMemcpyHostToDevice, s->st));
@@ -1983,13 +2027,17 @@ extern "C" int fl_dequant_split_test(int32_t type, const void* src, uint64_t nby
 }
 
 extern "C" int fl_gemm_f16(const void* a, int64_t lda, const void* b, int64_t ldb, int32_t M, int32_t N, int32_t K,
-                           int32_t batch, int32_t a_batch_rows, int32_t b_batch_rows, float alpha, float beta, float* y)
+                           int32_t batch, int32_t a_batch_rows, int32_t b_batch_rows, float alpha, float beta,
+                           int32_t ksplit, int32_t causal, int32_t c_grp, int32_t c_start, int32_t c_seg, float* y)
 {
     if (!a || !b || !y) return fail(FL_ERR_ARG, "null argument");
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || lda < K || ldb < K || (lda % 8) || (ldb % 8))
         return fail(FL_ERR_ARG, "bad GEMM shape (M %d, N %d, K %d, lda %lld, ldb %lld: strides multiples of 8)", M, N,
                     K, (long long)lda, (long long)ldb);
     if (batch > 1 && (a_batch_rows < M || b_batch_rows < N)) return fail(FL_ERR_ARG, "batch rows below M / N");
+    if (ksplit < 1 || ksplit > 64 || causal < 0 || causal > 2 || (ksplit > 1 && causal) || (causal && c_grp < 1) ||
+        (causal == 2 && (c_seg < 1 || K % c_seg || (K / c_seg) % 64)))
+        return fail(FL_ERR_ARG, "bad split / causal arguments");
     const long long arows = batch > 1 ? (long long)batch * a_batch_rows : M;
     const long long brows = batch > 1 ? (long long)batch * b_batch_rows : N;
     const size_t ab = (size_t)arows * lda * 2, bb = (size_t)brows * ldb * 2, yb = (size_t)batch * N * M * 4;
@@ -1997,10 +2045,12 @@ extern "C" int fl_gemm_f16(const void* a, int64_t lda, const void* b, int64_t ld
     __half *da = nullptr, *db = nullptr;
     float* dy = nullptr;
     int* derr = nullptr;
+    float* dpart = nullptr;
     int rc = dalloc(al, &da, ab);
     if (!rc) rc = dalloc(al, &db, bb);
     if (!rc) rc = dalloc(al, &dy, yb);
     if (!rc) rc = dalloc(al, &derr, 16);
+    if (!rc && ksplit > 1) rc = dalloc(al, &dpart, yb * (size_t)ksplit);
     cudaError_t e = cudaSuccess;
     if (!rc) {
         e = cudaMemcpy(da, a, ab, cudaMemcpyHostToDevice);
@@ -2021,6 +2071,13 @@ extern "C" int fl_gemm_f16(const void* a, int64_t lda, const void* b, int64_t ld
             p.alpha = alpha;
             p.beta = beta;
             p.err = derr;
+            p.ksplit = ksplit;
+            p.part = dpart;
+            p.causal = causal;
+            p.c_grp = c_grp;
+            p.c_start = c_start;
+            p.c_seg = c_seg;
+            p.c_seglen = causal == 2 ? K / c_seg : 0;
             e = fl_tc_gemm(da, lda, db, ldb, p, 0);
         }
         if (e == cudaSuccess) e = cudaDeviceSynchronize();

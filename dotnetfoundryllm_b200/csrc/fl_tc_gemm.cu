@@ -33,6 +33,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <algorithm>
+
 #include "fl_device.cuh"
 #include "fl_kernels.h"
 
@@ -123,12 +125,59 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32])
 struct TcArgs {
     int M, N, K, batch;            /* per batch: M weight rows, N tokens, K */
     int a_batch_rows, b_batch_rows; /* rows of A / B between batches in the 2-D maps */
-    int mt, nt;                    /* tiles per batch along M and N */
+    int mt, nt, ks;                /* tiles per batch along M and N; K splits */
     float* Y;
     long long ldy, y_batch;        /* Y row stride and batch stride (elements) */
     float alpha, beta;
+    float* part;                   /* ks > 1: [ks][batch][N][M] partial products */
+    int causal, c_grp, c_start, c_seg, c_seglen; /* see FlTcGemm */
     int* err;
 };
+
+/* The output tile of work item t (split s fastest, then token tiles, then
+ * weight-row tiles, then batches) and its k-blocks: k-block i of the tile is
+ * global k-block kb_of(i), i < count.  Causal mode 1 gives a count of 0 to a
+ * tile whose A rows (keys) all lie past the last key any of its B rows (query
+ * rows of tokens start..) may attend to; mode 2 keeps, of each of the c_seg
+ * segments of c_seglen columns of K, the columns (keys) below that bound. */
+struct TileWork {
+    int b, m0, n0, s;
+    int count, kb_lo, per_seg, seg_kb;
+    __device__ __forceinline__ int kb_of(int i) const
+    {
+        return per_seg ? (i / per_seg) * seg_kb + (i % per_seg) : kb_lo + i;
+    }
+};
+
+template <int BN>
+__device__ __forceinline__ TileWork tile_work(const TcArgs& g, int t, int nkb)
+{
+    TileWork w;
+    w.s = t % g.ks;
+    const int r0 = t / g.ks;
+    w.b = r0 / (g.mt * g.nt);
+    const int r = r0 % (g.mt * g.nt);
+    w.m0 = (r / g.nt) * BM;
+    w.n0 = (r % g.nt) * BN;
+    w.kb_lo = (int)((long long)nkb * w.s / g.ks);
+    w.count = (int)((long long)nkb * (w.s + 1) / g.ks) - w.kb_lo;
+    w.per_seg = 0;
+    w.seg_kb = 0;
+    if (g.causal) {
+        const int last_row = min(g.N, w.n0 + BN) - 1;
+        const int kbound = g.c_start + last_row / g.c_grp + 1; /* keys [0, kbound) */
+        if (g.causal == 1) {
+            if (w.m0 >= kbound) w.count = 0;
+        } else {
+            const int kmax = min(g.c_seglen, kbound);
+            w.seg_kb = g.c_seglen / BK;
+            w.per_seg = (kmax + BK - 1) / BK;
+            w.count = w.per_seg * g.c_seg;
+            w.kb_lo = 0;
+        }
+    }
+    return w;
+}
 
 /* Bounded wait on an mbarrier phase; false (and the CTA's abort flag and the
  * launch's error set) once ~2 s passed or another role of the CTA gave up. */
@@ -171,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     volatile int* consumed = reinterpret_cast<volatile int*>(tmem_holder + 2); /* k-blocks the MMA lane took */
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tiles = g.batch * g.mt * g.nt;
+    const int tiles = g.batch * g.mt * g.nt * g.ks;
     const int nkb = (g.K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
@@ -206,10 +255,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const int b = t / (g.mt * g.nt), r = t % (g.mt * g.nt);
-                const int arow = b * g.a_batch_rows + (r / g.nt) * BM;
-                const int brow = b * g.b_batch_rows + (r % g.nt) * BN;
-                for (int kb = 0; kb < nkb; kb++, issued++) {
+                const TileWork w = tile_work<BN>(g, t, nkb);
+                const int arow = w.b * g.a_batch_rows + w.m0;
+                const int brow = w.b * g.b_batch_rows + w.n0;
+                for (int i = 0; i < w.count; i++, issued++) {
+                    const int kb = w.kb_of(i);
                     const int s = issued % C::STAGES;
                     if (issued >= C::STAGES && !tc_wait(&empty[s], ((issued / C::STAGES) - 1) & 1, abort, g.err)) {
                         ok = false;
@@ -227,7 +277,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc = idesc_f16<BN>();
             bool ok = true;
             int kcount = 0, local = 0;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, local++) {
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const TileWork w = tile_work<BN>(g, t, nkb);
+                if (w.count == 0) continue; /* no MMA, no epilogue */
                 const int acc = local & 1;
                 if (local >= 2 && !tc_wait(&tempty[acc], ((local >> 1) - 1) & 1, abort, g.err)) {
                     ok = false;
@@ -235,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-                for (int kb = 0; kb < nkb; kb++, kcount++) {
+                for (int i = 0; i < w.count; i++, kcount++) {
                     const int s = kcount % C::STAGES;
                     if (!tc_wait(&full[s], (kcount / C::STAGES) & 1, abort, g.err)) {
                         ok = false;
@@ -246,12 +298,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t da = umma_desc_sw128(sa), db = umma_desc_sw128(sa + C::A_BYTES);
 #pragma unroll
                     for (int k = 0; k < BK / 16; k++) /* K 16 = 32 bytes: +2 in 16-byte units */
-                        umma_f16(d, da + 2 * k, db + 2 * k, idesc, (kb | k) != 0);
+                        umma_f16(d, da + 2 * k, db + 2 * k, idesc, (i | k) != 0);
                     umma_commit(&empty[s]);
                     *consumed = kcount + 1;
                 }
                 if (!ok) break;
                 umma_commit(&tfull[acc]);
+                local++;
             }
             /* every MMA issued has completed before the tensor memory is freed */
             umma_commit(done);
@@ -262,14 +315,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         /* epilogue: warps 2..5 own TMEM lanes 32*(warp % 4) .. +31 */
         const int q = warp & 3;
         int local = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, local++) {
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            const TileWork w = tile_work<BN>(g, t, nkb);
+            if (w.count == 0) continue;
             const int acc = local & 1;
             if (!tc_wait(&tfull[acc], (local >> 1) & 1, abort, g.err)) break;
+            local++;
             tc_fence_after();
-            const int b = t / (g.mt * g.nt), r = t % (g.mt * g.nt);
-            const int m = (r / g.nt) * BM + q * 32 + lane;
-            const int n0 = (r % g.nt) * BN;
-            float* yb = g.Y + (long long)b * g.y_batch;
+            const int m = w.m0 + q * 32 + lane;
+            const int n0 = w.n0;
+            /* a K split writes its raw partial; the reduction applies alpha, beta */
+            const bool split = g.ks > 1;
+            float* yb = split ? g.part + ((long long)w.s * g.batch + w.b) * g.N * (long long)g.M
+                              : g.Y + (long long)w.b * g.y_batch;
+            const long long ldy = split ? g.M : g.ldy;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; c++) {
                 uint32_t v[32];
@@ -279,10 +338,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 32; j++) {
                         const int n = n0 + c * 32 + j;
                         if (n < g.N) {
-                            float* p = yb + (long long)n * g.ldy + m;
-                            float o = g.alpha * __uint_as_float(v[j]);
-                            if (g.beta != 0.0f) o = fmaf(g.beta, *p, o);
-                            *p = o;
+                            float* p = yb + (long long)n * ldy + m;
+                            if (split) {
+                                *p = __uint_as_float(v[j]);
+                            } else {
+                                float o = g.alpha * __uint_as_float(v[j]);
+                                if (g.beta != 0.0f) o = fmaf(g.beta, *p, o);
+                                *p = o;
+                            }
                         }
                     }
                 }
@@ -307,6 +370,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C::TMEM_COLS)
                      : "memory");
+    }
+}
+
+/* Y = alpha * (sum of the K splits' partials, in split order) + beta * Y. */
+__global__ void split_reduce_kernel(const float* __restrict__ part, int ks, int batch, int N, int M, float* Y,
+                                    long long ldy, long long y_batch, float alpha, float beta)
+{
+    const long long per = (long long)N * M, count = per * batch;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < count; i += (long long)gridDim.x * blockDim.x) {
+        float sum = part[i];
+        for (int s = 1; s < ks; s++) sum += part[(long long)s * count + i];
+        const long long b = i / per, r = i % per, n = r / M, m = r % M;
+        float* p = Y + b * y_batch + n * ldy + m;
+        float o = alpha * sum;
+        if (beta != 0.0f) o = fmaf(beta, *p, o);
+        *p = o;
     }
 }
 
@@ -375,20 +454,33 @@ cudaError_t launch(const __half* A, long long lda, const __half* B, long long ld
     g.b_batch_rows = p.b_batch_rows;
     g.mt = (p.M + BM - 1) / BM;
     g.nt = (p.N + BN - 1) / BN;
+    g.ks = p.ksplit > 1 ? p.ksplit : 1;
     g.Y = p.Y;
     g.ldy = p.ldy;
     g.y_batch = p.y_batch;
     g.alpha = p.alpha;
     g.beta = p.beta;
+    g.part = p.part;
+    g.causal = p.causal;
+    g.c_grp = p.c_grp > 0 ? p.c_grp : 1;
+    g.c_start = p.c_start;
+    g.c_seg = p.c_seg;
+    g.c_seglen = p.c_seglen;
     g.err = p.err;
     CUtensorMap ma, mb;
     const long long arows = p.batch > 1 ? (long long)p.batch * p.a_batch_rows : p.M;
     const long long brows = p.batch > 1 ? (long long)p.batch * p.b_batch_rows : p.N;
     if ((e = make_map(&ma, A, arows, p.K, lda, BM)) != cudaSuccess) return e;
     if ((e = make_map(&mb, B, brows, p.K, ldb, BN)) != cudaSuccess) return e;
-    const long long tiles = (long long)g.batch * g.mt * g.nt;
+    const long long tiles = (long long)g.batch * g.mt * g.nt * g.ks;
     const int grid = (int)(tiles < g_sm_count[dev] ? tiles : g_sm_count[dev]);
     fl_tc_gemm_kernel<BN><<<grid, kThreads, C::SMEM, st>>>(ma, mb, g);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || g.ks == 1) return e;
+    const long long count = (long long)g.batch * g.N * g.M;
+    const long long blocks = std::min<long long>((count + 255) / 256, (long long)g_sm_count[dev] * 8);
+    split_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(g.part, g.ks, g.batch, g.N, g.M, g.Y, g.ldy, g.y_batch,
+                                                           g.alpha, g.beta);
     return cudaGetLastError();
 }
 
@@ -404,6 +496,8 @@ cudaError_t fl_tc_gemm(const __half* A, long long lda, const __half* B, long lon
 {
     if (p.M <= 0 || p.N <= 0 || p.K <= 0 || p.batch <= 0 || !p.Y) return cudaErrorInvalidValue;
     if (p.batch > 1 && (p.a_batch_rows < p.M || p.b_batch_rows < p.N)) return cudaErrorInvalidValue;
+    if (p.ksplit > 1 && (!p.part || p.causal)) return cudaErrorInvalidValue;
+    if (p.causal == 2 && (p.c_seglen % BK || (long long)p.c_seg * p.c_seglen != p.K)) return cudaErrorInvalidValue;
     /* the token tile: as wide as the token count needs, at most 256 */
     if (p.N > 128) return launch<256>(A, lda, B, ldb, p, st);
     if (p.N > 64) return launch<128>(A, lda, B, ldb, p, st);

@@ -427,15 +427,18 @@ def matvec(ggml_type: int, raw: np.ndarray, rows: int, cols: int, x: np.ndarray)
 
 
 def gemm_f16(a: np.ndarray, b: np.ndarray, m: int, n: int, k: int, alpha: float = 1.0, beta: float = 0.0,
-             y: np.ndarray | None = None, batch: int = 1, a_batch_rows: int = 0, b_batch_rows: int = 0) -> np.ndarray:
+             y: np.ndarray | None = None, batch: int = 1, a_batch_rows: int = 0, b_batch_rows: int = 0,
+             ksplit: int = 1, causal: int = 0, c_grp: int = 1, c_start: int = 0, c_seg: int = 0) -> np.ndarray:
     """fl_gemm_f16: y[b][j][i] = alpha * a[b][i] . b[b][j] (+ beta * y) on the
     tensor cores for i < m, j < n over k; a and b are float16 arrays whose
-    last axis is the row stride (k of it used)."""
+    last axis is the row stride (k of it used).  ksplit / causal as the C
+    hook documents."""
     a = np.ascontiguousarray(a, dtype=np.float16)
     b = np.ascontiguousarray(b, dtype=np.float16)
     y = np.zeros((batch, n, m), np.float32) if y is None else np.ascontiguousarray(y, dtype=np.float32).copy()
     check(N.cuda().fl_gemm_f16(_ptr(a), a.shape[-1], _ptr(b), b.shape[-1], m, n, k, batch, a_batch_rows,
-                               b_batch_rows, alpha, beta, _ptr(y)), "fl_gemm_f16")
+                               b_batch_rows, alpha, beta, ksplit, causal, c_grp, c_start, c_seg, _ptr(y)),
+          "fl_gemm_f16")
     return y
 
 

@@ -277,9 +277,16 @@ int fl_matvec(int32_t ggml_type, const void* w, uint64_t nbytes, int32_t rows, i
  * for each batch b < batch, y[b][n][m] = alpha * sum_k a[b][m][k] * b[b][n][k]
  * + beta * y[b][n][m], with a (fp16 bits) holding batch * a_batch_rows rows
  * of lda elements (M rows when batch is 1), b likewise, y dense
- * [batch][N][M] fp32.  lda and ldb are multiples of 8. */
+ * [batch][N][M] fp32.  lda and ldb are multiples of 8.
+ * ksplit > 1: each output tile's K range split over ksplit work items, their
+ * partials summed in split order.  causal (the prompt path's attention, with
+ * c_grp B rows per token of tokens c_start..): 1 = a[m] are keys and y[n][m]
+ * is left unwritten for every key past the last one token n / c_grp's tile
+ * may see (keys 0..c_start + that token); 2 = K is c_seg segments, each cut
+ * to those keys (a multiple of 64 long). */
 int fl_gemm_f16(const void* a, int64_t lda, const void* b, int64_t ldb, int32_t M, int32_t N, int32_t K,
-                int32_t batch, int32_t a_batch_rows, int32_t b_batch_rows, float alpha, float beta, float* y);
+                int32_t batch, int32_t a_batch_rows, int32_t b_batch_rows, float alpha, float beta, int32_t ksplit,
+                int32_t causal, int32_t c_grp, int32_t c_start, int32_t c_seg, float* y);
 
 /* Timing helpers for the benchmark/* Timing helpers for the benchmark: runs one token step and reads the
  * device timestamps the token kernel takes at every phase boundary; fills
