@@ -356,11 +356,31 @@ __device__ __forceinline__ float gelu_ref(float v)
     return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, tanhf(inner)));
 }
 
+/* The operand an epilogue reads from memory for lane r's row of a tile: the
+ * residual row (FL_EPI_RESID) or the RoPE (cos, sin) pair of a q or k row
+ * (FL_EPI_QKV).  A warp loads it for its first and last tile before their
+ * units, so the epilogue does not wait on memory after them. */
+__device__ __forceinline__ float2 epilogue_operand(const FlMvArgs& a, int tile, int lane, int pos)
+{
+    const int si = seg_of(a, tile);
+    const FlMvSeg& sg = a.seg[si];
+    const int row_local = (tile - sg.tile0) * 16 + (lane & 15);
+    if (lane >= 16 || row_local >= sg.rows) return make_float2(0.0f, 0.0f);
+    if (a.epi == FL_EPI_RESID) return make_float2(__ldcg(a.y + sg.tile0 * 16 + row_local), 0.0f);
+    if (a.epi == FL_EPI_QKV && si < 2) {
+        const int d = row_local % a.head_dim, half = a.head_dim >> 1;
+        return *reinterpret_cast<const float2*>(a.rope_cs + ((size_t)pos * half + (d >> 1)) * 2);
+    }
+    return make_float2(0.0f, 0.0f);
+}
+
 /* Runs in the warp that completed the tile; lane r < 16 holds row r in v.
- * All 32 lanes call it (shuffles). */
+ * All 32 lanes call it (shuffles).  With has_pre, `pre` is the tile's
+ * epilogue_operand. */
 template <int EPI>
 __device__ __forceinline__ void epilogue(const FlMvArgs& a, const FlMvSeg& sg, int si, int tile, int lane, float v,
-                                         int pos, float& best_v, int& best_i)
+                                         int pos, float& best_v, int& best_i, float2 pre = make_float2(0.0f, 0.0f),
+                                         bool has_pre = false)
 {
     const int r = lane & 15;
     const bool act = lane < 16;
@@ -370,7 +390,7 @@ __device__ __forceinline__ void epilogue(const FlMvArgs& a, const FlMvSeg& sg, i
         if (in_seg) {
             const int row = sg.tile0 * 16 + row_local;
             if (EPI == FL_EPI_STORE) a.y[row] = sg.bias ? __fadd_rn(v, sg.bias[row_local]) : v;
-            else a.y[row] = __fadd_rn(__ldcg(a.y + row), v);
+            else a.y[row] = __fadd_rn(has_pre ? pre.x : __ldcg(a.y + row), v);
         }
     } else if constexpr (EPI == FL_EPI_QKV) {
         if (sg.bias && in_seg) v = __fadd_rn(v, sg.bias[row_local]);
@@ -380,7 +400,7 @@ __device__ __forceinline__ void epilogue(const FlMvArgs& a, const FlMvSeg& sg, i
                 /* TensorOperations.ApplyRope (TensorOperations.cs:250-260) with the
                  * host-computed cos/sin of pos*invFreq[i] */
                 const int d = row_local % a.head_dim, i = d >> 1, half = a.head_dim >> 1;
-                const float2 cs = *reinterpret_cast<const float2*>(a.rope_cs + ((size_t)pos * half + i) * 2);
+                const float2 cs = has_pre ? pre : *reinterpret_cast<const float2*>(a.rope_cs + ((size_t)pos * half + i) * 2);
                 float o;
                 if ((d & 1) == 0) o = __fsub_rn(__fmul_rn(v, cs.x), __fmul_rn(partner, cs.y));
                 else o = __fadd_rn(__fmul_rn(partner, cs.y), __fmul_rn(v, cs.x));
@@ -448,12 +468,13 @@ __device__ __forceinline__ void wait_slot(volatile int* done, int gen, int* err)
 
 /* Runtime-dispatched epilogue (the persistent kernel mixes epilogues). */
 __device__ __forceinline__ void epilogue_any(const FlMvArgs& a, const FlMvSeg& sg, int si, int tile, int lane, float v,
-                                             int pos, float& best_v, int& best_i)
+                                             int pos, float& best_v, int& best_i,
+                                             float2 pre = make_float2(0.0f, 0.0f), bool has_pre = false)
 {
     switch (a.epi) {
     case FL_EPI_STORE: epilogue<FL_EPI_STORE>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
-    case FL_EPI_RESID: epilogue<FL_EPI_RESID>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
-    case FL_EPI_QKV: epilogue<FL_EPI_QKV>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
+    case FL_EPI_RESID: epilogue<FL_EPI_RESID>(a, sg, si, tile, lane, v, pos, best_v, best_i, pre, has_pre); break;
+    case FL_EPI_QKV: epilogue<FL_EPI_QKV>(a, sg, si, tile, lane, v, pos, best_v, best_i, pre, has_pre); break;
     case FL_EPI_GLU: epilogue<FL_EPI_GLU>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     default: epilogue<FL_EPI_LOGITS>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
     }

@@ -839,7 +839,14 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         const int Uph = my_tiles_of(a) * n_kb;
         const Split S{Uph / NW, Uph % NW};
         const int lo = S.lo(warp), hi = lo + S.len(warp);
-        const int first_it = lo / n_kb;
+        const int first_it = lo / n_kb, last_it = hi > lo ? (hi - 1) / n_kb : first_it;
+        /* the epilogue operands of the range's first and last tile, loaded now */
+        const bool has_pre = hi > lo && (a.epi == FL_EPI_RESID || a.epi == FL_EPI_QKV);
+        float2 pre0 = make_float2(0.0f, 0.0f), pre1 = pre0;
+        if (has_pre) {
+            pre0 = epilogue_operand(a, (int)blockIdx.x + first_it * G, lane, pos);
+            pre1 = epilogue_operand(a, (int)blockIdx.x + last_it * G, lane, pos);
+        }
         UnitStats st{0, 0, 0};
         bool pushed = false; /* this thread stored epilogue rows (to peers, with tensor parallelism) */
         if (ta.detail && blockIdx.x == 0 && tid == 0) ta.detail[(size_t)ta.n_phases * NW * 4 + p] = fl_globaltimer();
@@ -855,7 +862,11 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
             const int c = i1 - i0, kb0 = i0 - it * n_kb;
             Acc A{0.0f, 0.0f, 0.0f, 0.0f};
 #define FL_RUN(F, E) run_units<F, E>(ta, R, f, cslot, cpar, c, kb0, bptr, bval, zero, xs, xsum, lane, warp, A, st)
-            if (sg.expanded) {
+            if (!sg.expanded && sg.fmt == FL_FMT_Q4K) {
+                FL_RUN(FL_FMT_Q4K, false);
+            } else if (!sg.expanded && sg.fmt == FL_FMT_Q6K) {
+                FL_RUN(FL_FMT_Q6K, false);
+            } else if (sg.expanded) {
                 switch (sg.fmt) {
                 case FL_FMT_Q4K: FL_RUN(FL_FMT_Q4K, true); break;
                 case FL_FMT_Q5K: FL_RUN(FL_FMT_Q5K, true); break;
@@ -864,9 +875,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                 }
             } else {
                 switch (sg.fmt) {
-                case FL_FMT_Q4K: FL_RUN(FL_FMT_Q4K, false); break;
                 case FL_FMT_Q5K: FL_RUN(FL_FMT_Q5K, false); break;
-                case FL_FMT_Q6K: FL_RUN(FL_FMT_Q6K, false); break;
                 case FL_FMT_Q8_0: FL_RUN(FL_FMT_Q8_0, false); break;
                 case FL_FMT_Q4_0: FL_RUN(FL_FMT_Q4_0, false); break;
                 default: FL_RUN(FL_FMT_Q8K, false); break;
@@ -909,7 +918,8 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                 }
                 if (lane == 0) tcnt[it] = 0;
             }
-            epilogue_any(a, sg, si, tile, lane, v, pos, best_v, best_i);
+            epilogue_any(a, sg, si, tile, lane, v, pos, best_v, best_i, it == first_it ? pre0 : pre1,
+                         has_pre && (it == first_it || it == last_it));
             pushed |= lane < 16;
         }
         if (ta.detail && blockIdx.x == 0 && lane == 0) {
