@@ -80,3 +80,36 @@ def test_largest_size_with_ties_matches_numpy():
             ids, vals = _topk_device(d_logits, n, k)
             np.testing.assert_array_equal(ids, order)
             np.testing.assert_array_equal(vals, lg[order])
+
+
+@pytest.mark.gpu
+def test_flat_logits_at_the_largest_size_are_fast_and_in_index_order():
+    """All n logits equal: every key ties with the k-th, so the selection is
+    the first k indices.  The kernel takes the ties in index order with one
+    block scan (no pairwise ranking), so this finishes in milliseconds even
+    for k = n."""
+    import time
+
+    import torch
+    n = N.FL_TOPK_DEVICE_MAX_N
+    d_logits = torch.full((n,), 0.25, dtype=torch.float32, device="cuda:0")
+    for k in (1, 40, 4096, n):
+        _topk_device(d_logits, n, k)  # warm
+        t0 = time.perf_counter()
+        ids, vals = _topk_device(d_logits, n, k)
+        dt = time.perf_counter() - t0
+        np.testing.assert_array_equal(ids, np.arange(k))
+        assert (vals == np.float32(0.25)).all()
+        assert dt < 0.25, f"k={k}: {dt * 1e3:.1f} ms"
+
+
+@pytest.mark.gpu
+def test_signed_zeros_tie_and_go_by_index():
+    """-0.0 and +0.0 compare equal (the reference's float compares), so among
+    zeros the lower index comes first whatever the sign."""
+    import torch
+    lg = np.array([-0.0, 1.0, 0.0, -0.0, 0.0, -1.0, 0.0, -0.0], dtype=np.float32)
+    d_logits = torch.from_numpy(lg).to("cuda:0")
+    ids, vals = _topk_device(d_logits, lg.size, 6)
+    np.testing.assert_array_equal(ids, [1, 0, 2, 3, 4, 6])
+    np.testing.assert_array_equal(vals.view(np.uint32), lg[[1, 0, 2, 3, 4, 6]].view(np.uint32))
