@@ -489,12 +489,15 @@ def run_ours(args, ws, rank, local):
         tf = ROOT / "profiles" / "traffic.json"
         if tf.exists() and not args.layers and args.prompt == PROMPT:
             tj = json.loads(tf.read_text())
-            if CONFIG in tj:
-                # the captured launch's traffic/algorithmic ratio applied to this launch's bytes
-                # (a tensor-parallel rank's bytes are its shard)
+            if CONFIG in tj and not tp:
+                # dram__bytes of one full launch of this workload, measured by ncu (profiles/)
+                traffic = int(tj[CONFIG])
+                traffic_note = (f"ncu dram__bytes_read + write of one full 32-layer launch at position "
+                                f"{tj['position']} ({tj['ratio']:.4f} x its algorithmic bytes)")
+            elif CONFIG in tj:
+                # a rank streams its shard: the measured ratio applied to the rank's bytes
                 traffic = int(step_bytes * tj["ratio"])
-                traffic_note = ("ncu traffic/algorithmic ratio of the 4-layer capture x this launch's bytes"
-                                + (" (per rank)" if tp else ""))
+                traffic_note = "measured full-launch traffic/algorithmic ratio x this rank's bytes (per rank)"
         result = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
