@@ -61,29 +61,44 @@ struct Prolog {
 
 /* Lane l encodes word (c = l>>2, t = l&3) of k-block kb — the input values
  * kb*256 + 8l .. kb*256 + 8l + 7, given in v — into 3 limbs (B-fragment
- * order), the limb sums of its half-chunk and the float half sums. */
+ * order), the limb sums of its half-chunk and the float half sums.
+ *
+ * y = v * inv (|y| <= 127) is rounded once to the 2^-14 grid, Y = rint(y *
+ * 2^14) (one FMA against the 1.5 * 2^23 rounding constant; |Y| < 2^22), and
+ * Y is cut into X0 * 2^14 + X1 * 2^7 + X2 with X0 in [-127, 127], X1 in
+ * [-64, 64], X2 in [-64, 63]: y = X0 + X1/128 + X2/16384 within 2^-15, in
+ * integer operations. */
 __device__ __forceinline__ void encode_values(const float (&v)[8], int kb, float inv, int lane, uint8_t* xl, short2* xs,
                                               float* xsum)
 {
     const int c = lane >> 2, t = lane & 3;
     const int cg = kb * 8 + c;
-    uint32_t lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
-    int sl[3] = {0, 0, 0};
+    const float inv14 = inv * 16384.0f; /* exact: a power-of-two scale */
+    int X[3][8];
     float hs = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         hs += v[i];
-        float y = __fmul_rn(v[i], inv);
+        const int Y = __float_as_int(fmaf(v[i], inv14, kMagic)) - __float_as_int(kMagic);
+        const int x0 = (Y + 8192) >> 14;
+        const int r = Y - (x0 << 14);
+        const int x1 = (r + 64) >> 7;
+        X[0][i] = x0;
+        X[1][i] = x1;
+        X[2][i] = r - (x1 << 7);
+    }
+    uint32_t lo[3], hi[3];
+    int sl[3];
 #pragma unroll
-        for (int l = 0; l < 3; l++) {
-            const float tq = __fadd_rn(y, kMagic);
-            const float q = __fsub_rn(tq, kMagic);
-            const uint32_t byte = __float_as_uint(tq) & 0xFFu;
-            sl[l] += (int)(int8_t)byte;
-            if (i & 1) hi[l] |= byte << (8 * (i >> 1));
-            else lo[l] |= byte << (8 * (i >> 1));
-            y = __fmul_rn(__fsub_rn(y, q), 128.0f);
-        }
+    for (int l = 0; l < 3; l++) {
+        /* even values into lo, odd into hi, byte k = value 2k (+1) */
+        const uint32_t e01 = __byte_perm((uint32_t)X[l][0], (uint32_t)X[l][2], 0x0040u);
+        const uint32_t e23 = __byte_perm((uint32_t)X[l][4], (uint32_t)X[l][6], 0x0040u);
+        const uint32_t o01 = __byte_perm((uint32_t)X[l][1], (uint32_t)X[l][3], 0x0040u);
+        const uint32_t o23 = __byte_perm((uint32_t)X[l][5], (uint32_t)X[l][7], 0x0040u);
+        lo[l] = __byte_perm(e01, e23, 0x5410u);
+        hi[l] = __byte_perm(o01, o23, 0x5410u);
+        sl[l] = __dp4a((int)lo[l], 0x01010101, __dp4a((int)hi[l], 0x01010101, 0));
     }
 #pragma unroll
     for (int l = 0; l < 3; l++)

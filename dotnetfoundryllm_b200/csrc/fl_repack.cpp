@@ -266,15 +266,17 @@ extern "C" int fl_emulate_matvec(const fl_matrix_layout* L, const uint8_t* packe
     float inv = amax > 0.0f ? 127.0f / amax : 0.0f;
     std::vector<int> X[3];
     for (auto& v : X) v.assign((size_t)K, 0);
+    const float inv14 = inv * 16384.0f;
     for (int i = 0; i < K; i++) {
-        float y0 = xp[i] * inv;
-        float x0 = rintf(y0);
-        float y1 = (y0 - x0) * 128.0f;
-        float x1 = rintf(y1);
-        float y2 = (y1 - x1) * 128.0f;
-        X[0][i] = (int)x0;
-        X[1][i] = (int)x1;
-        X[2][i] = (int)rintf(y2);
+        /* Y = rint(x * inv * 2^14) in one rounding (the device's FMA against
+         * 1.5 * 2^23), cut into X0 * 2^14 + X1 * 2^7 + X2 */
+        const int Y = (int)std::nearbyint((double)xp[i] * (double)inv14);
+        const int x0 = (Y + 8192) >> 14;
+        const int r = Y - x0 * 16384;
+        const int x1 = (r + 64) >> 7;
+        X[0][i] = x0;
+        X[1][i] = x1;
+        X[2][i] = r - x1 * 128;
     }
     std::vector<float> sx((size_t)K / 16, 0.0f);
     for (int i = 0; i < K / 16; i++) {

@@ -254,7 +254,7 @@ __device__ __forceinline__ void load_row_smem(const float* p, float (&v)[PER])
  * ComputeAttention: LlamaForwardPass.cs:158-211; MistralForwardPass.cs:186-240;
  * Gemma2ForwardPass.cs:126-185. */
 template <int HD, int GMAX>
-__device__ void phase_attn_t(const FlAttnArgs& a, float* scr, uint64_t* stamps)
+__device__ void phase_attn_t(const FlAttnArgs& a, int pos, float* scr, uint64_t* stamps)
 {
     /* profiling: CTA 0 records the end of each step of its first item */
 #define FL_STAMP(i) \
@@ -268,7 +268,7 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr, uint64_t* stamps)
     float* sq = scr;                   /* [grp][HD] */
     float* sacc = sq + grp * HD;       /* [NW][grp][HD] */
     float* sml = sacc + NW * grp * HD; /* [NW][GMAX][2] running (max, sum) */
-    const int seq = __ldcg(a.pos) + 1;
+    const int seq = pos + 1;
     int start = 0;
     if (a.window < seq) start = seq - a.window;
     const int per = (seq - start + a.n_split - 1) / a.n_split;
@@ -297,23 +297,23 @@ __device__ void phase_attn_t(const FlAttnArgs& a, float* scr, uint64_t* stamps)
             float sc[GMAX];
 #pragma unroll
             for (int h = 0; h < GMAX; h++) sc[h] = 0.0f;
+            float4 kv[8]; /* this lane's 8 float4 of key base + kj */
             {
                 const float4* kr = reinterpret_cast<const float4*>(kbase + (size_t)min(base + kj, n - 1) * kv_dim);
-                float4 kv[8];
 #pragma unroll
                 for (int c = 0; c < 8; c++) kv[c] = __ldcg(kr + c * LPK + qd);
-#pragma unroll
-                for (int c = 0; c < 8; c++)
-#pragma unroll
-                    for (int h = 0; h < GMAX; h++) {
-                        if (h >= grp) break;
-                        const float4 q4 = reinterpret_cast<const float4*>(sq + h * HD)[c * LPK + qd];
-                        sc[h] = fmaf(q4.x, kv[c].x, sc[h]);
-                        sc[h] = fmaf(q4.y, kv[c].y, sc[h]);
-                        sc[h] = fmaf(q4.z, kv[c].z, sc[h]);
-                        sc[h] = fmaf(q4.w, kv[c].w, sc[h]);
-                    }
             }
+#pragma unroll
+            for (int c = 0; c < 8; c++)
+#pragma unroll
+                for (int h = 0; h < GMAX; h++) {
+                    if (h >= grp) break;
+                    const float4 q4 = reinterpret_cast<const float4*>(sq + h * HD)[c * LPK + qd];
+                    sc[h] = fmaf(q4.x, kv[c].x, sc[h]);
+                    sc[h] = fmaf(q4.y, kv[c].y, sc[h]);
+                    sc[h] = fmaf(q4.z, kv[c].z, sc[h]);
+                    sc[h] = fmaf(q4.w, kv[c].w, sc[h]);
+                }
             float vv[KPW][PER]; /* this lane's dims of the round's values */
 #pragma unroll
             for (int j = 0; j < KPW; j++) load_row<PER>(vbase + (size_t)min(base + j, n - 1) * kv_dim, vv[j]);
@@ -462,9 +462,8 @@ __device__ void phase_attn_combine(const FlAttnArgs& a, float* scr)
  * (every position before the current one; the current row is written by the
  * QKV phase), so that the attention phase reads them from L2.  Same item
  * split as phase_attn_t. */
-__device__ void prefetch_attn_kv(const FlAttnArgs& a)
+__device__ void prefetch_attn_kv(const FlAttnArgs& a, int pos)
 {
-    const int pos = __ldcg(a.pos);
     const int seq = pos + 1;
     int start = 0;
     if (a.window < seq) start = seq - a.window;
@@ -523,6 +522,19 @@ __device__ void phase_tp_reduce(const FlTokenArgs& ta, const FlTpArgs& r, int ep
             sum += fl_ld_relaxed_sys(reinterpret_cast<const float*>(ta.tp_peer[q] + off) + (size_t)q * ta.tp_recv_n + i);
         r.y[i] = r.mode ? sum : __fadd_rn(__ldcg(r.y + i), sum);
     }
+}
+
+/* L2 prefetch of a matvec phase's norm weights (and Gemma's pending
+ * post-norm weights), whole 16-byte granules. */
+__device__ void prefetch_prologue(const FlPhase& ph)
+{
+    if (ph.kind != FL_PH_MATVEC) return;
+    const FlMvArgs& a = ph.mv;
+    if (a.in_mode == FL_IN_PLAIN) return;
+    const uint32_t bytes = (uint32_t)((a.K * 4 + 15) & ~15);
+    if (a.norm_w && (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0) fl_prefetch_l2(a.norm_w, bytes);
+    if (a.in_mode == FL_IN_GEMMA_RESID && a.pend_w && (reinterpret_cast<uintptr_t>(a.pend_w) & 15) == 0)
+        fl_prefetch_l2(a.pend_w, bytes);
 }
 
 /* A warp's private weight ring: S slots of slot_bytes with one full barrier
@@ -684,6 +696,14 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
     float best_v = 0.0f;
     int best_i = 0x7fffffff;
     const int tp_epoch0 = ta.tp_size > 1 ? __ldcg(ta.tp_epoch) : 0;
+    /* the step's position: every phase of the launch uses the same one (the
+     * device-resident loop advances it only after the last phase) */
+    const int pos0 = __ldcg(ta.pos);
+    /* The warp's k-blocks of a matvec input are kb = warp + r*NW; lane l
+     * encodes inputs kb*256 + 8l .. +8.  With up to RK k-blocks per warp every
+     * input load of the prologue is issued at once and the values stay in
+     * registers until they are encoded. */
+    constexpr int RK = 4;
     for (int p = 0; p < ta.n_phases; p++) {
         const int kind = ta.phases[p].kind;
         /* this phase's arguments into the buffer phase p-2 used (every warp
@@ -691,12 +711,17 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         uint8_t* abuf = smem + Ls.args + (size_t)(p & 1) * Ls.args_stride;
         if (kind == FL_PH_MATVEC) {
             copy_words(abuf, &ta.phases[p].mv, sizeof(FlMvArgs));
-            if (p + 1 < ta.n_phases && ta.phases[p + 1].kind == FL_PH_ATTN) prefetch_attn_kv(ta.phases[p + 1].at);
+            if (p + 1 < ta.n_phases && ta.phases[p + 1].kind == FL_PH_ATTN) prefetch_attn_kv(ta.phases[p + 1].at, pos0);
         } else if (kind == FL_PH_ATTN || kind == FL_PH_ATTN_COMBINE) {
             copy_words(abuf, &ta.phases[p].at, sizeof(FlAttnArgs));
         } else if (kind == FL_PH_TP_REDUCE) {
             copy_words(abuf, &ta.phases[p].tp, sizeof(FlTpArgs));
         }
+        /* The next matvec phase's static prologue operands (norm weights) do
+         * not depend on the step's data: one CTA asks L2 for them a phase
+         * early, so that the prologue after the barrier finds them there
+         * instead of waiting on HBM behind the weight stream. */
+        if (p + 1 < ta.n_phases && tid == 0 && (int)blockIdx.x == (p * 7) % G) prefetch_prologue(ta.phases[p + 1]);
         if (p > 0) grid_sync(ta.bar, p * G, ta.err, ta.cta_done ? ta.cta_done + (size_t)(p - 1) * G + blockIdx.x : nullptr);
         else consumer_sync();
         if (ta.timestamps && blockIdx.x == 0 && tid == 0) ta.timestamps[p] = fl_globaltimer();
@@ -705,7 +730,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
             continue;
         }
         if (kind == FL_PH_ATTN) {
-            phase_attn_t<HD, GMAX>(*reinterpret_cast<const FlAttnArgs*>(abuf), reinterpret_cast<float*>(scratch),
+            phase_attn_t<HD, GMAX>(*reinterpret_cast<const FlAttnArgs*>(abuf), pos0, reinterpret_cast<float*>(scratch),
                                    ta.detail && blockIdx.x == 0 ? ta.detail + (size_t)p * NW * 4 : nullptr);
             continue;
         }
@@ -725,11 +750,6 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         short2* xs = reinterpret_cast<short2*>(scratch + nc * FL_XENC_LIMB_BYTES);
         float* xsum = reinterpret_cast<float*>(scratch + nc * (FL_XENC_LIMB_BYTES + FL_XENC_LSUM_BYTES));
         Prolog P{a.in_mode, a.K, a.x, a.norm_w, a.pend, a.pend_w, 1.0f, 1.0f};
-        /* The warp's k-blocks are kb = warp + r*NW; lane l encodes inputs
-         * kb*256 + 8l .. +8.  With up to RK k-blocks per warp every input load
-         * of the prologue is issued at once and the values stay in registers
-         * until they are encoded. */
-        constexpr int RK = 4;
         const bool in_regs = n_kb <= RK * NW;
         float amax;
         if (in_regs) {
@@ -831,7 +851,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         }
         const float xscale = amax / 127.0f;
         consumer_sync();
-        const int pos = a.epi == FL_EPI_QKV ? __ldcg(a.pos) : 0;
+        const int pos = pos0;
         const int limb = g & 3;
         const bool bval = (limb < 3) && ((g >> 2) == (t >> 1));
         const uint8_t* bptr = xl + (limb * 4 + t) * 8;

@@ -288,7 +288,7 @@ int fl_gemm_f16(const void* a, int64_t lda, const void* b, int64_t ldb, int32_t 
                 int32_t batch, int32_t a_batch_rows, int32_t b_batch_rows, float alpha, float beta, int32_t ksplit,
                 int32_t causal, int32_t c_grp, int32_t c_start, int32_t c_seg, float* y);
 
-/* Timing helpers for the benchmark/* Timing helpers for the benchmark: runs one token step and reads the
+/* Timing helpers for the benchmark: runs one token step and reads the
  * device timestamps the token kernel takes at every phase boundary; fills
  * ms[class] (time spent in phases of that class) and bytes[class]
  * (algorithmic bytes) for the FL_PROF_* classes, and *launches with the
