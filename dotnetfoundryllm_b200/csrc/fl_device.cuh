@@ -123,6 +123,15 @@ __device__ __forceinline__ float fl_ld_relaxed_sys(const float* p)
     return v;
 }
 
+/* Two 8-byte words, each read atomically, through L2 every time (polling
+ * words another CTA or GPU writes with single 8-byte stores). */
+__device__ __forceinline__ ulonglong2 fl_ld_volatile_u64x2(const ulonglong2* p)
+{
+    ulonglong2 v;
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
 /* Asks L2 to fetch [p, p + bytes) (16-byte aligned, size a multiple of 16). */
 __device__ __forceinline__ void fl_prefetch_l2(const void* p, uint32_t bytes)
 {

@@ -52,6 +52,16 @@ struct FlMvArgs {
     const float* pend_w;
     float* resid_out;
     const float* absmax;           /* FL_IN_PLAIN bound on |x| */
+    /* The rows of the row-parallel projection before this one (Wo, down), as
+     * 8-byte words (float bits, exchange tag) in this rank's receive slots,
+     * parts[q * part_stride + i] = rank q's partial row i for q < tp_parts
+     * (one slot on one GPU): the prologue waits for every word of the
+     * exchange's tag and sums them in rank order: FL_IN_RMSNORM x' = x + sum
+     * (CTA 0 stores x' in resid_out), FL_IN_GEMMA_RESID pend = sum.  No grid
+     * barrier precedes such a phase: the tags are its synchronization.
+     * tp_parts = 0: off. */
+    int32_t tp_parts, part_stride;
+    const unsigned long long* parts;
     /* epilogue */
     int32_t epi;
     float* y;
@@ -74,9 +84,12 @@ struct FlMvArgs {
     int32_t* argmax_out;
     int* err;
     /* tensor parallelism: the LOGITS epilogue writes tp_out[q] = rank q's
-     * full logits, rows offset by tp_row0 (the argmax index is global too).
-     * tp_n = 0: off. */
-    int32_t tp_n, tp_row0;
+     * full logits, rows offset by tp_row0 (the argmax index is global too);
+     * the STORE epilogue of a row-parallel projection writes its rows as
+     * (float bits, tag) words to tp_out[q] = this rank's receive slot of rank
+     * q (q < tp_n; tp_n = 1 on one GPU), tag = the step's exchange count
+     * before it + push_x.  tp_n = 0: off. */
+    int32_t tp_n, tp_row0, push_x;
     float* tp_out[FL_TP_MAX];
 };
 
@@ -126,29 +139,21 @@ struct FlAttnArgs {
 #define FL_TK_MAX_TILES 256      /* 16-row tiles of one matvec phase per CTA */
 
 /* FL_PH_ATTN writes per-split partials; FL_PH_ATTN_COMBINE merges them (same args). */
-enum { FL_PH_EMBED = 0, FL_PH_MATVEC = 1, FL_PH_ATTN = 2, FL_PH_ATTN_COMBINE = 3, FL_PH_TP_REDUCE = 4 };
-
-/* Tensor-parallel allreduce of a row-parallel projection's output: every rank
- * signals exchange `k` of the step, waits for all, then sums every rank's
- * partial slot of `parity` in rank order into y (mode 0: y += sum, 1: y = sum). */
-struct FlTpArgs {
-    int32_t k, parity, mode, n;
-    float* y;
-};
+enum { FL_PH_EMBED = 0, FL_PH_MATVEC = 1, FL_PH_ATTN = 2, FL_PH_ATTN_COMBINE = 3 };
 
 struct FlPhase {
     int32_t kind;
-    int32_t pad;
+    int32_t xk; /* > 0: this phase reads row exchange xk (1-based) of the step and has no grid barrier before it */
     FlMvArgs mv;
     FlAttnArgs at;
     FlEmbedArgs em;
-    FlTpArgs tp;
 };
 
 /* A rank's exchange region (one device allocation, mapped by every peer):
  * [FL_TP_MAX] int flags written by peers (epochs), [FL_TP_MAX][2] floats of
- * argmax candidates, [2][FL_TP_MAX][recv_n] partial-sum slots (a rank stores
- * its own into [parity][rank]; peers read them), [vocab] logits. */
+ * argmax candidates, [2][FL_TP_MAX][recv_n] 8-byte receive words (rank r
+ * pushes its rows of exchange x into [(x - 1) & 1][r] of every rank),
+ * [vocab] logits.  On one GPU a session keeps just the [2][1][recv_n] words. */
 #define FL_TP_FLAGS_OFF 0
 #define FL_TP_BEST_OFF 128
 #define FL_TP_RECV_OFF 256
@@ -182,9 +187,11 @@ struct FlTokenArgs {
     int32_t* step;
     /* tensor parallelism (tp_size 1 = off) */
     int32_t tp_size, tp_rank;
-    int32_t tp_n_exchanges;      /* per step: 2 per layer + the argmax */
+    int32_t tp_n_exchanges;      /* flag epochs per step: the argmax exchange */
     int32_t tp_recv_n;           /* floats per receive slot */
-    int32_t* tp_epoch;           /* device counter: epochs of earlier steps */
+    int32_t* tp_epoch;           /* device counters: [0] flag epochs, [1] row exchanges of earlier steps
+                                    (the exchange tags; kept on one GPU too) */
+    int32_t tp_rows_per_step;    /* row exchanges per step (2 per layer) */
     uint8_t* tp_peer[FL_TP_MAX]; /* every rank's exchange region (this rank's too) */
 };
 

@@ -395,7 +395,7 @@ __device__ __forceinline__ float2 epilogue_operand(const FlMvArgs& a, int tile, 
 template <int EPI>
 __device__ __forceinline__ void epilogue(const FlMvArgs& a, const FlMvSeg& sg, int si, int tile, int lane, float v,
                                          int pos, float& best_v, int& best_i, float2 pre = make_float2(0.0f, 0.0f),
-                                         bool has_pre = false)
+                                         bool has_pre = false, uint32_t tag = 0)
 {
     const int r = lane & 15;
     const bool act = lane < 16;
@@ -404,8 +404,26 @@ __device__ __forceinline__ void epilogue(const FlMvArgs& a, const FlMvSeg& sg, i
     if constexpr (EPI == FL_EPI_STORE || EPI == FL_EPI_RESID) {
         if (in_seg) {
             const int row = sg.tile0 * 16 + row_local;
-            if (EPI == FL_EPI_STORE) a.y[row] = sg.bias ? __fadd_rn(v, sg.bias[row_local]) : v;
-            else a.y[row] = __fadd_rn(has_pre ? pre.x : __ldcg(a.y + row), v);
+            if (EPI == FL_EPI_STORE) {
+                const float o = sg.bias ? __fadd_rn(v, sg.bias[row_local]) : v;
+                if (a.tp_n > 0) {
+                    /* a row-parallel projection's (partial) row, with the
+                     * exchange tag, into this rank's receive slot of every
+                     * rank: one 8-byte store each (NVLink for the peers), so
+                     * a reader sees the value and its tag together */
+                    const unsigned long long word = (unsigned long long)__float_as_uint(o) |
+                                                    ((unsigned long long)tag << 32);
+                    for (int q = 0; q < a.tp_n; q++)
+                        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(
+                                         reinterpret_cast<unsigned long long*>(a.tp_out[q]) + row),
+                                     "l"(word)
+                                     : "memory");
+                } else {
+                    a.y[row] = o;
+                }
+            } else {
+                a.y[row] = __fadd_rn(has_pre ? pre.x : __ldcg(a.y + row), v);
+            }
         }
     } else if constexpr (EPI == FL_EPI_QKV) {
         if (sg.bias && in_seg) v = __fadd_rn(v, sg.bias[row_local]);
@@ -484,10 +502,11 @@ __device__ __forceinline__ void wait_slot(volatile int* done, int gen, int* err)
 /* Runtime-dispatched epilogue (the persistent kernel mixes epilogues). */
 __device__ __forceinline__ void epilogue_any(const FlMvArgs& a, const FlMvSeg& sg, int si, int tile, int lane, float v,
                                              int pos, float& best_v, int& best_i,
-                                             float2 pre = make_float2(0.0f, 0.0f), bool has_pre = false)
+                                             float2 pre = make_float2(0.0f, 0.0f), bool has_pre = false,
+                                             uint32_t tag = 0)
 {
     switch (a.epi) {
-    case FL_EPI_STORE: epilogue<FL_EPI_STORE>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;
+    case FL_EPI_STORE: epilogue<FL_EPI_STORE>(a, sg, si, tile, lane, v, pos, best_v, best_i, pre, false, tag); break;
     case FL_EPI_RESID: epilogue<FL_EPI_RESID>(a, sg, si, tile, lane, v, pos, best_v, best_i, pre, has_pre); break;
     case FL_EPI_QKV: epilogue<FL_EPI_QKV>(a, sg, si, tile, lane, v, pos, best_v, best_i, pre, has_pre); break;
     case FL_EPI_GLU: epilogue<FL_EPI_GLU>(a, sg, si, tile, lane, v, pos, best_v, best_i); break;

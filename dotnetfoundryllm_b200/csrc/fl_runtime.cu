@@ -153,6 +153,7 @@ struct fl_session {
     int pf_tp_rows = 0; /* rows of a prompt chunk's partial-sum slot in the exchange region */
     int32_t pf_epoch = 0; /* the prompt path's flag epoch (host copy while it runs) */
     int xchg_recv_n = 0;
+    int tp_rows_per_step = 0; /* row exchanges of one token step (2 per layer) */
     int32_t* tp_epoch = nullptr;
     uint8_t* tp_peer[FL_TP_MAX] = {};
     void* tp_opened[FL_TP_MAX] = {};
@@ -653,27 +654,33 @@ static void build_phases(fl_session* s, PhaseList& P)
     const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, T = m->T;
     const bool gemma = d.arch == FL_ARCH_GEMMA2;
     int32_t* pos = s->state + ST_POS;
-    /* tensor parallelism: a row-parallel projection pushes its partial rows
-     * to every rank (receive slot [parity][this rank]), then an allreduce
-     * phase sums them into y */
-    auto tp_partial = [&](FlMvArgs& a, int parity) {
-        /* this rank's partial rows, in its own exchange region (peers pull them) */
+    /* Tensor parallelism, row exchanges: a row-parallel projection (Wo,
+     * down) stores its partial rows as tagged 8-byte words into this rank's
+     * receive slot [parity][rank] of every rank (tp_push), and the next
+     * phase's prologue waits for the exchange's tags and sums the T slots of
+     * its own region in rank order, with the residual or as Gemma's pending
+     * post-norm input (tp_sum_in) — with no grid barrier in between.  The
+     * residual stream alternates between xa and xb at every exchange.  (On one
+     * GPU the projection adds into the residual in its epilogue and a grid
+     * barrier separates the phases, which measured faster there.) */
+    int xk = 0;
+    auto slot_base = [&](uint8_t* region, int parity, int rank) {
+        return reinterpret_cast<unsigned long long*>(region + FL_TP_RECV_OFF) +
+               ((size_t)parity * FL_TP_MAX + rank) * s->xchg_recv_n;
+    };
+    auto tp_push = [&](FlMvArgs& a, int parity) {
         a.epi = FL_EPI_STORE;
-        a.y = reinterpret_cast<float*>(s->xchg + FL_TP_RECV_OFF) + ((size_t)parity * FL_TP_MAX + m->rank) * s->xchg_recv_n;
+        a.tp_n = T;
+        a.push_x = xk + 1;
+        for (int q = 0; q < T; q++) a.tp_out[q] = reinterpret_cast<float*>(slot_base(s->tp_peer[q], parity, m->rank));
     };
-    auto tp_reduce = [&](int k, int parity, int mode, float* y) {
-        FlPhase r;
-        memset(&r, 0, sizeof r);
-        r.kind = FL_PH_TP_REDUCE;
-        r.tp.k = k;
-        r.tp.parity = parity;
-        r.tp.mode = mode;
-        r.tp.n = h;
-        r.tp.y = y;
-        P.ph.push_back(r);
-        P.cls.push_back(CLS_OTHER);
-        P.bytes.push_back(0.0);
+    auto tp_sum_in = [&](FlMvArgs& a, int parity) {
+        a.tp_parts = T;
+        a.part_stride = s->xchg_recv_n;
+        a.parts = slot_base(s->xchg, parity, 0);
     };
+    /* marks the phase just added as the one that reads exchange xk */
+    auto after_exchange = [&]() { P.ph.back().xk = ++xk; };
 
     FlPhase e;
     memset(&e, 0, sizeof e);
@@ -706,11 +713,17 @@ static void build_phases(fl_session* s, PhaseList& P)
         set_seg(a, 2, L.wv, L.bv, L.wq.L.n_tiles + L.wk.L.n_tiles);
         a.n_seg = 3;
         a.n_tiles = L.wq.L.n_tiles + L.wk.L.n_tiles + L.wv.L.n_tiles;
+        const bool x_after_down = T > 1 && l > 0; /* x + the ranks' down rows */
         if (!gemma) {
             a.in_mode = FL_IN_RMSNORM;
             a.x = x;
             a.norm_w = L.attn_norm;
             a.eps = d.rms_eps;
+            if (x_after_down) {
+                tp_sum_in(a, 1);
+                a.resid_out = x_other;
+                std::swap(x, x_other);
+            }
         } else if (l == 0) {
             a.in_mode = FL_IN_GEMMA_NORM;
             a.x = x;
@@ -724,6 +737,7 @@ static void build_phases(fl_session* s, PhaseList& P)
             a.resid_out = x_other;
             a.norm_w = L.attn_norm;
             a.eps = 1e-6f;
+            if (x_after_down) tp_sum_in(a, 1);
             std::swap(x, x_other);
         }
         a.epi = FL_EPI_QKV;
@@ -736,6 +750,7 @@ static void build_phases(fl_session* s, PhaseList& P)
         a.k_cache = kc;
         a.v_cache = vc;
         P.add_mv(a, mat_bytes(L.wq) + mat_bytes(L.wk) + mat_bytes(L.wv) + 4.0 * h);
+        if (x_after_down) after_exchange();
 
         FlPhase at;
         memset(&at, 0, sizeof at);
@@ -774,9 +789,8 @@ static void build_phases(fl_session* s, PhaseList& P)
         a.absmax = amax_att;
         a.epi = gemma ? FL_EPI_STORE : FL_EPI_RESID;
         a.y = gemma ? s->o : x;
-        if (T > 1) tp_partial(a, 0);
+        if (T > 1) tp_push(a, 0);
         P.add_mv(a, mat_bytes(L.wo));
-        if (T > 1) tp_reduce(2 * l, 0, gemma ? 1 : 0, gemma ? s->o : x);
 
         /* FFN: norm → gate/up → SiLU|GELU(gate)*up */
         a = base_args(s, L.gate_up, h);
@@ -785,6 +799,11 @@ static void build_phases(fl_session* s, PhaseList& P)
             a.x = x;
             a.norm_w = L.ffn_norm;
             a.eps = d.rms_eps;
+            if (T > 1) {
+                tp_sum_in(a, 0);
+                a.resid_out = x_other;
+                std::swap(x, x_other);
+            }
         } else {
             a.in_mode = FL_IN_GEMMA_RESID;
             a.x = x;
@@ -793,6 +812,7 @@ static void build_phases(fl_session* s, PhaseList& P)
             a.resid_out = x_other;
             a.norm_w = L.ffn_norm;
             a.eps = 1e-6f;
+            if (T > 1) tp_sum_in(a, 0);
             std::swap(x, x_other);
         }
         a.epi = FL_EPI_GLU;
@@ -801,6 +821,7 @@ static void build_phases(fl_session* s, PhaseList& P)
         a.act_out = s->act;
         a.act_absmax = amax_act;
         P.add_mv(a, mat_bytes(L.gate_up) + 4.0 * h);
+        if (T > 1) after_exchange();
 
         a = base_args(s, L.down, m->ffn_l);
         a.in_mode = FL_IN_PLAIN;
@@ -808,9 +829,8 @@ static void build_phases(fl_session* s, PhaseList& P)
         a.absmax = amax_act;
         a.epi = gemma ? FL_EPI_STORE : FL_EPI_RESID;
         a.y = gemma ? s->o : x;
-        if (T > 1) tp_partial(a, 1);
+        if (T > 1) tp_push(a, 1);
         P.add_mv(a, mat_bytes(L.down));
-        if (T > 1) tp_reduce(2 * l + 1, 1, gemma ? 1 : 0, gemma ? s->o : x);
     }
     /* final norm + LM head + greedy argmax */
     FlMvArgs a = base_args(s, m->output, h);
@@ -819,6 +839,10 @@ static void build_phases(fl_session* s, PhaseList& P)
         a.x = x;
         a.norm_w = m->out_norm;
         a.eps = d.rms_eps;
+        if (T > 1) {
+            tp_sum_in(a, 1);
+            a.resid_out = x_other;
+        }
     } else {
         a.in_mode = FL_IN_GEMMA_RESID;
         a.x = x;
@@ -827,6 +851,7 @@ static void build_phases(fl_session* s, PhaseList& P)
         a.resid_out = x_other;
         a.norm_w = m->out_norm;
         a.eps = 1e-6f;
+        if (T > 1) tp_sum_in(a, 1);
     }
     a.epi = FL_EPI_LOGITS;
     a.y = s->logits;
@@ -841,6 +866,8 @@ static void build_phases(fl_session* s, PhaseList& P)
     a.counter = s->state + ST_HEADCNT;
     a.argmax_out = s->state + ST_ARGMAX;
     P.add_mv(a, mat_bytes(m->output) + 4.0 * h);
+    if (T > 1) after_exchange();
+    s->tp_rows_per_step = xk;
 }
 
 /* One token step: zero the grid-barrier counter, then the persistent kernel. */
@@ -899,12 +926,13 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     AL(s->q, (size_t)qd * 4);
     AL(s->att, (size_t)qd * 4);
     AL(s->act, (size_t)m->ffn_l * 4);
+    /* receive words of the row exchanges: 8 bytes per row (value, tag) */
+    s->xchg_recv_n = (h + 63) & ~63;
     if (m->T == 1) {
         AL(s->logits, (size_t)d.vocab * 4);
     } else {
         /* the exchange region peers write into; the full logits live at its end */
-        s->xchg_recv_n = (h + 63) & ~63;
-        s->xchg_logits_off = FL_TP_RECV_OFF + (size_t)2 * FL_TP_MAX * s->xchg_recv_n * 4;
+        s->xchg_logits_off = FL_TP_RECV_OFF + (size_t)2 * FL_TP_MAX * s->xchg_recv_n * 8;
         /* then the prompt path's partial sums: two slots of pf_tp_rows x hidden floats */
         s->pf_tp_rows = std::min(max_ctx, 2048);
         s->xchg_pf_off = (s->xchg_logits_off + (size_t)d.vocab * 4 + 255) & ~(size_t)255;
@@ -1013,7 +1041,18 @@ static int session_build(fl_session* s)
     const int per_max = (span + s->attn_split - 1) / s->attn_split;
     const size_t attn =
         (size_t)(grp * d.head_dim + FL_TK_WARPS * grp * d.head_dim + FL_TK_WARPS * 8 * 2 + per_max * grp) * 4;
-    const size_t scratch = std::max(xenc, attn);
+    size_t scratch = std::max(xenc, attn);
+    if (m->T > 1) {
+        /* a phase after a row exchange (Wo, down) stages x + the ranks' rows
+         * (hidden floats) at the end of the scratch, behind the encoding, and
+         * its prologue keeps the input in registers (<= 64 k-blocks) */
+        if (d.hidden % 4 || d.hidden > 64 * 256)
+            return fail(FL_ERR_UNSUPPORTED, "tensor parallelism needs hidden a multiple of 4, at most 16384 (%d)",
+                        d.hidden);
+        const size_t enc_h = (size_t)((d.hidden + 255) / 256) * 8 * FL_XENC_CHUNK_BYTES;
+        scratch = std::max(scratch, ((enc_h + 15) & ~(size_t)15) + (size_t)d.hidden * 4);
+    }
+    scratch = (scratch + 15) & ~(size_t)15;
     const int n_feed = (int)feed.size();
     int n_slots = 1;
     while (n_slots < FL_TK_MAX_SLOTS && fl_token_smem_bytes(n_slots + 1, slot, scratch, n_feed) <= (size_t)max_dyn)
@@ -1040,10 +1079,12 @@ static int session_build(fl_session* s)
     ta.pos = s->state + ST_POS;
     ta.out_tokens = s->out_tokens;
     ta.step = s->state + ST_STEP;
+    ta.tp_epoch = s->tp_epoch;
+    ta.tp_rows_per_step = s->tp_rows_per_step;
     if (m->T > 1) {
         ta.tp_size = m->T;
         ta.tp_rank = m->rank;
-        ta.tp_n_exchanges = 2 * d.n_layers + 1;
+        ta.tp_n_exchanges = 1;
         ta.tp_recv_n = s->xchg_recv_n;
         ta.tp_epoch = s->tp_epoch;
         for (int q = 0; q < m->T; q++) ta.tp_peer[q] = s->tp_peer[q];
@@ -1213,10 +1254,13 @@ extern "C" int fl_session_tp_reset(fl_session* s)
         }
         return FL_OK;
     }
-    if (!s->xchg || !s->tp_epoch) return fail(FL_ERR_STATE, "not a tensor-parallel session");
-    /* this rank's epoch counter and the flags its peers raise in its region */
+    if (s->m->T == 1 || !s->xchg || !s->tp_epoch) return fail(FL_ERR_STATE, "not a tensor-parallel session");
+    /* this rank's counters, the flags its peers raise in its region and the
+     * receive words (their tags restart with the counters, so no word of an
+     * earlier exchange may survive) */
     CK(cudaMemsetAsync(s->tp_epoch, 0, 16, s->st));
-    CK(cudaMemsetAsync(s->xchg + FL_TP_FLAGS_OFF, 0, FL_TP_RECV_OFF - FL_TP_FLAGS_OFF, s->st));
+    CK(cudaMemsetAsync(s->xchg + FL_TP_FLAGS_OFF, 0,
+                       FL_TP_RECV_OFF - FL_TP_FLAGS_OFF + (size_t)2 * FL_TP_MAX * s->xchg_recv_n * 8, s->st));
     CK(cudaStreamSynchronize(s->st));
     s->pf_epoch = 0;
     s->cur_len = 0;

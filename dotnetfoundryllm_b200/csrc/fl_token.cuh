@@ -189,6 +189,106 @@ __device__ __forceinline__ void load8(const float* p, int base, int n, float (&o
     }
 }
 
+/* 8 consecutive floats of a shared-memory vector (zero beyond n). */
+__device__ __forceinline__ void load8_smem(const float* p, int base, int n, float (&o)[8])
+{
+    if (base + 8 <= n) {
+        const float4 u = *reinterpret_cast<const float4*>(p + base);
+        const float4 v = *reinterpret_cast<const float4*>(p + base + 4);
+        o[0] = u.x; o[1] = u.y; o[2] = u.z; o[3] = u.w;
+        o[4] = v.x; o[5] = v.y; o[6] = v.z; o[7] = v.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) o[i] = base + i < n ? p[base + i] : 0.0f;
+    }
+}
+
+/* The input of a phase after a row-parallel projection (Wo, down): the
+ * projection's rows arrive as (float bits, tag) words in this rank's receive
+ * slots, one slot per rank (one on one GPU).  Every thread waits for its
+ * element pairs of every rank to carry `tag` — 16-byte loads of two 8-byte
+ * words, each word written by one 8-byte store, re-read until current — and
+ * sums them in rank order into the shared stage; then x + sum for a plain
+ * norm (CTA 0 also stores it in resid_out, the residual stream of later
+ * phases), the sum itself for Gemma's pending post-norm input.  Bounded: ~2 s,
+ * then FL_DEV_ERR_TIMEOUT; no wait once an error is recorded.  K is even. */
+__device__ void stage_parts(const FlMvArgs& a, float* stage, uint32_t tag, int* err)
+{
+    constexpr int JB = 4; /* element pairs per thread and batch */
+    constexpr int QB = 2; /* ranks per poll */
+    const int npairs = a.K >> 1;
+    const size_t qstride = (size_t)a.part_stride >> 1; /* in pairs */
+    const ulonglong2* base = reinterpret_cast<const ulonglong2*>(a.parts);
+    const bool add_x = a.in_mode != FL_IN_GEMMA_RESID;
+    uint64_t t0 = 0;
+    bool timed = false;
+    for (int p0 = threadIdx.x; p0 < npairs; p0 += NC * JB) {
+        /* the residual pairs first: their load overlaps the wait for the words */
+        float2 xr[JB];
+#pragma unroll
+        for (int j = 0; j < JB; j++) {
+            const int pr = p0 + j * NC;
+            xr[j] = add_x && pr < npairs ? __ldcg(reinterpret_cast<const float2*>(a.x) + pr) : make_float2(0.0f, 0.0f);
+        }
+        float2 acc[JB];
+        for (int q0 = 0; q0 < a.tp_parts; q0 += QB) {
+            ulonglong2 w[QB][JB];
+#pragma unroll
+            for (int qq = 0; qq < QB; qq++)
+#pragma unroll
+                for (int j = 0; j < JB; j++) {
+                    const int pr = p0 + j * NC;
+                    if (q0 + qq < a.tp_parts && pr < npairs) w[qq][j] = fl_ld_volatile_u64x2(base + (q0 + qq) * qstride + pr);
+                    else w[qq][j] = make_ulonglong2((unsigned long long)tag << 32, (unsigned long long)tag << 32);
+                }
+            for (uint32_t it = 0;; it++) {
+                bool ok = true;
+#pragma unroll
+                for (int qq = 0; qq < QB; qq++)
+#pragma unroll
+                    for (int j = 0; j < JB; j++)
+                        if ((uint32_t)(w[qq][j].x >> 32) != tag || (uint32_t)(w[qq][j].y >> 32) != tag) {
+                            ok = false;
+                            w[qq][j] = fl_ld_volatile_u64x2(base + (q0 + qq) * qstride + p0 + j * NC);
+                        }
+                if (ok || fl_err_set(err)) break;
+                __nanosleep(64); /* every CTA polls the whole vector: keep the re-reads sparse */
+                if ((it & 63u) == 0) {
+                    const uint64_t now = fl_globaltimer();
+                    if (!timed) {
+                        t0 = now;
+                        timed = true;
+                    } else if (now - t0 > 2000000000ull) {
+                        atomicExch(err, FL_DEV_ERR_TIMEOUT);
+                        break;
+                    }
+                }
+            }
+            /* rank order: acc = w[rank 0], then + w[rank 1], ... */
+#pragma unroll
+            for (int qq = 0; qq < QB; qq++)
+#pragma unroll
+                for (int j = 0; j < JB; j++) {
+                    if (q0 + qq >= a.tp_parts) continue;
+                    const float v0 = __uint_as_float((uint32_t)w[qq][j].x), v1 = __uint_as_float((uint32_t)w[qq][j].y);
+                    if (q0 + qq == 0) acc[j] = make_float2(v0, v1);
+                    else acc[j] = make_float2(__fadd_rn(acc[j].x, v0), __fadd_rn(acc[j].y, v1));
+                }
+        }
+#pragma unroll
+        for (int j = 0; j < JB; j++) {
+            const int pr = p0 + j * NC;
+            if (pr >= npairs) continue;
+            float2 v = acc[j];
+            if (add_x) {
+                v = make_float2(__fadd_rn(xr[j].x, v.x), __fadd_rn(xr[j].y, v.y));
+                if (blockIdx.x == 0) reinterpret_cast<float2*>(a.resid_out)[pr] = v;
+            }
+            reinterpret_cast<float2*>(stage)[pr] = v;
+        }
+    }
+}
+
 /* ── phases ─────────────────────────────────────────────────────────────── */
 
 __device__ void phase_embed(const FlEmbedArgs& e, int* err)
@@ -482,48 +582,6 @@ __device__ void prefetch_attn_kv(const FlAttnArgs& a, int pos)
 
 /* ── tensor parallelism ─────────────────────────────────────────────────── */
 
-/* Exchange `epoch`: CTA 0 (when `signal`) tells every rank that this rank's
- * pushes are done; every CTA then waits, bounded, until all ranks have said
- * so.  Flags are written by the peers into this rank's own exchange region,
- * so the wait polls local memory. */
-__device__ void tp_signal_wait(const FlTokenArgs& ta, int epoch, bool signal)
-{
-    if (threadIdx.x == 0) {
-        if (signal)
-            for (int q = 0; q < ta.tp_size; q++)
-                fl_st_release_sys(reinterpret_cast<int*>(ta.tp_peer[q] + FL_TP_FLAGS_OFF) + ta.tp_rank, epoch);
-        const int* fl = reinterpret_cast<const int*>(ta.tp_peer[ta.tp_rank] + FL_TP_FLAGS_OFF);
-        const uint64_t t0 = fl_globaltimer();
-        for (int q = 0; q < ta.tp_size && !fl_err_set(ta.err); q++) {
-            for (uint32_t it = 0; fl_ld_acquire_sys(fl + q) < epoch; it++) {
-                if ((it & 255u) == 0 && (fl_err_set(ta.err) || fl_globaltimer() - t0 > 2000000000ull)) {
-                    if (!fl_err_set(ta.err)) atomicExch(ta.err, FL_DEV_ERR_TIMEOUT);
-                    q = ta.tp_size;
-                    break;
-                }
-            }
-        }
-    }
-    consumer_sync();
-}
-
-/* The allreduce after a row-parallel projection: every rank has stored its
- * partial rows in its own exchange region; after the flag exchange each CTA
- * reads its rows from every rank (over NVLink for the peers) and sums them in
- * rank order (the same order on every rank, so all ranks get identical
- * values). */
-__device__ void phase_tp_reduce(const FlTokenArgs& ta, const FlTpArgs& r, int epoch0)
-{
-    tp_signal_wait(ta, epoch0 + r.k + 1, blockIdx.x == 0);
-    const size_t off = FL_TP_RECV_OFF + ((size_t)r.parity * FL_TP_MAX) * ta.tp_recv_n * 4;
-    for (int i = blockIdx.x * NC + threadIdx.x; i < r.n; i += gridDim.x * NC) {
-        float sum = 0.0f;
-        for (int q = 0; q < ta.tp_size; q++)
-            sum += fl_ld_relaxed_sys(reinterpret_cast<const float*>(ta.tp_peer[q] + off) + (size_t)q * ta.tp_recv_n + i);
-        r.y[i] = r.mode ? sum : __fadd_rn(__ldcg(r.y + i), sum);
-    }
-}
-
 /* L2 prefetch of a matvec phase's norm weights (and Gemma's pending
  * post-norm weights), whole 16-byte granules. */
 __device__ void prefetch_prologue(const FlPhase& ph)
@@ -696,6 +754,9 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
     float best_v = 0.0f;
     int best_i = 0x7fffffff;
     const int tp_epoch0 = ta.tp_size > 1 ? __ldcg(ta.tp_epoch) : 0;
+    /* row exchanges of earlier steps: exchange x of this step carries tag tp_rows0 + x */
+    const uint32_t tp_rows0 = ta.tp_epoch ? (uint32_t)__ldcg(ta.tp_epoch + 1) : 0u;
+    int n_sync = 0; /* grid barriers passed */
     /* the step's position: every phase of the launch uses the same one (the
      * device-resident loop advances it only after the last phase) */
     const int pos0 = __ldcg(ta.pos);
@@ -714,16 +775,22 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
             if (p + 1 < ta.n_phases && ta.phases[p + 1].kind == FL_PH_ATTN) prefetch_attn_kv(ta.phases[p + 1].at, pos0);
         } else if (kind == FL_PH_ATTN || kind == FL_PH_ATTN_COMBINE) {
             copy_words(abuf, &ta.phases[p].at, sizeof(FlAttnArgs));
-        } else if (kind == FL_PH_TP_REDUCE) {
-            copy_words(abuf, &ta.phases[p].tp, sizeof(FlTpArgs));
         }
         /* The next matvec phase's static prologue operands (norm weights) do
          * not depend on the step's data: one CTA asks L2 for them a phase
          * early, so that the prologue after the barrier finds them there
          * instead of waiting on HBM behind the weight stream. */
         if (p + 1 < ta.n_phases && tid == 0 && (int)blockIdx.x == (p * 7) % G) prefetch_prologue(ta.phases[p + 1]);
-        if (p > 0) grid_sync(ta.bar, p * G, ta.err, ta.cta_done ? ta.cta_done + (size_t)(p - 1) * G + blockIdx.x : nullptr);
-        else consumer_sync();
+        uint64_t* done_stamp = ta.cta_done && p > 0 ? ta.cta_done + (size_t)(p - 1) * G + blockIdx.x : nullptr;
+        /* a phase that reads a row exchange waits on the exchange's tags in
+         * its prologue instead of at a grid barrier */
+        const int xk = ta.phases[p].xk;
+        if (p > 0 && xk == 0) {
+            grid_sync(ta.bar, ++n_sync * G, ta.err, done_stamp);
+        } else {
+            if (done_stamp && tid == 0) *done_stamp = fl_globaltimer();
+            consumer_sync();
+        }
         if (ta.timestamps && blockIdx.x == 0 && tid == 0) ta.timestamps[p] = fl_globaltimer();
         if (kind == FL_PH_EMBED) {
             phase_embed(ta.phases[p].em, ta.err);
@@ -732,10 +799,6 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         if (kind == FL_PH_ATTN) {
             phase_attn_t<HD, GMAX>(*reinterpret_cast<const FlAttnArgs*>(abuf), pos0, reinterpret_cast<float*>(scratch),
                                    ta.detail && blockIdx.x == 0 ? ta.detail + (size_t)p * NW * 4 : nullptr);
-            continue;
-        }
-        if (kind == FL_PH_TP_REDUCE) {
-            phase_tp_reduce(ta, *reinterpret_cast<const FlTpArgs*>(abuf), tp_epoch0);
             continue;
         }
         if (kind == FL_PH_ATTN_COMBINE) {
@@ -756,10 +819,18 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
             const int mode = a.in_mode;
             float xv[RK][8];
             const float am_plain = mode == FL_IN_PLAIN ? __ldcg(a.absmax) : 0.0f;
+            /* tensor parallelism: x + the ranks' partial rows (or Gemma's
+             * pending vector) summed once into shared memory, read from there */
+            const bool staged = a.tp_parts > 0;
+            float* stage = reinterpret_cast<float*>(scratch + ta.scratch_bytes - (size_t)a.K * 4);
+            if (staged) {
+                stage_parts(a, stage, tp_rows0 + (uint32_t)xk, ta.err);
+                consumer_sync();
+            }
             if (mode == FL_IN_GEMMA_RESID) {
                 float sp = 0.0f, dummy = 0.0f;
                 for (int i = tid; i < a.K; i += NC) {
-                    const float v = __ldcg(a.pend + i);
+                    const float v = staged ? stage[i] : __ldcg(a.pend + i);
                     sp = fmaf(v, v, sp);
                 }
                 consumer_sum_max(sp, dummy, misc);
@@ -768,7 +839,8 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
 #pragma unroll
             for (int r = 0; r < RK; r++) {
                 const int base = (warp + r * NW) * 256 + lane * 8;
-                load8_cg(a.x, base, a.K, xv[r]);
+                if (staged && mode != FL_IN_GEMMA_RESID) load8_smem(stage, base, a.K, xv[r]);
+                else load8_cg(a.x, base, a.K, xv[r]);
             }
             if (mode == FL_IN_PLAIN) {
                 amax = am_plain;
@@ -783,7 +855,8 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                     if (mode == FL_IN_GEMMA_RESID) {
                         /* x' = x + GemmaRmsNorm(pend, pend_w), kept by CTA 0 */
                         float pe[8], pw[8];
-                        load8_cg(a.pend, base, a.K, pe);
+                        if (staged) load8_smem(stage, base, a.K, pe);
+                        else load8_cg(a.pend, base, a.K, pe);
                         load8(a.pend_w, base, a.K, pw);
 #pragma unroll
                         for (int i = 0; i < 8; i++)
@@ -939,7 +1012,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                 if (lane == 0) tcnt[it] = 0;
             }
             epilogue_any(a, sg, si, tile, lane, v, pos, best_v, best_i, it == first_it ? pre0 : pre1,
-                         has_pre && (it == first_it || it == last_it));
+                         has_pre && (it == first_it || it == last_it), tp_rows0 + (uint32_t)a.push_x);
             pushed |= lane < 16;
         }
         if (ta.detail && blockIdx.x == 0 && lane == 0) {
@@ -951,7 +1024,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
         }
         /* rows pushed to other GPUs are visible system-wide before this CTA
          * reports the phase done (only the lanes that stored them fence) */
-        if (a.tp_n > 0 && pushed) __threadfence_system();
+        if (a.epi == FL_EPI_LOGITS && a.tp_n > 0 && pushed) __threadfence_system();
 
         if (a.epi == FL_EPI_LOGITS) {
             /* greedy ArgMax (TensorPrimitives.IndexOfMax): per CTA, then across CTAs */
@@ -1039,6 +1112,7 @@ __global__ void __launch_bounds__(NT, 1) fl_token_kernel(const __grid_constant__
                 if (lane == 0) {
                     *a.argmax_out = bi;
                     *a.counter = 0;
+                    if (ta.tp_epoch) ta.tp_epoch[1] = (int32_t)(tp_rows0 + (uint32_t)ta.tp_rows_per_step);
                     /* the device-resident decode loop: next token, next position */
                     if (ta.advance) {
                         const int s = __ldcg(ta.step);
