@@ -908,8 +908,11 @@ extern "C" int fl_session_create(fl_model* m, int32_t max_ctx, int32_t max_batch
     /* this rank's share of the model (the whole model without tensor parallelism) */
     const int h = d.hidden, qd = m->qd_l, kvd = m->kvd_l, grp = d.n_heads / d.n_kv_heads;
     const int G = m->sm_count;
-    /* attention items (kv head, split): at most one per SM */
+    /* attention items (kv head, split): at most one per SM, and at most 32
+     * splits per kv head, so that the split merge reads each split's (max,
+     * sum) in one warp load (a tensor-parallel rank keeps few kv heads) */
     int split = G / m->nkv_l;
+    if (split > 32) split = 32;
     if (split > max_ctx) split = max_ctx;
     if (split < 1) split = 1;
     s->attn_split = split;
