@@ -77,11 +77,13 @@ def test_ranks_match_the_oracle(name, ranks, tmp_path):
 
 def test_a_rank_that_misses_a_step_times_out_fast_and_the_group_recovers(tmp_path):
     """Failure detection without a GPU fault: rank 1 skips one step, so rank
-    0's token kernel finds no peer flags.  Its first bounded wait gives up
-    after ~2 s and every later exchange of the step returns at once, so the
-    call fails with FL_ERR_TIMEOUT in a few seconds (not one limit per
-    exchange: 2 per layer + 1).  After fl_session_tp_reset on both ranks the
-    teacher-forced logits match the oracle again, identical on both ranks."""
+    0's token kernel never sees rank 1's row words of the step's first
+    exchange.  That bounded wait gives up after ~2 s and every later exchange
+    of the step returns at once, so the call fails with FL_ERR_TIMEOUT in a
+    few seconds (not one limit per exchange: 2 per layer + the argmax).  After
+    fl_session_tp_reset on both ranks (which also clears the receive words,
+    whose tags restart) the teacher-forced logits match the oracle again,
+    identical on both ranks."""
     ranks = 2
     if _gpus() < ranks:
         pytest.skip(f"needs {ranks} GPUs")
