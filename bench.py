@@ -235,6 +235,15 @@ def decode_workload(pos_timed: int, steps: int, prompt: int) -> str:
             f"after a {prompt}-token prompt")
 
 
+def decode_config(args, ws: int, pos_timed: int, streams: int = 1) -> dict:
+    """The decode line's config, the same dict on both arms for the same launch."""
+    tp = ws > 1 and args.parallel == "tp"
+    return {"workload": decode_workload(pos_timed, args.steps, args.prompt),
+            "model": CONFIG, "global_batch": streams, "seq_len": args.prompt,
+            "parallelism": f"tp{ws}" if tp else (f"replicas x{ws}" if ws > 1 else "single GPU"),
+            "l2": "inputs larger than L2 (4.9 GB of weights per step)"}
+
+
 def run_reference(args, ws, rank):
     if rank != 0:
         return
@@ -278,8 +287,7 @@ def run_reference(args, ws, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF)",
-        "config": {"workload": decode_workload(pos_timed, args.steps, args.prompt),
-                   "model": CONFIG, "global_batch": 1, "seq_len": args.prompt},
+        "config": decode_config(args, ws, pos_timed, 1 if (ws == 1 or args.parallel == "tp") else ws),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample,
                          "single_thread_value": one_thread},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -503,10 +511,7 @@ def run_ours(args, ws, rank, local):
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
             "scaling": "strong" if tp else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init GGUF, N(0,0.02) weights)",
-            "config": {"workload": decode_workload(pos_timed, args.steps, args.prompt),
-                       "model": CONFIG, "global_batch": streams, "seq_len": args.prompt,
-                       "parallelism": f"tp{ws}" if tp else (f"replicas x{ws}" if ws > 1 else "single GPU"),
-                       "l2": "inputs larger than L2 (4.9 GB of weights per step)"},
+            "config": decode_config(args, ws, pos_timed, streams),
             "roofline": {"bound": "hbm", "achieved": step_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": step_gbs / peaks["hbm_gbs"], "traffic": traffic,
                          "kernel": "fl_token_kernel (one persistent launch per token)",
