@@ -51,9 +51,22 @@ sys.path.insert(0, str(ROOT))
 
 CONFIG = "llama3-8b"
 PROMPT = 2048
+# --model: the decode line's model (BASELINE configs[1] by default); name, quantization, weights per step
+MODELS = {
+    "llama3-8b": ("Llama-3-8B-arch Q4_K_M-style GGUF", "Q4_K/Q6_K", "4.9 GB"),
+    "gemma2-9b": ("Gemma-2-9B-arch Q5_K/Q6_K GGUF", "Q5_K/Q6_K", "6.5 GB"),
+    "mistral-7b": ("Mistral-7B-arch Q8_0 GGUF", "Q8_0", "7.6 GB"),
+}
 METRIC = "decode tok/s, Llama-3-8B-arch Q4_K_M-style GGUF, bs=1 greedy after a 2048-token prompt"
 NOMINAL_HBM_GBS = 8000.0
 PREFILL_WARMUP, PREFILL_TIMED = 2, 3
+
+
+def set_model(name: str, prompt: int) -> None:
+    """The decode line's model and metric string (the default keeps the headline's)."""
+    global CONFIG, METRIC
+    CONFIG = name
+    METRIC = f"decode tok/s, {MODELS[name][0]}, bs=1 greedy after a {prompt}-token prompt"
 
 
 def load_peaks() -> dict:
@@ -231,7 +244,7 @@ def cpu_sample(img: np.ndarray, position: int, repeats: int = 3, threads: int | 
 
 def decode_workload(pos_timed: int, steps: int, prompt: int) -> str:
     """config.workload of the decode line, the same string on both arms."""
-    return (f"{CONFIG} Q4_K/Q6_K bs=1 greedy decode, positions {pos_timed}..{pos_timed + steps - 1} "
+    return (f"{CONFIG} {MODELS[CONFIG][1]} bs=1 greedy decode, positions {pos_timed}..{pos_timed + steps - 1} "
             f"after a {prompt}-token prompt")
 
 
@@ -241,7 +254,7 @@ def decode_config(args, ws: int, pos_timed: int, streams: int = 1) -> dict:
     return {"workload": decode_workload(pos_timed, args.steps, args.prompt),
             "model": CONFIG, "global_batch": streams, "seq_len": args.prompt,
             "parallelism": f"tp{ws}" if tp else (f"replicas x{ws}" if ws > 1 else "single GPU"),
-            "l2": "inputs larger than L2 (4.9 GB of weights per step)"}
+            "l2": f"inputs larger than L2 ({MODELS[CONFIG][2]} of weights per step)"}
 
 
 def run_reference(args, ws, rank):
@@ -555,7 +568,11 @@ def main():
                     help="profiling only: the prompt path alone (one GPU), W + K device-timed passes")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
                     help="N > 1: tensor parallelism (default) or independent replicas")
+    ap.add_argument("--model", default=CONFIG, choices=sorted(MODELS),
+                    help="decode workload's model: llama3-8b (default, BASELINE configs[1]), gemma2-9b "
+                         "(configs[3]: use --prompt 4096), mistral-7b")
     args = ap.parse_args()
+    set_model(args.model, args.prompt)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
