@@ -396,7 +396,7 @@ def run_batch(args):
     ms = dt / args.steps * 1e3
     peaks = load_peaks()
     gbs = step_bytes / (ms / 1e3) / 1e9
-    split_bytes = 6.0 * (wbytes / (34.0 / 32.0))  # Q8_0: 34 B per 32 weights; the cache holds 6 B per weight
+    split_bytes = 4.0 * (wbytes / (34.0 / 32.0))  # Q8_0: 34 B per 32 weights; the [lo | hi] cache holds 4 B per weight
     print(json.dumps({
         "metric": "batched decode tok/s, Mistral-7B-arch Q8_0, 32 sequences, greedy after 512-token prompts",
         "value": B * args.steps / dt, "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
